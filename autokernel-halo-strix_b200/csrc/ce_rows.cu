@@ -1,0 +1,326 @@
+// Cross-entropy over materialised logit rows, sm_100a.
+//
+// Semantics follow cross_entropy_fwd_kernel / cross_entropy_bwd_tiny_kernel
+// (kernels/ce_fused.py:122-329, 405-488):
+//   x'   = softcap > 0 ? softcap * tanh(x / softcap) : x
+//   lse  = log(sum exp x'),  loss = lse - (1-a) x'_y - a * mean(x')   (a = label smoothing)
+//   grad = (softmax(x') - (1-a)[i==y] - a/V) * (1 - tanh^2) * scale
+//   rows with y == ignore_index: loss 0, grad row 0.
+// One CTA per row (grid-strided), 16-byte loads, online (max, sum) merged once
+// per vector of 8/16 elements so the SFU does ~1 exp per element.
+#include "ak_common.cuh"
+
+namespace ak {
+namespace {
+
+constexpr int kThreads = 256;
+
+struct CeParams {
+  float softcap, inv_softcap, ls, ls_uniform, target_coeff;
+  int64_t ignore_index;
+};
+
+__device__ __forceinline__ float cap(float x, const CeParams& p) {
+  return p.softcap > 0.f ? p.softcap * tanhf(x * p.inv_softcap) : x;
+}
+
+// Merge (m_b, s_b) into (m, s): s is a sum of exp2((x - m) * log2e).
+__device__ __forceinline__ void merge(float& m, float& s, float mb, float sb) {
+  const float mn = fmaxf(m, mb);
+  if (mn == -INFINITY) return;
+  s = s * ex2((m - mn) * kLog2e) + sb * ex2((mb - mn) * kLog2e);
+  m = mn;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, float* __restrict__ max_out,
+                   float* __restrict__ sum_out, T* __restrict__ grad, const T* __restrict__ logits,
+                   const int64_t* __restrict__ targets, int64_t B, int V, CeParams p, float scale_grad,
+                   const float* __restrict__ scale_dev, bool vec_ok) {
+  constexpr int VEC = 16 / sizeof(T);
+  __shared__ float s_m[kThreads / 32], s_s[kThreads / 32], s_x[kThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool use_ls = p.ls > 0.f;
+  const float scale = scale_grad * (scale_dev ? *scale_dev : 1.f);
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const T* row = logits + b * V;
+    const int64_t tgt = targets[b];
+    const bool ignored = (tgt == p.ignore_index);
+    float m = -INFINITY, s = 0.f, sx = 0.f;
+    const int nvec = vec_ok ? V / VEC : 0;
+    for (int v = tid; v < nvec; v += kThreads) {
+      float e[VEC];
+      load_frag<T, VEC>(e, row + (int64_t)v * VEC);
+      float lm = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        e[k] = cap(e[k], p);
+        lm = fmaxf(lm, e[k]);
+        sx += e[k];
+      }
+      const float mn = fmaxf(m, lm);
+      if (mn != -INFINITY) {
+        float acc = s * ex2((m - mn) * kLog2e);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) acc += ex2((e[k] - mn) * kLog2e);
+        s = acc;
+        m = mn;
+      }
+    }
+    for (int i = nvec * VEC + tid; i < V; i += kThreads) {
+      const float e = cap(to_f<T>(row[i]), p);
+      sx += e;
+      merge(m, s, e, 1.f);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+      const float so = __shfl_xor_sync(0xffffffffu, s, o);
+      merge(m, s, mo, so);
+    }
+    sx = warp_sum(sx);
+    if (lane == 0) { s_m[warp] = m; s_s[warp] = s; s_x[warp] = sx; }
+    __syncthreads();
+    float M = -INFINITY, S = 0.f, SX = 0.f;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) { merge(M, S, s_m[w], s_s[w]); SX += s_x[w]; }
+    __syncthreads();
+    const float lse = M + lg2(S) * kLn2;
+    if (tid == 0) {
+      lse_out[b] = lse;
+      if (max_out) max_out[b] = M;
+      if (sum_out) sum_out[b] = S;
+      float loss = 0.f;
+      if (!ignored) {
+        if (tgt < 0 || tgt >= V) {
+          loss = NAN;
+        } else {
+          const float xt = cap(to_f<T>(row[tgt]), p);
+          loss = use_ls ? lse - p.target_coeff * xt - p.ls * (SX / (float)V) : lse - xt;
+        }
+      }
+      losses[b] = loss;
+    }
+    if (grad != nullptr) {
+      T* grow = grad + b * V;
+      const float inv_s = 1.f / S;
+      for (int v = tid; v < nvec; v += kThreads) {
+        float o[VEC];
+        if (ignored) {
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) o[k] = 0.f;
+        } else {
+          float e[VEC];
+          load_frag<T, VEC>(e, row + (int64_t)v * VEC);
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) {
+            const float xc = cap(e[k], p);
+            float g = ex2((xc - M) * kLog2e) * inv_s;
+            if ((int64_t)v * VEC + k == tgt) g -= p.target_coeff;
+            g -= p.ls_uniform;
+            if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
+            o[k] = g * scale;
+          }
+        }
+        store_frag<T, VEC>(grow + (int64_t)v * VEC, o);
+      }
+      for (int i = nvec * VEC + tid; i < V; i += kThreads) {
+        float g = 0.f;
+        if (!ignored) {
+          const float xc = cap(to_f<T>(row[i]), p);
+          g = ex2((xc - M) * kLog2e) * inv_s;
+          if (i == tgt) g -= p.target_coeff;
+          g -= p.ls_uniform;
+          if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
+          g *= scale;
+        }
+        grow[i] = from_f<T>(g);
+      }
+    }
+  }
+}
+
+// Tiny-mode backward: recompute softmax from saved (row_max, row_sum), plus the
+// optional z-loss gradient z_coef * lse * softmax (kernels/ce_fused.py:672-689).
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+ce_rows_bwd_kernel(T* __restrict__ grad, const T* __restrict__ logits, const int64_t* __restrict__ targets,
+                   const float* __restrict__ row_max, const float* __restrict__ row_sum, int64_t B, int V,
+                   CeParams p, float scale_h, const float* __restrict__ scale_dev, float z_coef, bool vec_ok) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int tid = threadIdx.x;
+  const float sd = scale_dev ? *scale_dev : 1.f;
+  const float scale = scale_h * sd;
+  const float zc = z_coef * sd;
+  for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
+    const T* row = logits + b * V;
+    T* grow = grad + b * V;
+    const int64_t tgt = targets[b];
+    const bool ignored = (tgt == p.ignore_index);
+    const float M = row_max[b];
+    const float inv_s = 1.f / row_sum[b];
+    const float lse = M + lg2(row_sum[b]) * kLn2;
+    const int nvec = vec_ok ? V / VEC : 0;
+    for (int v = tid; v < nvec; v += kThreads) {
+      float o[VEC];
+      if (ignored) {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) o[k] = 0.f;
+      } else {
+        float e[VEC];
+        load_frag<T, VEC>(e, row + (int64_t)v * VEC);
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+          const float xc = cap(e[k], p);
+          const float pr = ex2((xc - M) * kLog2e) * inv_s;
+          float g = pr;
+          if ((int64_t)v * VEC + k == tgt) g -= p.target_coeff;
+          g -= p.ls_uniform;
+          if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
+          o[k] = g * scale + zc * lse * pr;
+        }
+      }
+      store_frag<T, VEC>(grow + (int64_t)v * VEC, o);
+    }
+    for (int i = nvec * VEC + tid; i < V; i += kThreads) {
+      float g = 0.f;
+      if (!ignored) {
+        const float xc = cap(to_f<T>(row[i]), p);
+        const float pr = ex2((xc - M) * kLog2e) * inv_s;
+        g = pr;
+        if (i == tgt) g -= p.target_coeff;
+        g -= p.ls_uniform;
+        if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
+        g = g * scale + zc * lse * pr;
+      }
+      grow[i] = from_f<T>(g);
+    }
+  }
+}
+
+// Single-CTA reductions over the row results (no host sync).
+__global__ void __launch_bounds__(1024)
+ce_reduce_kernel(float* __restrict__ loss_out, float* __restrict__ nvalid_out, const float* __restrict__ losses,
+                 const float* __restrict__ lse, const int64_t* __restrict__ targets, int64_t B,
+                 int64_t ignore_index, float zw) {
+  __shared__ float r0[32], r1[32], r2[32];
+  float sl = 0.f, sn = 0.f, sz = 0.f;
+  for (int64_t i = threadIdx.x; i < B; i += blockDim.x) {
+    const bool valid = targets[i] != ignore_index;
+    if (valid) {
+      sl += losses[i];
+      sn += 1.f;
+      if (zw > 0.f && lse) sz += lse[i] * lse[i];
+    }
+  }
+  sl = warp_sum(sl); sn = warp_sum(sn); sz = warp_sum(sz);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) { r0[w] = sl; r1[w] = sn; r2[w] = sz; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f, n = 0.f, z = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { a += r0[i]; n += r1[i]; z += r2[i]; }
+    n = fmaxf(n, 1.f);
+    float loss = a / n;
+    if (zw > 0.f) loss += zw * z / n;
+    if (loss_out) loss_out[0] = loss;
+    if (nvalid_out) nvalid_out[0] = n;
+  }
+}
+
+__global__ void __launch_bounds__(1024)
+ce_inv_valid_kernel(float* __restrict__ inv_out, const int64_t* __restrict__ targets, int64_t B,
+                    int64_t ignore_index) {
+  __shared__ float r[32];
+  float n = 0.f;
+  for (int64_t i = threadIdx.x; i < B; i += blockDim.x) n += (targets[i] != ignore_index) ? 1.f : 0.f;
+  n = warp_sum(n);
+  if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = n;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += r[i];
+    inv_out[0] = 1.f / fmaxf(t, 1.f);
+  }
+}
+
+CeParams make_params(float softcap, int64_t ignore_index, float ls, int64_t V) {
+  CeParams p;
+  p.softcap = softcap > 0.f ? softcap : 0.f;
+  p.inv_softcap = softcap > 0.f ? 1.f / softcap : 0.f;
+  p.ls = ls > 0.f ? ls : 0.f;
+  p.ls_uniform = p.ls / (float)V;
+  p.target_coeff = 1.f - p.ls;
+  p.ignore_index = ignore_index;
+  return p;
+}
+
+unsigned row_grid(int64_t B) {
+  const int64_t cap = (int64_t)sm_count() * 8;
+  return (unsigned)(B < cap ? B : cap);
+}
+
+}  // namespace
+}  // namespace ak
+
+using namespace ak;
+
+extern "C" int ak_ce_rows_fwd(float* losses, float* lse, float* row_max, float* row_sum, void* grad,
+                              const void* logits, const int64_t* targets, int64_t B, int64_t V, float softcap,
+                              int64_t ignore_index, float label_smoothing, float scale_grad,
+                              const float* scale_dev, int dt, void* stream) {
+  clear_error();
+  AK_REQUIRE(B >= 0 && V > 0 && V < (1LL << 31), AK_ERR_SHAPE, "ak_ce_rows_fwd: bad shape");
+  if (B == 0) return AK_OK;
+  AK_REQUIRE(losses && lse && logits && targets, AK_ERR_ARG, "ak_ce_rows_fwd: null pointer");
+  const CeParams p = make_params(softcap, ignore_index, label_smoothing, V);
+  const int es = elem_size(dt);
+  const bool vec_ok = aligned16(logits) && (grad == nullptr || aligned16(grad)) && ((V * es) % 16 == 0);
+  AK_DISPATCH_DTYPE(dt, T,
+                    ce_rows_fwd_kernel<T><<<row_grid(B), kThreads, 0, (cudaStream_t)stream>>>(
+                        losses, lse, row_max, row_sum, (T*)grad, (const T*)logits, targets, B, (int)V, p,
+                        scale_grad, scale_dev, vec_ok));
+  AK_CHECK_LAUNCH("ak_ce_rows_fwd");
+  return AK_OK;
+}
+
+extern "C" int ak_ce_rows_bwd(void* grad, const void* logits, const int64_t* targets, const float* row_max,
+                              const float* row_sum, int64_t B, int64_t V, float softcap, int64_t ignore_index,
+                              float label_smoothing, float scale, const float* scale_dev, float z_coef, int dt,
+                              void* stream) {
+  clear_error();
+  AK_REQUIRE(B >= 0 && V > 0 && V < (1LL << 31), AK_ERR_SHAPE, "ak_ce_rows_bwd: bad shape");
+  if (B == 0) return AK_OK;
+  AK_REQUIRE(grad && logits && targets && row_max && row_sum, AK_ERR_ARG, "ak_ce_rows_bwd: null pointer");
+  const CeParams p = make_params(softcap, ignore_index, label_smoothing, V);
+  const int es = elem_size(dt);
+  const bool vec_ok = aligned16(logits) && aligned16(grad) && ((V * es) % 16 == 0);
+  AK_DISPATCH_DTYPE(dt, T,
+                    ce_rows_bwd_kernel<T><<<row_grid(B), kThreads, 0, (cudaStream_t)stream>>>(
+                        (T*)grad, (const T*)logits, targets, row_max, row_sum, B, (int)V, p, scale, scale_dev,
+                        z_coef, vec_ok));
+  AK_CHECK_LAUNCH("ak_ce_rows_bwd");
+  return AK_OK;
+}
+
+extern "C" int ak_ce_rows_reduce(float* loss_out, float* n_valid_out, const float* losses, const float* lse,
+                                 const int64_t* targets, int64_t B, int64_t ignore_index, float z_loss_weight,
+                                 void* stream) {
+  clear_error();
+  AK_REQUIRE(B >= 0 && (B == 0 || (losses && targets)), AK_ERR_ARG, "ak_ce_rows_reduce: bad args");
+  AK_REQUIRE(z_loss_weight <= 0.f || lse || B == 0, AK_ERR_ARG, "ak_ce_rows_reduce: z-loss needs lse");
+  ce_reduce_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(loss_out, n_valid_out, losses, lse, targets, B,
+                                                         ignore_index, z_loss_weight);
+  AK_CHECK_LAUNCH("ak_ce_rows_reduce");
+  return AK_OK;
+}
+
+extern "C" int ak_ce_inv_valid(float* inv_out, const int64_t* targets, int64_t B, int64_t ignore_index,
+                               void* stream) {
+  clear_error();
+  AK_REQUIRE(inv_out && B >= 0 && (B == 0 || targets), AK_ERR_ARG, "ak_ce_inv_valid: bad args");
+  ce_inv_valid_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(inv_out, targets, B, ignore_index);
+  AK_CHECK_LAUNCH("ak_ce_inv_valid");
+  return AK_OK;
+}

@@ -1,0 +1,389 @@
+// RMSNorm forward / backward for sm_100a.
+//
+// Forward (reference semantics: reference.py:26-29, kernels/hip/rmsnorm.py:39-117):
+//   y = x * rsqrt(mean(x^2) + eps) * w
+// Backward (kernels/hip/_torch_ops.py:73-97):
+//   dx = r*dy*w - x * r^3 * sum(dy*w*x)/N,   dw = sum_rows dy*x*r
+//
+// Design: one warp per row, the row held in registers (16-byte vector loads,
+// one HBM read of x / dy), fp32 accumulation, warp-shuffle reductions only.
+// dw is reduced without global atomics: each CTA folds its rows into a private
+// fp32 partial row (workspace), and a second tiny kernel sums the partial rows
+// in a fixed order, so dw is bitwise deterministic.
+#include "ak_common.cuh"
+
+namespace ak {
+namespace {
+
+constexpr int kWarps = 8;  // rows in flight per CTA
+
+// ----------------------------------------------------------------------------
+// Forward, row in registers
+// ----------------------------------------------------------------------------
+template <typename T, typename TW, int VEC, int NIT>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __restrict__ x,
+                 const TW* __restrict__ w, int64_t M, int N, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float wr[NIT][VEC];
+#pragma unroll
+  for (int it = 0; it < NIT; ++it) {
+    const int c = (it * 32 + lane) * VEC;
+    if (c < N) load_frag<TW, VEC>(wr[it], w + c);
+    else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) wr[it][k] = 0.f;
+    }
+  }
+  const float inv_n = 1.f / (float)N;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < M; row += (int64_t)gridDim.x * kWarps) {
+    const T* xr = x + row * N;
+    float xv[NIT][VEC];
+    float ss = 0.f;
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
+      const int c = (it * 32 + lane) * VEC;
+      if (c < N) {
+        load_frag<T, VEC>(xv[it], xr + c);
+      } else {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) xv[it][k] = 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) ss = fmaf(xv[it][k], xv[it][k], ss);
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss * inv_n + eps);
+    if (rstd_out != nullptr && lane == 0) rstd_out[row] = r;
+    T* yr = y + row * N;
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
+      const int c = (it * 32 + lane) * VEC;
+      if (c < N) {
+        float o[VEC];
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) o[k] = xv[it][k] * r * wr[it][k];
+        store_frag<T, VEC>(yr + c, o);
+      }
+    }
+  }
+}
+
+// Forward fallback for rows that do not fit the register path (very wide or
+// unaligned rows): one CTA per row, scalar accesses, two passes (second from L2).
+template <typename T, typename TW>
+__global__ void __launch_bounds__(256)
+rmsnorm_fwd_block(T* __restrict__ y, float* __restrict__ rstd_out, const T* __restrict__ x,
+                  const TW* __restrict__ w, int64_t M, int N, float eps) {
+  __shared__ float red[32];
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const T* xr = x + row * N;
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+      const float v = to_f<T>(xr[c]);
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+    const float r = rsqrtf(tot / (float)N + eps);
+    if (rstd_out != nullptr && threadIdx.x == 0) rstd_out[row] = r;
+    T* yr = y + row * N;
+    for (int c = threadIdx.x; c < N; c += blockDim.x)
+      yr[c] = from_f<T>(to_f<T>(xr[c]) * r * to_f<TW>(w[c]));
+    __syncthreads();
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Backward, row in registers; per-CTA dw partial row into the workspace.
+// ----------------------------------------------------------------------------
+template <typename T, typename TW, int VEC, int NIT>
+__global__ void __launch_bounds__(kWarps * 32)
+rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __restrict__ dy,
+                 const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps) {
+  extern __shared__ float s_dw[];  // [kWarps][N]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  float wr[NIT][VEC], acc[NIT][VEC];
+#pragma unroll
+  for (int it = 0; it < NIT; ++it) {
+    const int c = (it * 32 + lane) * VEC;
+    if (c < N) load_frag<TW, VEC>(wr[it], w + c);
+    else {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) wr[it][k] = 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) acc[it][k] = 0.f;
+  }
+  const float inv_n = 1.f / (float)N;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < M; row += (int64_t)gridDim.x * kWarps) {
+    float xv[NIT][VEC], gv[NIT][VEC];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
+      const int c = (it * 32 + lane) * VEC;
+      if (c < N) {
+        load_frag<T, VEC>(xv[it], x + row * N + c);
+        load_frag<T, VEC>(gv[it], dy + row * N + c);
+      } else {
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) { xv[it][k] = 0.f; gv[it][k] = 0.f; }
+      }
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        s1 = fmaf(xv[it][k], xv[it][k], s1);
+        s2 = fmaf(gv[it][k] * wr[it][k], xv[it][k], s2);
+      }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    const float r = rsqrtf(s1 * inv_n + eps);
+    const float c3 = r * r * r * s2 * inv_n;
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
+      const int c = (it * 32 + lane) * VEC;
+      if (c < N) {
+        float o[VEC];
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+          o[k] = r * gv[it][k] * wr[it][k] - xv[it][k] * c3;
+          acc[it][k] = fmaf(gv[it][k], xv[it][k] * r, acc[it][k]);
+        }
+        store_frag<T, VEC>(dx + row * N + c, o);
+      }
+    }
+  }
+  // Fold the kWarps per-warp partials in a fixed order (deterministic).
+#pragma unroll
+  for (int it = 0; it < NIT; ++it) {
+    const int c = (it * 32 + lane) * VEC;
+    if (c < N) {
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) s_dw[warp * N + c + k] = acc[it][k];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < N; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) s += s_dw[i * N + c];
+    dw_part[(int64_t)blockIdx.x * N + c] = s;
+  }
+}
+
+// Backward fallback (wide / unaligned rows): one CTA per row at a time, the
+// CTA owns partial row blockIdx.x of the workspace exclusively.
+template <typename T, typename TW>
+__global__ void __launch_bounds__(256)
+rmsnorm_bwd_block(T* __restrict__ dx, float* __restrict__ dw_part, const T* __restrict__ dy,
+                  const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps) {
+  __shared__ float red1[32], red2[32];
+  float* part = dw_part + (int64_t)blockIdx.x * N;
+  for (int c = threadIdx.x; c < N; c += blockDim.x) part[c] = 0.f;
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const T* xr = x + row * N;
+    const T* gr = dy + row * N;
+    float s1 = 0.f, s2 = 0.f;
+    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+      const float xv = to_f<T>(xr[c]), gv = to_f<T>(gr[c]);
+      s1 = fmaf(xv, xv, s1);
+      s2 = fmaf(gv * to_f<TW>(w[c]), xv, s2);
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if ((threadIdx.x & 31) == 0) { red1[threadIdx.x >> 5] = s1; red2[threadIdx.x >> 5] = s2; }
+    __syncthreads();
+    float t1 = 0.f, t2 = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { t1 += red1[i]; t2 += red2[i]; }
+    const float r = rsqrtf(t1 / (float)N + eps);
+    const float c3 = r * r * r * t2 / (float)N;
+    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+      const float xv = to_f<T>(xr[c]), gv = to_f<T>(gr[c]);
+      dx[row * N + c] = from_f<T>(r * gv * to_f<TW>(w[c]) - xv * c3);
+      part[c] = fmaf(gv, xv * r, part[c]);
+    }
+    __syncthreads();
+  }
+}
+
+// dw[c] = sum_g part[g][c] in a fixed order.  Block (32, 8): 32 columns x 8
+// row-groups, folded through shared memory in index order.
+template <typename TD>
+__global__ void __launch_bounds__(256)
+rmsnorm_dw_reduce(TD* __restrict__ dw, const float* __restrict__ part, int G, int N) {
+  __shared__ float s[8][33];
+  const int c = blockIdx.x * 32 + threadIdx.x;
+  float acc = 0.f;
+  if (c < N)
+    for (int g = threadIdx.y; g < G; g += 8) acc += part[(int64_t)g * N + c];
+  s[threadIdx.y][threadIdx.x] = acc;
+  __syncthreads();
+  if (threadIdx.y == 0 && c < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += s[i][threadIdx.x];
+    dw[c] = from_f<TD>(t);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Host dispatch
+// ----------------------------------------------------------------------------
+int pick_nit(int N, int vec) {
+  const int need = (N + 32 * vec - 1) / (32 * vec);
+  const int opts[] = {1, 2, 3, 4, 6, 8, 12, 16};
+  for (int o : opts)
+    if (o >= need) return o;
+  return 0;  // too wide for the register path
+}
+
+#define AK_NIT_SWITCH(nit, NIT, ...)              \
+  switch (nit) {                                  \
+    case 1: { constexpr int NIT = 1; __VA_ARGS__; } break;   \
+    case 2: { constexpr int NIT = 2; __VA_ARGS__; } break;   \
+    case 3: { constexpr int NIT = 3; __VA_ARGS__; } break;   \
+    case 4: { constexpr int NIT = 4; __VA_ARGS__; } break;   \
+    case 6: { constexpr int NIT = 6; __VA_ARGS__; } break;   \
+    case 8: { constexpr int NIT = 8; __VA_ARGS__; } break;   \
+    case 12: { constexpr int NIT = 12; __VA_ARGS__; } break; \
+    case 16: { constexpr int NIT = 16; __VA_ARGS__; } break; \
+    default: break;                               \
+  }
+
+struct RmsPlan {
+  bool warp_path;
+  int vec, nit, grid;
+};
+
+template <typename T, typename TW>
+RmsPlan plan(int64_t M, int N, const void* a, const void* b, const void* w) {
+  RmsPlan p{};
+  constexpr int vec = 16 / sizeof(T);
+  const bool al = aligned16(a) && aligned16(b) &&
+                  (reinterpret_cast<uintptr_t>(w) % (sizeof(TW) * vec) == 0);
+  p.vec = vec;
+  p.nit = (N % vec == 0 && al) ? pick_nit(N, vec) : 0;
+  p.warp_path = p.nit > 0;
+  return p;
+}
+
+int bwd_grid(int64_t M, int N) {
+  const int64_t rows_per_cta = kWarps;
+  int64_t g = (M + rows_per_cta - 1) / rows_per_cta;
+  const int64_t cap = 2LL * sm_count();
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  (void)N;
+  return (int)g;
+}
+
+template <typename T, typename TW>
+int fwd_impl(void* y, float* rstd, const void* x, const void* w, int64_t M, int N, float eps,
+             cudaStream_t st) {
+  RmsPlan p = plan<T, TW>(M, N, x, y, w);
+  constexpr int VEC = 16 / sizeof(T);
+  if (p.warp_path) {
+    int64_t g = (M + kWarps - 1) / kWarps;
+    const int64_t cap = (int64_t)sm_count() * 16;
+    if (g > cap) g = cap;
+    AK_NIT_SWITCH(p.nit, NIT,
+                  rmsnorm_fwd_warp<T, TW, VEC, NIT><<<(unsigned)g, kWarps * 32, 0, st>>>(
+                      (T*)y, rstd, (const T*)x, (const TW*)w, M, N, eps));
+  } else {
+    int64_t g = M;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (g > cap) g = cap;
+    rmsnorm_fwd_block<T, TW><<<(unsigned)g, 256, 0, st>>>((T*)y, rstd, (const T*)x,
+                                                          (const TW*)w, M, N, eps);
+  }
+  AK_CHECK_LAUNCH("ak_rmsnorm_fwd");
+  return AK_OK;
+}
+
+template <typename T, typename TW>
+int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const void* x, const void* w,
+             int64_t M, int N, float eps, cudaStream_t st) {
+  RmsPlan p = plan<T, TW>(M, N, x, dx, w);
+  if (!aligned16(dy)) p.warp_path = false;
+  // x, dy, w and the dw accumulator all live in registers: beyond 32 elements
+  // per lane the register path spills, so wider rows take the CTA fallback.
+  if (p.nit * p.vec > 32) p.warp_path = false;
+  constexpr int VEC = 16 / sizeof(T);
+  const int G = bwd_grid(M, N);
+  if (M > 0) {
+    if (p.warp_path) {
+      const size_t smem = (size_t)kWarps * N * sizeof(float);
+      AK_NIT_SWITCH(p.nit, NIT, {
+        auto kern = rmsnorm_bwd_warp<T, TW, VEC, NIT>;
+        if (smem > 48 * 1024)
+          AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                      "ak_rmsnorm_bwd: smem attribute");
+        kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps);
+      });
+    } else {
+      rmsnorm_bwd_block<T, TW><<<G, 256, 0, st>>>((T*)dx, ws, (const T*)dy, (const T*)x,
+                                                  (const TW*)w, M, N, eps);
+    }
+    AK_CHECK_LAUNCH("ak_rmsnorm_bwd");
+  }
+  const int Gred = M > 0 ? G : 0;
+  dim3 rb(32, 8);
+  const unsigned rg = (unsigned)((N + 31) / 32);
+  AK_DISPATCH_DTYPE(dt_dw, TD, rmsnorm_dw_reduce<TD><<<rg, rb, 0, st>>>((TD*)dw, ws, Gred, N));
+  AK_CHECK_LAUNCH("ak_rmsnorm_bwd(dw reduce)");
+  return AK_OK;
+}
+
+}  // namespace
+}  // namespace ak
+
+using namespace ak;
+
+#define AK_DISPATCH_XW(dt_x, dt_w, ...)                                                   \
+  do {                                                                                     \
+    if (dt_x == AK_F32 && dt_w == AK_F32) { using T = float; using TW = float; __VA_ARGS__; }      \
+    else if (dt_x == AK_BF16 && dt_w == AK_BF16) { using T = __nv_bfloat16; using TW = __nv_bfloat16; __VA_ARGS__; } \
+    else if (dt_x == AK_BF16 && dt_w == AK_F32) { using T = __nv_bfloat16; using TW = float; __VA_ARGS__; } \
+    else if (dt_x == AK_F16 && dt_w == AK_F16) { using T = __half; using TW = __half; __VA_ARGS__; } \
+    else if (dt_x == AK_F16 && dt_w == AK_F32) { using T = __half; using TW = float; __VA_ARGS__; } \
+    else { set_error("rmsnorm: unsupported dtype pair x=%d w=%d", dt_x, dt_w); return AK_ERR_DTYPE; } \
+  } while (0)
+
+extern "C" int ak_rmsnorm_fwd(void* y, float* rstd, const void* x, const void* w, int64_t M,
+                              int64_t N, float eps, int dt_x, int dt_w, void* stream) {
+  clear_error();
+  AK_REQUIRE(M >= 0 && N > 0 && N <= (1 << 24), AK_ERR_SHAPE, "ak_rmsnorm_fwd: bad shape M=%lld N=%lld",
+             (long long)M, (long long)N);
+  if (M == 0) return AK_OK;
+  AK_REQUIRE(y && x && w, AK_ERR_ARG, "ak_rmsnorm_fwd: null pointer");
+  AK_DISPATCH_XW(dt_x, dt_w, return fwd_impl<T, TW>(y, rstd, x, w, M, (int)N, eps, (cudaStream_t)stream));
+  return AK_OK;
+}
+
+extern "C" int ak_rmsnorm_bwd_workspace_size(int64_t M, int64_t N, size_t* bytes) {
+  clear_error();
+  AK_REQUIRE(bytes && M >= 0 && N > 0, AK_ERR_ARG, "ak_rmsnorm_bwd_workspace_size: bad args");
+  *bytes = (size_t)bwd_grid(M, (int)N) * (size_t)N * sizeof(float);
+  return AK_OK;
+}
+
+extern "C" int ak_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspace, size_t ws_bytes,
+                              const void* dy, const void* x, const void* w, int64_t M, int64_t N,
+                              float eps, int dt_x, int dt_w, void* stream) {
+  clear_error();
+  AK_REQUIRE(M >= 0 && N > 0 && N <= (1 << 24), AK_ERR_SHAPE, "ak_rmsnorm_bwd: bad shape");
+  AK_REQUIRE(dw && w, AK_ERR_ARG, "ak_rmsnorm_bwd: null pointer");
+  AK_REQUIRE(M == 0 || (dx && dy && x), AK_ERR_ARG, "ak_rmsnorm_bwd: null pointer");
+  const size_t need = (size_t)bwd_grid(M, (int)N) * (size_t)N * sizeof(float);
+  AK_REQUIRE(M == 0 || (workspace && ws_bytes >= need), AK_ERR_WORKSPACE,
+             "ak_rmsnorm_bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  AK_DISPATCH_XW(dt_x, dt_w,
+                 return bwd_impl<T, TW>(dx, dw, dt_dw, (float*)workspace, dy, x, w, M, (int)N, eps,
+                                        (cudaStream_t)stream));
+  return AK_OK;
+}

@@ -1,0 +1,363 @@
+"""ctypes binding of libak_b200.so (the sm_100a kernels) plus tensor-level wrappers.
+
+Every wrapper allocates its outputs and workspaces with PyTorch on the input's
+device, passes raw pointers and PyTorch's current stream to the C ABI
+(`include/ak_b200.h`), and raises `AkError` with the library's message when a
+call fails.  There is no CPU or PyTorch fallback: inputs must be CUDA tensors
+and the shared library must be present, otherwise the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+from typing import Optional, Sequence
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent.parent / "libak_b200.so"
+
+F32, BF16, F16 = 0, 1, 2
+_DT = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+_vp, _i64, _f, _i, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_int, ctypes.c_size_t
+
+# name -> argtypes (all entry points return int status)
+SIGNATURES = {
+    "ak_version": [],
+    "ak_rmsnorm_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
+    "ak_rmsnorm_bwd_workspace_size": [_i64, _i64, ctypes.POINTER(_sz)],
+    "ak_rmsnorm_bwd": [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
+    "ak_softmax_fwd": [_vp, _vp, _i64, _i64, _i, _vp],
+    "ak_softmax_bwd": [_vp, _vp, _vp, _i64, _i64, _i, _vp],
+    "ak_ce_rows_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _i, _vp],
+    "ak_ce_rows_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _f, _i, _vp],
+    "ak_ce_rows_reduce": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp],
+    "ak_ce_inv_valid": [_vp, _vp, _i64, _i64, _vp],
+    "ak_scan1_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "ak_scan1_bwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
+    "ak_scan1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "ak_selective_scan_state_stride": [],
+    "ak_selective_scan_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
+                              _i64, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_selective_scan_bwd_workspace_size": [_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_sz)],
+    "ak_selective_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp,
+                              _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64, _i64, _i, _vp],
+}
+
+
+class AkError(RuntimeError):
+    """A libak_b200 entry point returned a nonzero status."""
+
+
+_lib: Optional[ctypes.CDLL] = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """Load libak_b200.so once (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise ImportError(
+                        f"libak_b200.so not found at {LIB_PATH}; build it with "
+                        "`python autokernel-halo-strix_b200/csrc/build.py`")
+                handle = ctypes.CDLL(str(LIB_PATH))
+                for name, argtypes in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.argtypes = argtypes
+                    fn.restype = ctypes.c_int
+                handle.ak_last_error.argtypes = []
+                handle.ak_last_error.restype = ctypes.c_char_p
+                _lib = handle
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    rc = getattr(lib(), name)(*args)
+    if rc != 0:
+        msg = lib().ak_last_error().decode(errors="replace")
+        raise AkError(f"{name} failed (status {rc}): {msg}")
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32, bfloat16 or float16") from None
+
+
+def ptr(t: Optional[torch.Tensor]):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("autokernel B200 kernels need CUDA tensors (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} vs {t.device}")
+    if dev is None:
+        raise RuntimeError("no tensor given")
+    return dev
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def _size_query(name: str, *dims: int) -> int:
+    out = ctypes.c_size_t(0)
+    call(name, *dims, ctypes.byref(out))
+    return int(out.value)
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm
+# ---------------------------------------------------------------------------
+def rmsnorm_fwd(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, want_rstd: bool = False):
+    dev = require_cuda(x, w)
+    x = x.contiguous()
+    w = w.contiguous()
+    N = x.shape[-1]
+    M = x.numel() // N if N else 0
+    y = torch.empty_like(x)
+    rstd = torch.empty(M, dtype=torch.float32, device=dev) if want_rstd else None
+    call("ak_rmsnorm_fwd", ptr(y), ptr(rstd), ptr(x), ptr(w), M, N, float(eps), dtype_code(x), dtype_code(w),
+         stream(dev))
+    return (y, rstd) if want_rstd else y
+
+
+def rmsnorm_bwd(x: torch.Tensor, w: torch.Tensor, dy: torch.Tensor, eps: float = 1e-6,
+                dw_dtype: torch.dtype = torch.float32):
+    dev = require_cuda(x, w, dy)
+    x = x.contiguous()
+    w = w.contiguous()
+    dy = dy.to(x.dtype).contiguous()
+    N = x.shape[-1]
+    M = x.numel() // N if N else 0
+    dx = torch.empty_like(x)
+    dw = torch.empty(N, dtype=dw_dtype, device=dev)
+    ws_bytes = _size_query("ak_rmsnorm_bwd_workspace_size", M, N)
+    ws = workspace(ws_bytes, dev)
+    call("ak_rmsnorm_bwd", ptr(dx), ptr(dw), _DT[dw_dtype], ptr(ws), ws_bytes, ptr(dy), ptr(x), ptr(w), M, N,
+         float(eps), dtype_code(x), dtype_code(w), stream(dev))
+    return dx, dw
+
+
+# ---------------------------------------------------------------------------
+# Softmax (last dim)
+# ---------------------------------------------------------------------------
+def softmax_fwd(x: torch.Tensor) -> torch.Tensor:
+    dev = require_cuda(x)
+    x = x.contiguous()
+    cols = x.shape[-1] if x.dim() > 0 else 1
+    rows = x.numel() // cols if cols else 0
+    y = torch.empty_like(x)
+    if x.numel():
+        call("ak_softmax_fwd", ptr(y), ptr(x), rows, cols, dtype_code(x), stream(dev))
+    return y
+
+
+def softmax_bwd(y: torch.Tensor, dy: torch.Tensor) -> torch.Tensor:
+    dev = require_cuda(y, dy)
+    y = y.contiguous()
+    dy = dy.to(y.dtype).contiguous()
+    cols = y.shape[-1] if y.dim() > 0 else 1
+    rows = y.numel() // cols if cols else 0
+    dx = torch.empty_like(y)
+    if y.numel():
+        call("ak_softmax_bwd", ptr(dx), ptr(y), ptr(dy), rows, cols, dtype_code(y), stream(dev))
+    return dx
+
+
+# ---------------------------------------------------------------------------
+# Cross entropy over logit rows
+# ---------------------------------------------------------------------------
+def ce_rows_fwd(logits: torch.Tensor, targets: torch.Tensor, softcap: float = 0.0, ignore_index: int = -100,
+                label_smoothing: float = 0.0, write_grad: bool = False, save_max_sum: bool = False,
+                scale_grad: float = 1.0, scale_dev: Optional[torch.Tensor] = None):
+    """Returns [losses, lse, row_max, row_sum, grad] (absent ones are None)."""
+    dev = require_cuda(logits, targets)
+    logits = logits.contiguous()
+    targets = targets.to(torch.int64).contiguous()
+    B, V = logits.shape
+    f32 = dict(dtype=torch.float32, device=dev)
+    losses = torch.empty(B, **f32)
+    lse = torch.empty(B, **f32)
+    rmax = torch.empty(B, **f32) if save_max_sum else None
+    rsum = torch.empty(B, **f32) if save_max_sum else None
+    grad = torch.empty_like(logits) if write_grad else None
+    if scale_dev is not None:
+        scale_dev = scale_dev.to(torch.float32).contiguous()
+    call("ak_ce_rows_fwd", ptr(losses), ptr(lse), ptr(rmax), ptr(rsum), ptr(grad), ptr(logits), ptr(targets), B, V,
+         float(softcap), int(ignore_index), float(label_smoothing), float(scale_grad), ptr(scale_dev),
+         dtype_code(logits), stream(dev))
+    return [losses, lse, rmax, rsum, grad]
+
+
+def ce_rows_bwd(logits, targets, row_max, row_sum, softcap=0.0, ignore_index=-100, label_smoothing=0.0,
+                scale=1.0, scale_dev: Optional[torch.Tensor] = None, z_coef: float = 0.0,
+                out: Optional[torch.Tensor] = None):
+    dev = require_cuda(logits, targets, row_max, row_sum)
+    logits = logits.contiguous()
+    targets = targets.to(torch.int64).contiguous()
+    B, V = logits.shape
+    grad = torch.empty_like(logits) if out is None else out
+    if scale_dev is not None:
+        scale_dev = scale_dev.to(torch.float32).contiguous()
+    call("ak_ce_rows_bwd", ptr(grad), ptr(logits), ptr(targets), ptr(row_max.contiguous()),
+         ptr(row_sum.contiguous()), B, V, float(softcap), int(ignore_index), float(label_smoothing), float(scale),
+         ptr(scale_dev), float(z_coef), dtype_code(logits), stream(dev))
+    return grad
+
+
+def ce_rows_reduce(losses, lse, targets, ignore_index=-100, z_loss_weight=0.0):
+    """Device-side mean over valid rows; returns (loss 0-d fp32, n_valid 0-d fp32)."""
+    dev = require_cuda(losses, targets)
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    nvalid = torch.empty((), dtype=torch.float32, device=dev)
+    targets = targets.to(torch.int64).contiguous()
+    call("ak_ce_rows_reduce", ptr(loss), ptr(nvalid), ptr(losses.contiguous()),
+         ptr(lse.contiguous() if lse is not None else None), ptr(targets), targets.numel(), int(ignore_index),
+         float(z_loss_weight), stream(dev))
+    return loss, nvalid
+
+
+def ce_inv_valid(targets: torch.Tensor, ignore_index: int = -100) -> torch.Tensor:
+    dev = require_cuda(targets)
+    targets = targets.to(torch.int64).contiguous()
+    inv = torch.empty((), dtype=torch.float32, device=dev)
+    call("ak_ce_inv_valid", ptr(inv), ptr(targets), targets.numel(), int(ignore_index), stream(dev))
+    return inv
+
+
+# ---------------------------------------------------------------------------
+# Collapsed selective scan (fp32, (B, L, d))
+# ---------------------------------------------------------------------------
+def _f32c(t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.float32:
+        raise TypeError(f"collapsed selective scan is fp32-only (got {t.dtype})")
+    return t.contiguous()
+
+
+def scan1_fwd(dA, dBx, C, D, x) -> torch.Tensor:
+    dev = require_cuda(dA, dBx, C, D, x)
+    dA, dBx, C, D, x = map(_f32c, (dA, dBx, C, D, x))
+    if dA.dim() != 3:
+        raise ValueError("dA must be 3D [batch, seq, d_inner]")
+    B, L, d = dA.shape
+    y = torch.empty_like(dA)
+    call("ak_scan1_fwd", ptr(y), ptr(dA), ptr(dBx), ptr(C), ptr(D), ptr(x), B, L, d, stream(dev))
+    return y
+
+
+def scan1_bwd(dA, dBx, C, D, x, gy):
+    dev = require_cuda(dA, dBx, C, D, x, gy)
+    dA, dBx, C, D, x, gy = map(_f32c, (dA, dBx, C, D, x, gy))
+    B, L, d = dA.shape
+    gdA, gdBx, gC, gx = (torch.empty_like(dA) for _ in range(4))
+    gD = torch.empty(d, dtype=torch.float32, device=dev)
+    ws_bytes = _size_query("ak_scan1_bwd_workspace_size", B, L, d)
+    ws = workspace(ws_bytes, dev)
+    call("ak_scan1_bwd", ptr(gdA), ptr(gdBx), ptr(gC), ptr(gD), ptr(gx), ptr(ws), ws_bytes, ptr(dA), ptr(dBx),
+         ptr(C), ptr(D), ptr(x), ptr(gy), B, L, d, stream(dev))
+    return gdA, gdBx, gC, gD, gx
+
+
+# ---------------------------------------------------------------------------
+# Mamba-style selective scan ((batch, dim, L), N states)
+# ---------------------------------------------------------------------------
+def state_stride() -> int:
+    return int(lib().ak_selective_scan_state_stride())
+
+
+def _bc4(t: torch.Tensor) -> torch.Tensor:
+    if t.dim() == 3:
+        return t.unsqueeze(1)
+    if t.dim() == 4:
+        return t
+    raise NotImplementedError("only input-dependent B/C of shape (batch, N, L) or (batch, G, N, L) are supported")
+
+
+def selective_scan_fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                       save_states: bool = True):
+    """Returns (out, last_state, chunk_states)."""
+    dev = require_cuda(u, delta, A, B, C, D, z, delta_bias)
+    if A.is_complex():
+        raise NotImplementedError("complex A is not supported")
+    u = u.contiguous()
+    dtype = u.dtype
+    delta = delta.to(dtype).contiguous()
+    B4 = _bc4(B).to(dtype).contiguous()
+    C4 = _bc4(C).to(dtype).contiguous()
+    if B4.shape[1] != C4.shape[1]:
+        raise ValueError("B and C must have the same number of groups")
+    A = A.to(torch.float32).contiguous()
+    D = D.to(torch.float32).contiguous() if D is not None else None
+    z = z.to(dtype).contiguous() if z is not None else None
+    delta_bias = delta_bias.to(torch.float32).contiguous() if delta_bias is not None else None
+    batch, dim, L = u.shape
+    N = A.shape[1]
+    G = B4.shape[1]
+    out = torch.empty_like(u)
+    f32 = dict(dtype=torch.float32, device=dev)
+    last = torch.empty(batch, dim, N, **f32)
+    nsaved = (L + state_stride() - 1) // state_stride()
+    states = torch.empty(batch, dim, nsaved, N, **f32) if save_states else None
+    call("ak_selective_scan_fwd", ptr(out), ptr(last), ptr(states), ptr(u), ptr(delta), ptr(A), ptr(B4), ptr(C4),
+         ptr(D), ptr(z), ptr(delta_bias), int(bool(delta_softplus)), batch, dim, L, N, G, dtype_code(u), stream(dev))
+    return out, last, states
+
+
+def selective_scan_bwd(dout, u, delta, A, B, C, D, z, delta_bias, delta_softplus, chunk_states):
+    """Returns (du, ddelta, dA, dB, dC, dD, dz, ddelta_bias) with B/C grads shaped like B/C."""
+    dev = require_cuda(dout, u, delta, A, B, C)
+    u = u.contiguous()
+    dtype = u.dtype
+    delta = delta.to(dtype).contiguous()
+    dout = dout.to(dtype).contiguous()
+    B4 = _bc4(B).to(dtype).contiguous()
+    C4 = _bc4(C).to(dtype).contiguous()
+    A = A.to(torch.float32).contiguous()
+    D = D.to(torch.float32).contiguous() if D is not None else None
+    z = z.to(dtype).contiguous() if z is not None else None
+    delta_bias = delta_bias.to(torch.float32).contiguous() if delta_bias is not None else None
+    batch, dim, L = u.shape
+    N = A.shape[1]
+    G = B4.shape[1]
+    f32 = dict(dtype=torch.float32, device=dev)
+    du = torch.empty_like(u)
+    ddelta = torch.empty_like(u)
+    dA = torch.empty(dim, N, **f32)
+    dB = torch.empty_like(B4)
+    dC = torch.empty_like(C4)
+    dD = torch.empty(dim, **f32) if D is not None else None
+    dz = torch.empty_like(u) if z is not None else None
+    dbias = torch.empty(dim, **f32) if delta_bias is not None else None
+    ws_bytes = _size_query("ak_selective_scan_bwd_workspace_size", batch, dim, L, N, G)
+    ws = workspace(ws_bytes, dev)
+    call("ak_selective_scan_bwd", ptr(du), ptr(ddelta), ptr(dA), ptr(dB), ptr(dC), ptr(dD), ptr(dz), ptr(dbias),
+         ptr(ws), ws_bytes, ptr(dout), ptr(u), ptr(delta), ptr(A), ptr(B4), ptr(C4), ptr(D), ptr(z),
+         ptr(delta_bias), ptr(chunk_states), int(bool(delta_softplus)), batch, dim, L, N, G, dtype_code(u),
+         stream(dev))
+    if B.dim() == 3:
+        dB = dB.squeeze(1)
+    if C.dim() == 3:
+        dC = dC.squeeze(1)
+    return du, ddelta, dA, dB, dC, dD, dz, dbias
+
+
+def exported_symbols() -> Sequence[str]:
+    return list(SIGNATURES) + ["ak_last_error"]

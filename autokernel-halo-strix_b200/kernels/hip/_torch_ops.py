@@ -1,0 +1,191 @@
+"""Register the B200 kernels as `torch.library` custom ops (namespace `autokernel`).
+
+Mirrors kernels/hip/_torch_ops.py of the reference:
+  * `torch.ops.autokernel.rmsnorm(Tensor x, Tensor weight) -> Tensor`
+    (reference _torch_ops.py:56-111: fake = empty like x, autograd grads
+    (dx, dw), autocast rule cuda/fp16, eps fixed at 1e-6 as in :70);
+  * `torch.ops.autokernel.selective_scan(Tensor dA, Tensor dBx, Tensor C,
+    Tensor D, Tensor x) -> Tensor` (reference :312-394, grads
+    (d dA, d dBx, dC, dD, dx)).
+Added here (no reference counterpart):
+  * `autokernel::rmsnorm_eps(x, weight, eps)` — same op with the module's eps
+    and no autocast cast, used by the module replacement;
+  * `autokernel::softmax(x)` — differentiable row softmax;
+  * the backward passes as their own custom ops (`*_bwd`), so torch.compile
+    sees opaque nodes in both directions instead of tracing into ctypes calls.
+
+Every op body calls libak_b200.so; there is no PyTorch fallback.  The
+reference's `AUTOKERNEL_NO_BWD_HIP` / `disable_hip_backward()` switch selects a
+PyTorch backward there; here the backward is always the CUDA custom op, so the
+switch is accepted for compatibility and has no effect.
+"""
+import os
+from typing import List, Tuple
+
+import torch
+
+from kernels import _ak
+
+_USE_BWD_HIP = os.environ.get("AUTOKERNEL_NO_BWD_HIP", "0") != "1"
+
+
+def _use_hip_backward() -> bool:
+    """Kept for API compatibility; the CUDA backward is always used."""
+    return True
+
+
+def disable_hip_backward() -> None:
+    """Kept for API compatibility (the backward custom ops are compile-safe)."""
+    global _USE_BWD_HIP
+    _USE_BWD_HIP = False
+
+
+RMSNORM_EPS = 1e-6
+
+# ---------------------------------------------------------------------------
+# RMSNorm
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::rmsnorm_bwd", mutates_args=())
+def rmsnorm_bwd_op(x: torch.Tensor, weight: torch.Tensor, grad: torch.Tensor, eps: float) -> List[torch.Tensor]:
+    x2 = x.reshape(-1, x.shape[-1])
+    gx, gw = _ak.rmsnorm_bwd(x2, weight, grad.reshape(-1, grad.shape[-1]), eps, dw_dtype=torch.float32)
+    return [gx.view(x.shape), gw.to(weight.dtype)]
+
+
+@rmsnorm_bwd_op.register_fake
+def _(x, weight, grad, eps):
+    return [x.new_empty(x.shape), weight.new_empty(weight.shape)]
+
+
+@torch.library.custom_op("autokernel::rmsnorm", mutates_args=())
+def rmsnorm_op(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    return _ak.rmsnorm_fwd(x, weight, RMSNORM_EPS)
+
+
+@rmsnorm_op.register_fake
+def _(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    return x.new_empty(x.shape)
+
+
+def _rmsnorm_setup(ctx, inputs, output):
+    x, weight = inputs
+    ctx.save_for_backward(x, weight)
+    ctx.eps = RMSNORM_EPS
+
+
+def _rmsnorm_backward(ctx, grad_output):
+    x, weight = ctx.saved_tensors
+    gx, gw = torch.ops.autokernel.rmsnorm_bwd(x, weight, grad_output.contiguous(), ctx.eps)
+    return gx, gw
+
+
+rmsnorm_op.register_autograd(_rmsnorm_backward, setup_context=_rmsnorm_setup)
+try:
+    rmsnorm_op.register_autocast("cuda", torch.float16)
+except AttributeError:  # older PyTorch
+    pass
+
+
+@torch.library.custom_op("autokernel::rmsnorm_eps", mutates_args=())
+def rmsnorm_eps_op(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    return _ak.rmsnorm_fwd(x, weight, eps)
+
+
+@rmsnorm_eps_op.register_fake
+def _(x, weight, eps):
+    return x.new_empty(x.shape)
+
+
+def _rmsnorm_eps_setup(ctx, inputs, output):
+    x, weight, eps = inputs
+    ctx.save_for_backward(x, weight)
+    ctx.eps = eps
+
+
+def _rmsnorm_eps_backward(ctx, grad_output):
+    x, weight = ctx.saved_tensors
+    gx, gw = torch.ops.autokernel.rmsnorm_bwd(x, weight, grad_output.contiguous(), ctx.eps)
+    return gx, gw, None
+
+
+rmsnorm_eps_op.register_autograd(_rmsnorm_eps_backward, setup_context=_rmsnorm_eps_setup)
+
+# ---------------------------------------------------------------------------
+# Softmax (last dim)
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::softmax_bwd", mutates_args=())
+def softmax_bwd_op(y: torch.Tensor, grad: torch.Tensor) -> torch.Tensor:
+    return _ak.softmax_bwd(y, grad)
+
+
+@softmax_bwd_op.register_fake
+def _(y, grad):
+    return y.new_empty(y.shape)
+
+
+@torch.library.custom_op("autokernel::softmax", mutates_args=())
+def softmax_op(x: torch.Tensor) -> torch.Tensor:
+    return _ak.softmax_fwd(x)
+
+
+@softmax_op.register_fake
+def _(x):
+    return x.new_empty(x.shape)
+
+
+def _softmax_setup(ctx, inputs, output):
+    ctx.save_for_backward(output)
+
+
+def _softmax_backward(ctx, grad_output):
+    (y,) = ctx.saved_tensors
+    return torch.ops.autokernel.softmax_bwd(y, grad_output.contiguous())
+
+
+softmax_op.register_autograd(_softmax_backward, setup_context=_softmax_setup)
+
+# ---------------------------------------------------------------------------
+# Collapsed selective scan
+# forward: state[t] = dA[t] * state[t-1] + dBx[t]; y[t] = C[t]*state[t] + D*x[t]
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::selective_scan_bwd", mutates_args=())
+def selective_scan_bwd_op(dA: torch.Tensor, dBx: torch.Tensor, C: torch.Tensor, D: torch.Tensor, x: torch.Tensor,
+                          grad_y: torch.Tensor) -> List[torch.Tensor]:
+    return list(_ak.scan1_bwd(dA, dBx, C, D, x, grad_y.float()))
+
+
+@selective_scan_bwd_op.register_fake
+def _(dA, dBx, C, D, x, grad_y):
+    return [dA.new_empty(dA.shape), dBx.new_empty(dBx.shape), C.new_empty(C.shape), D.new_empty(D.shape),
+            x.new_empty(x.shape)]
+
+
+@torch.library.custom_op("autokernel::selective_scan", mutates_args=())
+def selective_scan_op(dA: torch.Tensor, dBx: torch.Tensor, C: torch.Tensor, D: torch.Tensor,
+                      x: torch.Tensor) -> torch.Tensor:
+    return _ak.scan1_fwd(dA, dBx, C, D, x)
+
+
+@selective_scan_op.register_fake
+def _(dA, dBx, C, D, x):
+    return dA.new_empty(dA.shape)
+
+
+def _selective_scan_setup(ctx, inputs, output):
+    dA, dBx, C, D, x = inputs
+    ctx.save_for_backward(dA, dBx, C, D, x, output)
+
+
+def _selective_scan_backward(ctx, grad_y):
+    dA, dBx, C, D, x, _y = ctx.saved_tensors
+    gdA, gdBx, gC, gD, gx = torch.ops.autokernel.selective_scan_bwd(dA, dBx, C, D, x, grad_y.contiguous())
+    return (gdA.to(dA.dtype), gdBx.to(dBx.dtype), gC.to(C.dtype), gD.to(D.dtype), gx.to(x.dtype))
+
+
+selective_scan_op.register_autograd(_selective_scan_backward, setup_context=_selective_scan_setup)

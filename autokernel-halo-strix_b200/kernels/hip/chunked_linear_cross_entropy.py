@@ -1,0 +1,94 @@
+"""Chunked linear + cross-entropy on B200 (logits never materialised in full).
+
+Drop-in for kernels/hip/chunked_linear_cross_entropy.py of the reference
+(`ChunkedLinearCrossEntropyLoss`, :178-229; `_ChunkedLinearCrossEntropy`,
+:50-175): for each row chunk, logits = h W^T, the fused CE row kernel writes
+loss, lse and the pre-scaled gradient G, then dH = G W and dW += G^T h (fp32
+accumulation).  All gradients are produced in the forward; the backward
+returns them scaled by grad_output.
+
+Differences, all deliberate: inputs keep their dtype (the reference coerces to
+fp16, :219-223); the valid-row count and 1/n_valid stay on the device (the
+reference syncs with `.item()`, :73).
+"""
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+from torch.amp import custom_bwd, custom_fwd
+
+from kernels import _ak
+
+
+class _ChunkedLinearCrossEntropy(torch.autograd.Function):
+    @staticmethod
+    @custom_fwd(device_type="cuda")
+    def forward(ctx, hidden, weight, targets, chunk_size, softcap, ignore_index, label_smoothing, z_loss_weight):
+        N, D = hidden.shape
+        V = weight.shape[0]
+        dev = hidden.device
+        h = hidden.contiguous()
+        w = weight.to(h.dtype).contiguous()
+        t = targets.contiguous()
+        inv_valid = _ak.ce_inv_valid(t, ignore_index)
+        losses = torch.empty(N, dtype=torch.float32, device=dev)
+        lse = torch.empty(N, dtype=torch.float32, device=dev)
+        grad_h = torch.empty_like(h) if hidden.requires_grad else None
+        grad_w = torch.zeros(V, D, dtype=torch.float32, device=dev) if weight.requires_grad else None
+        for s in range(0, N, chunk_size):
+            e = min(s + chunk_size, N)
+            logits = F.linear(h[s:e], w)
+            if z_loss_weight > 0:
+                # z-loss gradient 2 w lse softmax / n_valid needs the final lse: two passes.
+                lc, zc, rm, rs, _ = _ak.ce_rows_fwd(logits, t[s:e], softcap, ignore_index, label_smoothing,
+                                                    save_max_sum=True)
+                g = _ak.ce_rows_bwd(logits, t[s:e], rm, rs, softcap, ignore_index, label_smoothing, scale=1.0,
+                                    scale_dev=inv_valid, z_coef=2.0 * z_loss_weight, out=logits)
+            else:
+                lc, zc, _, _, g = _ak.ce_rows_fwd(logits, t[s:e], softcap, ignore_index, label_smoothing,
+                                                  write_grad=True, scale_grad=1.0, scale_dev=inv_valid)
+            losses[s:e] = lc
+            lse[s:e] = zc
+            if grad_h is not None:
+                torch.mm(g, w, out=grad_h[s:e])
+            if grad_w is not None:
+                grad_w += torch.mm(g.t(), h[s:e], out_dtype=torch.float32)
+        loss, _ = _ak.ce_rows_reduce(losses, lse, t, ignore_index, z_loss_weight)
+        ctx.save_for_backward(grad_h, grad_w.to(weight.dtype) if grad_w is not None else None)
+        ctx.req = (hidden.requires_grad, weight.requires_grad)
+        return loss
+
+    @staticmethod
+    @custom_bwd(device_type="cuda")
+    def backward(ctx, grad_output):
+        gh, gw = ctx.saved_tensors
+        one = grad_output.dim() == 0 and grad_output.item() == 1.0
+        if ctx.req[0]:
+            gh = gh if one else gh * grad_output.to(gh.dtype)
+        if ctx.req[1]:
+            gw = gw if one else gw * grad_output.to(gw.dtype)
+        return gh, gw, None, None, None, None, None, None
+
+
+class ChunkedLinearCrossEntropyLoss(nn.Module):
+    """`nn.Linear + nn.CrossEntropyLoss` without materialising all logits.
+
+    Args mirror the reference: chunk_size, softcap, ignore_index, label_smoothing, z_loss_weight.
+    forward(hidden (N, D) or (B, T, D), weight (V, D), targets (N,) or (B, T)) -> scalar mean loss.
+    """
+
+    def __init__(self, chunk_size: int = 512, softcap: float = 0.0, ignore_index: int = -100,
+                 label_smoothing: float = 0.0, z_loss_weight: float = 0.0):
+        super().__init__()
+        self.chunk_size = int(chunk_size)
+        self.softcap = float(softcap)
+        self.ignore_index = int(ignore_index)
+        self.label_smoothing = float(label_smoothing)
+        self.z_loss_weight = float(z_loss_weight)
+
+    def forward(self, hidden, weight, targets):
+        if hidden.dim() == 3:
+            hidden = hidden.reshape(-1, hidden.shape[-1])
+        if targets.dim() == 2:
+            targets = targets.reshape(-1)
+        return _ChunkedLinearCrossEntropy.apply(hidden, weight, targets, self.chunk_size, self.softcap,
+                                                self.ignore_index, self.label_smoothing, self.z_loss_weight)

@@ -1,0 +1,451 @@
+"""Benchmark of the hot path on B200: selective-scan forward+backward (headline)
+plus the other swapped ops, with roofline fractions and a CPU baseline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+
+Headline workload: Mamba-style selective scan, B=8,
+D=1536, L=2048, N=16, bf16 inputs, fp32 state, softplus(delta + bias), SiLU(z)
+gate, last state; one step = forward + backward over one batch per rank
+(weak scaling: every rank processes its own batch; no collective on the data
+path).  `value` = algorithmic bytes of all ranks / max-over-ranks device time.
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "autokernel-halo-strix_b200"
+for _p in (str(PKG), str(REPO)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+HEADLINE = dict(batch=8, dim=1536, L=2048, N=16, groups=1)
+METRIC = "selective_scan fwd+bwd HBM GB/s (algorithmic bytes / device time)"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures, scaled
+# to the full config where the capture was smaller (see profiles/).  None = not captured.
+NCU_TRAFFIC_BYTES = {
+    "sscan_bwd": None,
+}
+
+
+# ----------------------------------------------------------------------------
+# algorithmic bytes
+# ----------------------------------------------------------------------------
+def sscan_bytes(batch, dim, L, N, groups, es=2):
+    E = batch * dim * L
+    bc = batch * groups * N * L * es
+    par = dim * N * 4 + 2 * dim * 4
+    fwd = 3 * E * es + 2 * bc + par + E * es + batch * dim * N * 4
+    bwd = 4 * E * es + 2 * bc + par + 3 * E * es + 2 * bc + dim * N * 4 + 2 * dim * 4
+    return fwd, bwd
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+# ----------------------------------------------------------------------------
+# clocks sampling (nvidia-smi during the timed region)
+# ----------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+            time.sleep(0.3)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# distributed helpers
+# ----------------------------------------------------------------------------
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo")
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------
+# workloads
+# ----------------------------------------------------------------------------
+def make_sscan_inputs(cfg, dev, seed, dtype=torch.bfloat16):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    b, dim, L, N = cfg["batch"], cfg["dim"], cfg["L"], cfg["N"]
+    import math
+    dt_min, dt_max = 1e-3, 1e-1
+    dtv = torch.exp(torch.rand(dim, generator=g) * (math.log(dt_max) - math.log(dt_min)) + math.log(dt_min))
+    dtv = dtv.clamp(min=1e-4)
+    inv_dt = dtv + torch.log(-torch.expm1(-dtv))  # mamba_simple.py:91-99 dt-bias init
+    host = dict(
+        u=torch.randn(b, dim, L, generator=g).to(dtype),
+        delta=(torch.randn(b, dim, L, generator=g) - 4.6).to(dtype),
+        A=-torch.arange(1, N + 1, dtype=torch.float32).repeat(dim, 1),
+        B=torch.randn(b, N, L, generator=g).to(dtype),
+        C=torch.randn(b, N, L, generator=g).to(dtype),
+        D=torch.rand(dim, generator=g),
+        z=torch.randn(b, dim, L, generator=g).to(dtype),
+        delta_bias=inv_dt.float(),
+        dout=torch.randn(b, dim, L, generator=g).to(dtype),
+    )
+    return host
+
+
+def time_sscan(cfg, dev, steps, warmup, world):
+    from kernels import _ak
+    host = make_sscan_inputs(cfg, dev, seed=1234 + (dist.get_rank() if world > 1 else 0))
+    d = {k: v.to(dev) for k, v in host.items()}
+    st = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        if ev:
+            ev[0].record(st)
+        out, last, states = _ak.selective_scan_fwd(d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"],
+                                                   d["delta_bias"], True)
+        if ev:
+            ev[1].record(st)
+        grads = _ak.selective_scan_bwd(d["dout"], d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"],
+                                       d["delta_bias"], True, states)
+        if ev:
+            ev[2].record(st)
+        return out, grads
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        start.record(st)
+        for i in range(steps):
+            step(evs[i])
+        end.record(st)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    total_ms = start.elapsed_time(end)
+    fwd_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    bwd_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    return total_ms, fwd_ms, bwd_ms, clk.summary(), host
+
+
+def time_sscan_e2e(cfg, dev, steps, warmup, host):
+    """Same step through the public API (selective_scan_fn + autograd) with inputs in pinned
+    host memory: every step copies its inputs H2D and reads a result back D2H."""
+    from kernels.mamba_scan import selective_scan_fn
+    pinned = {k: v.pin_memory() for k, v in host.items()}
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values())
+    res_host = torch.empty(cfg["batch"], cfg["dim"], cfg["N"], dtype=torch.float32).pin_memory()
+    st = torch.cuda.current_stream(dev)
+
+    def step():
+        d = {k: v.to(dev, non_blocking=True) for k, v in pinned.items()}
+        leaves = [d[k].requires_grad_(True) for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")]
+        out, last = selective_scan_fn(*leaves[:5], D=leaves[5], z=leaves[6], delta_bias=leaves[7],
+                                      delta_softplus=True, return_last_state=True)
+        out.backward(d["dout"])
+        res_host.copy_(last, non_blocking=True)
+        return res_host
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(st)
+    for _ in range(steps):
+        step()
+    e.record(st)
+    torch.cuda.synchronize(dev)
+    d2h = res_host.numel() * res_host.element_size()
+    return s.elapsed_time(e) / steps, h2d, d2h
+
+
+def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
+    """Oracle (the reference's selective_scan_ref restated, fp32 on the host cores) timed on a
+    bounded sample: batch 1, `dim_sample` channels, full L, fwd + autograd bwd."""
+    from oracle import hot_path_oracle as O
+    cfg = dict(batch=1, dim=dim_sample, L=L, N=N, groups=1)
+    host = make_sscan_inputs(cfg, None, seed=7, dtype=torch.float32)
+    t0 = time.perf_counter()
+    for _ in range(repeats):
+        O.selective_scan_grads(host["u"], host["delta"], host["A"], host["B"], host["C"], host["D"], host["z"],
+                               host["delta_bias"], True, host["dout"], dt=torch.float32)
+    dt = (time.perf_counter() - t0) / repeats
+    fwd, bwd = sscan_bytes(1, dim_sample, L, N, 1, es=2)
+    return {"value": round((fwd + bwd) / dt / 1e9, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"batch 1 x {dim_sample} channels x L={L} x N={N}, fp32 fwd+bwd (oracle restatement of "
+                      f"selective_scan_ref + autograd), {dt:.2f} s/step; GB/s counts the bf16 algorithmic bytes "
+                      f"of the same sample"}
+
+
+def time_other_ops(dev, steps, warmup, hbm_peak):
+    """Device-timed GB/s of the other swapped ops at their BASELINE configs."""
+    from kernels import _ak
+    res = {}
+    st = torch.cuda.current_stream(dev)
+
+    def timeit(fn, nbytes, name, reps):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        for _ in range(reps):
+            fn()
+        b.record(st)
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / reps
+        gbs = nbytes / ms / 1e6
+        res[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3)}
+
+    # RMSNorm fp32 [8192, 768] (config 0); rows > L2 is false here (25 MB), so a 256 MB
+    # scratch write flushes L2 between repetitions and is excluded by timing fwd/bwd separately.
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(8192, 768, generator=g).to(dev)
+    w = (1 + 0.02 * torch.randn(768, generator=g)).to(dev)
+    dy = torch.randn(8192, 768, generator=g).to(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    E = 8192 * 768
+    fw_b, bw_b = 2 * E * 4 + 768 * 4, 3 * E * 4 + 2 * 768 * 4
+
+    def rms_f():
+        flush.zero_()
+        _ak.rmsnorm_fwd(x, w, 1e-6)
+
+    def rms_b():
+        flush.zero_()
+        _ak.rmsnorm_bwd(x, w, dy, 1e-6)
+
+    def flush_only():
+        flush.zero_()
+
+    timeit(flush_only, 1, "_flush", steps * 4)
+    fl = res.pop("_flush")["ms"]
+    timeit(rms_f, fw_b, "rmsnorm_fwd_fp32_8192x768", steps * 4)
+    timeit(rms_b, bw_b, "rmsnorm_bwd_fp32_8192x768", steps * 4)
+    for k, nb in (("rmsnorm_fwd_fp32_8192x768", fw_b), ("rmsnorm_bwd_fp32_8192x768", bw_b)):
+        ms = max(res[k]["ms"] - fl, 1e-6)
+        gbs = nb / ms / 1e6
+        res[k] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
+                  "note": "L2 flushed (256 MB write) before each rep; flush time subtracted"}
+    del x, dy, flush
+
+    # Softmax causal scores bf16 [96*2048, 2048] (config 3): 805 MB per tensor > L2.
+    rows, cols = 96 * 2048, 2048
+    s = (torch.randn(rows, cols, device=dev) / 8).to(torch.bfloat16)
+    r = torch.arange(rows, device=dev) % cols
+    s.masked_fill_(torch.arange(cols, device=dev)[None, :] > r[:, None], float("-inf"))
+    dys = torch.randn(rows, cols, device=dev).to(torch.bfloat16)
+    y = _ak.softmax_fwd(s)
+    T = rows * cols * 2
+    timeit(lambda: _ak.softmax_fwd(s), 2 * T, "softmax_fwd_bf16_196608x2048", steps)
+    timeit(lambda: _ak.softmax_bwd(y, dys), 3 * T, "softmax_bwd_bf16_196608x2048", steps)
+    del s, dys, y
+
+    # Collapsed scan fp32 (8, 2048, 1536): 100 MB per tensor.
+    Bsz, L, d = 8, 2048, 1536
+    dA = torch.rand(Bsz, L, d, device=dev) * 0.5 + 0.5
+    dBx, C, xx, gy = (torch.randn(Bsz, L, d, device=dev) for _ in range(4))
+    Dv = torch.randn(d, device=dev)
+    E = Bsz * L * d
+    timeit(lambda: _ak.scan1_fwd(dA, dBx, C, Dv, xx), 20 * E, "scan1_fwd_fp32_8x2048x1536", steps)
+    timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy), 36 * E, "scan1_bwd_fp32_8x2048x1536", steps)
+    del dA, dBx, C, xx, gy
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_ours(args, world, rank, local):
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    hbm_peak, tf_peak, peak_kind = peaks()
+    cfg = HEADLINE
+    total_ms, fwd_ms, bwd_ms, clocks, host = time_sscan(cfg, dev, args.steps, args.warmup, world)
+    total_ms = max_over_ranks(total_ms, world, dev)
+    fwd_b, bwd_b = sscan_bytes(cfg["batch"], cfg["dim"], cfg["L"], cfg["N"], cfg["groups"])
+    ms_per_step = total_ms / args.steps
+    value = world * (fwd_b + bwd_b) / (ms_per_step / 1e3) / 1e9
+    bwd_avg = statistics.mean(bwd_ms)
+    fwd_avg = statistics.mean(fwd_ms)
+    achieved = bwd_b / (bwd_avg / 1e3) / 1e9
+    traffic = NCU_TRAFFIC_BYTES.get("sscan_bwd")
+    e2e_ms, h2d, d2h = time_sscan_e2e(cfg, dev, max(2, args.steps // 2), 2, host)
+    e2e_ms = max_over_ranks(e2e_ms, world, dev)
+    e2e_value = world * (fwd_b + bwd_b) / (e2e_ms / 1e3) / 1e9
+    ops = time_other_ops(dev, args.steps, args.warmup, hbm_peak) if (rank == 0 and not args.no_ops) else None
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE config 1 distributions)",
+        "config": {"workload": "mamba selective_scan fwd+bwd B=8 D=1536 L=2048 N=16 bf16, fp32 state, "
+                               "softplus(delta+bias), SiLU(z), last_state",
+                   "per_rank_batch": cfg["batch"], "global_batch": cfg["batch"] * world,
+                   "parallelism": f"rows sharded over {world} GPU(s), no data-path collective",
+                   "l2": "no flush: per-step working set 558 MB > 126 MB L2",
+                   "fwd_ms": round(fwd_avg, 4), "bwd_ms": round(bwd_avg, 4),
+                   "fwd_GBps": round(fwd_b / (fwd_avg / 1e3) / 1e9, 1),
+                   "sfu_exp2_per_pass": cfg["batch"] * cfg["dim"] * cfg["L"] * cfg["N"]},
+        "roofline": {"kernel": "selective_scan_bwd (C-ABI call)", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                     "traffic": traffic, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": bwd_b},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+                "api": "kernels.mamba_scan.selective_scan_fn + autograd backward, pinned host inputs"},
+        "gpu_launches": 5 * args.steps,
+        "clocks": clocks,
+    }
+    if ops is not None:
+        line["ops"] = ops
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_sscan_sample()
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU path (the oracle port of selective_scan_ref + autograd), timed on
+    the host cores on a bounded sample of the headline workload; rank 0 only."""
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_sscan_sample(dim_sample=8, L=512)
+    samples = [cpu_sscan_sample() for _ in range(args.steps)]
+    v = statistics.median(s["value"] for s in samples)
+    cb = dict(samples[0])
+    cb["value"] = v
+    fwd_b, bwd_b = sscan_bytes(1, 48, 2048, 16, 1)
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round((fwd_b + bwd_b) / (v * 1e9) * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded; BASELINE config 1 distributions)",
+            "config": {"workload": "mamba selective_scan fwd+bwd, bounded CPU sample of B=8 D=1536 L=2048 N=16"},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-op sweep")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = setup_dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,206 @@
+/*
+ * ak_b200.h — C ABI of libak_b200.so, the sm_100a (B200) kernels behind the
+ * autokernel drop-in Python API.
+ *
+ * Conventions shared by every entry point:
+ *   - `extern "C"`, no C++ exceptions cross the boundary.
+ *   - Return AK_OK (0) on success, a nonzero ak_status otherwise; the reason
+ *     is available from ak_last_error() on the calling thread.
+ *   - All tensor arguments are raw device pointers to caller-owned, densely
+ *     packed row-major buffers (the Python layer allocates outputs and
+ *     workspaces with PyTorch).  Nothing here allocates device memory.
+ *   - `stream` is a cudaStream_t passed as void*; every call is asynchronous
+ *     on that stream (NULL = legacy default stream).
+ *   - Element types are given by ak_dtype codes.
+ *   - Functions keep no mutable global state beyond a per-device attribute
+ *     cache, so they are reentrant and thread-safe.
+ *
+ * Each declaration names the reference interface it replaces, as a path inside
+ * the joelhenwang/autokernel-halo-strix project.
+ */
+#ifndef AK_B200_H
+#define AK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AK_API __attribute__((visibility("default")))
+#else
+#define AK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum { AK_F32 = 0, AK_BF16 = 1, AK_F16 = 2 } ak_dtype;
+
+typedef enum {
+  AK_OK = 0,
+  AK_ERR_ARG = 1,       /* invalid pointer / size / alignment */
+  AK_ERR_DTYPE = 2,     /* unsupported dtype combination */
+  AK_ERR_SHAPE = 3,     /* unsupported shape */
+  AK_ERR_LAUNCH = 4,    /* CUDA launch or runtime error */
+  AK_ERR_TIMEOUT = 5,   /* a bounded device-side wait gave up */
+  AK_ERR_WORKSPACE = 6  /* workspace smaller than the *_workspace_size query */
+} ak_status;
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+AK_API int ak_version(void);
+/* Message for the last failing call on this thread ("" if none). */
+AK_API const char* ak_last_error(void);
+
+/* ------------------------------------------------------------------------ *
+ * RMSNorm
+ * ------------------------------------------------------------------------ */
+
+/* y[M,N] = x * rsqrt(mean(x^2, -1) + eps) * w.   x, y: dt_x; w: dt_w.
+ * rstd (nullable, fp32 [M]) receives rsqrt(mean(x^2)+eps).
+ * Replaces rmsnorm_hip / kernel_fn (kernels/hip/rmsnorm.py:119-177) and the
+ * torch.ops.autokernel.rmsnorm forward (kernels/hip/_torch_ops.py:56-59). */
+AK_API int ak_rmsnorm_fwd(void* y, float* rstd, const void* x, const void* w,
+                   int64_t M, int64_t N, float eps, int dt_x, int dt_w,
+                   void* stream);
+
+/* Workspace bytes needed by ak_rmsnorm_bwd for an [M, N] problem. */
+AK_API int ak_rmsnorm_bwd_workspace_size(int64_t M, int64_t N, size_t* bytes);
+
+/* dx[M,N] (dt_x) and dw[N] (dt_dw) of the RMSNorm above, given dy (dt_x).
+ * dw is a deterministic column reduction (no atomics).
+ * Replaces rmsnorm_backward_hip / kernel_fn (kernels/hip/rmsnorm_backward.py:191-281)
+ * and _rmsnorm_backward (kernels/hip/_torch_ops.py:73-97). */
+AK_API int ak_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspace, size_t ws_bytes,
+                   const void* dy, const void* x, const void* w,
+                   int64_t M, int64_t N, float eps, int dt_x, int dt_w,
+                   void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Row softmax over the last dimension
+ * ------------------------------------------------------------------------ */
+
+/* y[rows,cols] = softmax(x) along cols.  fp32 accumulation.
+ * Replaces softmax_hip / kernel_fn (kernels/hip/softmax.py:273-360). */
+AK_API int ak_softmax_fwd(void* y, const void* x, int64_t rows, int64_t cols, int dt,
+                   void* stream);
+
+/* dx = y * (dy - sum(dy * y)).  The reference has no backward kernel; this is
+ * the autograd of reference.softmax_ref (reference.py:15-17). */
+AK_API int ak_softmax_bwd(void* dx, const void* y, const void* dy, int64_t rows,
+                   int64_t cols, int dt, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Cross-entropy over logit rows
+ * ------------------------------------------------------------------------ */
+
+/* Per-row online-softmax cross entropy on logits[B, V] (dt), targets int64[B].
+ * Outputs (fp32 [B]): losses, lse; row_max/row_sum nullable.
+ * If grad != NULL, writes grad[B, V] (dt) =
+ *   (softmax - (1-a)*onehot - a/V) * softcap' * scale,
+ * where scale = scale_grad * (scale_dev ? *scale_dev : 1).
+ * Ignored rows (target == ignore_index) get loss 0 and a zero grad row.
+ * Replaces cross_entropy_fwd_hip (kernels/ce_fused.py:122-382). */
+AK_API int ak_ce_rows_fwd(float* losses, float* lse, float* row_max, float* row_sum,
+                   void* grad, const void* logits, const int64_t* targets,
+                   int64_t B, int64_t V, float softcap, int64_t ignore_index,
+                   float label_smoothing, float scale_grad,
+                   const float* scale_dev, int dt, void* stream);
+
+/* grad[B,V] from saved row_max/row_sum (tiny mode), optionally adding the
+ * z-loss term z_coef * lse * softmax (z_coef = 0 disables it).
+ * Replaces cross_entropy_bwd_tiny_hip (kernels/ce_fused.py:405-522) and the
+ * z-loss branch of _CrossEntropyHIP.backward (kernels/ce_fused.py:672-689). */
+AK_API int ak_ce_rows_bwd(void* grad, const void* logits, const int64_t* targets,
+                   const float* row_max, const float* row_sum, int64_t B,
+                   int64_t V, float softcap, int64_t ignore_index,
+                   float label_smoothing, float scale, const float* scale_dev,
+                   float z_coef, int dt, void* stream);
+
+/* loss_out[0] = sum(losses * valid) / max(1, n_valid) (+ z_w * sum(lse^2*valid)/n)
+ * computed on device; n_valid_out (nullable) receives max(1, n_valid).
+ * Replaces the host-side reductions of _CrossEntropyHIP.forward
+ * (kernels/ce_fused.py:593-629). */
+AK_API int ak_ce_rows_reduce(float* loss_out, float* n_valid_out, const float* losses,
+                      const float* lse, const int64_t* targets, int64_t B,
+                      int64_t ignore_index, float z_loss_weight, void* stream);
+
+/* inv_out[0] = 1 / max(1, count(targets != ignore_index)).  Device-side
+ * replacement of the `.item()` sync in _ChunkedLinearCrossEntropy.forward
+ * (kernels/hip/chunked_linear_cross_entropy.py:71-74). */
+AK_API int ak_ce_inv_valid(float* inv_out, const int64_t* targets, int64_t B,
+                    int64_t ignore_index, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Collapsed (single-state) selective scan, fp32, layout (B, L, d)
+ * ------------------------------------------------------------------------ */
+
+/* h_t = dA_t*h_{t-1} + dBx_t;  y_t = C_t*h_t + D*x_t   (h_{-1} = 0).
+ * Replaces selective_scan_hip / kernel_fn (kernels/hip/selective_scan.py:165-241)
+ * and torch.ops.autokernel.selective_scan (kernels/hip/_torch_ops.py:312-318). */
+AK_API int ak_scan1_fwd(float* y, const float* dA, const float* dBx, const float* C,
+                 const float* D, const float* x, int64_t B, int64_t L, int64_t d,
+                 void* stream);
+
+AK_API int ak_scan1_bwd_workspace_size(int64_t B, int64_t L, int64_t d, size_t* bytes);
+
+/* Gradients of ak_scan1_fwd given gy.  gD is reduced deterministically.
+ * Replaces selective_scan_backward_hip / kernel_fn
+ * (kernels/hip/selective_scan_backward.py:314-421) and _selective_scan_backward
+ * (kernels/hip/_torch_ops.py:335-389). */
+AK_API int ak_scan1_bwd(float* gdA, float* gdBx, float* gC, float* gD, float* gx,
+                 void* workspace, size_t ws_bytes, const float* dA,
+                 const float* dBx, const float* C, const float* D, const float* x,
+                 const float* gy, int64_t B, int64_t L, int64_t d, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Mamba-style selective scan, layout (batch, dim, L), N states per channel
+ * ------------------------------------------------------------------------ */
+
+/* Timesteps between two saved states in `chunk_states`.  The forward saves the
+ * state after every `ak_selective_scan_state_stride()` steps (and after the
+ * last step): n_saved = ceil(L / stride). */
+AK_API int ak_selective_scan_state_stride(void);
+
+/* delta' = softplus?(delta + delta_bias);  per state n:
+ *   h_t[n] = exp(delta'_t * A[d,n]) h_{t-1}[n] + delta'_t * B[b,g,n,t] * u_t
+ *   y_t = sum_n C[b,g,n,t] h_t[n] + D[d] u_t;  out = y * silu(z)  (if z)
+ * u, delta, z, out: (batch, dim, L) dt; A: fp32 (dim, dstate);
+ * B, C: (batch, groups, dstate, L) dt, g = d / (dim / groups);
+ * D, delta_bias: fp32 (dim) nullable; last_state: fp32 (batch, dim, dstate)
+ * nullable; chunk_states: fp32 (batch, dim, n_saved, dstate) nullable
+ * (required for the backward).
+ * Replaces selective_scan_cuda.fwd as called by SelectiveScanFn.forward
+ * (external/mamba/mamba_ssm/ops/selective_scan_interface.py:23-53), with the
+ * semantics of selective_scan_ref (same file, lines 115-181). */
+AK_API int ak_selective_scan_fwd(void* out, float* last_state, float* chunk_states,
+                          const void* u, const void* delta, const float* A,
+                          const void* Bm, const void* Cm, const float* D,
+                          const void* z, const float* delta_bias,
+                          int delta_softplus, int64_t batch, int64_t dim,
+                          int64_t seqlen, int64_t dstate, int64_t groups, int dt,
+                          void* stream);
+
+AK_API int ak_selective_scan_bwd_workspace_size(int64_t batch, int64_t dim,
+                                         int64_t seqlen, int64_t dstate,
+                                         int64_t groups, size_t* bytes);
+
+/* Gradients of ak_selective_scan_fwd w.r.t. u, delta, A, B, C, D, z,
+ * delta_bias (dD, dz, ddelta_bias nullable when the input was absent).
+ * du, ddelta, dB, dC, dz: dt; dA, dD, ddelta_bias: fp32.
+ * Replaces selective_scan_cuda.bwd as called by SelectiveScanFn.backward
+ * (external/mamba/mamba_ssm/ops/selective_scan_interface.py:56-83). */
+AK_API int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB, void* dC,
+                          float* dD, void* dz, float* ddelta_bias,
+                          void* workspace, size_t ws_bytes, const void* dout,
+                          const void* u, const void* delta, const float* A,
+                          const void* Bm, const void* Cm, const float* D,
+                          const void* z, const float* delta_bias,
+                          const float* chunk_states, int delta_softplus,
+                          int64_t batch, int64_t dim, int64_t seqlen,
+                          int64_t dstate, int64_t groups, int dt, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AK_B200_H */

@@ -1,0 +1,91 @@
+"""Cross-entropy CUDA kernels (rows + chunked linear) vs the oracle and golden fixtures."""
+import pytest
+import torch
+
+from conftest import assert_fp32_close, assert_lowp_close, golden
+from oracle import hot_path_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+CASES = [("plain", {}), ("softcap", dict(softcap=5.0)), ("ls", dict(label_smoothing=0.1)),
+         ("zloss", dict(z_loss_weight=1e-2)), ("all", dict(softcap=7.0, label_smoothing=0.05, z_loss_weight=1e-3))]
+
+
+@pytest.mark.parametrize("mode", ["fused", "tiny"])
+@pytest.mark.parametrize("case,kw", CASES)
+def test_ce_full_golden_cuda(case, kw, mode):
+    from kernels import ce_fused
+    g = golden("ce")
+    x = torch.from_numpy(g["logits"]).to(DEV).requires_grad_(True)
+    t = torch.from_numpy(g["targets"]).to(DEV)
+    loss = ce_fused.ce_full(x, t, mode=mode, **kw)
+    ref = float(g[f"{case}_loss"])
+    assert abs(loss.item() - ref) <= 1e-5 * max(1.0, abs(ref))
+    loss.backward()
+    assert_fp32_close(x.grad, g[f"{case}_grad"], what="grad")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,V", [(64, 32768), (7, 50257), (3, 1000), (5, 7)])
+def test_ce_rows_kernel(dtype, B, V):
+    from kernels import ce_fused
+    g = torch.Generator().manual_seed(B + V)
+    x = (torch.randn(B, V, generator=g) * 2).to(dtype)
+    t = torch.randint(0, V, (B,), generator=g)
+    t[0] = -100
+    mod = ce_fused._get_fwd_module()
+    losses, lse, rmax, rsum, grad = mod.cross_entropy_fwd_hip(x.to(DEV), t.to(DEV), 0.0, -100, 0.0, 1, 1, 0.5)
+    rl, rlse, rg = O.ce_rows(x, t, scale=0.5)
+    assert_fp32_close(losses, rl, rtol=1e-5 if dtype == torch.float32 else 1e-3, what="losses")
+    assert_fp32_close(lse, rlse, rtol=1e-5 if dtype == torch.float32 else 1e-3, what="lse")
+    (assert_fp32_close if dtype == torch.float32 else assert_lowp_close)(grad, rg, what="grad")
+    g2 = ce_fused._get_bwd_module().cross_entropy_bwd_tiny_hip(x.to(DEV), t.to(DEV), rmax, rsum, 0.0, -100, 0.0, 0.5)
+    (assert_fp32_close if dtype == torch.float32 else assert_lowp_close)(g2, rg, what="tiny grad")
+
+
+def test_kernel_fn_and_facade():
+    import kernel
+    x = torch.randn(32, 4096, device=DEV, dtype=torch.bfloat16)
+    t = torch.randint(0, 4096, (32,), device=DEV)
+    ref = torch.nn.functional.cross_entropy(x.double().cpu(), t.cpu())
+    assert abs(kernel.kernel_fn(x, t).item() - ref.item()) < 1e-3
+
+
+def test_ce_all_ignored_gives_zero():
+    from kernels import ce_fused
+    x = torch.randn(4, 100, device=DEV, requires_grad=True)
+    t = torch.full((4,), -100, device=DEV)
+    loss = ce_fused.ce_full(x, t)
+    loss.backward()
+    assert loss.item() == 0.0 and torch.all(x.grad == 0)
+
+
+def test_chunked_linear_ce_golden_cuda():
+    from kernels.hip.chunked_linear_cross_entropy import ChunkedLinearCrossEntropyLoss
+    g = golden("linear_ce")
+    H = torch.from_numpy(g["H"]).to(DEV).requires_grad_(True)
+    W = torch.from_numpy(g["W"]).to(DEV).requires_grad_(True)
+    lab = torch.from_numpy(g["labels"]).to(DEV)
+    loss = ChunkedLinearCrossEntropyLoss(chunk_size=40)(H, W, lab)
+    assert abs(loss.item() - float(g["loss"])) < 1e-4
+    loss.backward()
+    assert_fp32_close(H.grad, g["dH"], rtol=1e-4, what="dH")
+    assert_fp32_close(W.grad, g["dW"], rtol=1e-4, what="dW")
+
+
+@pytest.mark.parametrize("N,D,V", [(1024, 256, 32768), (300, 64, 1000)])
+def test_chunked_linear_ce_bf16(N, D, V):
+    from kernels.hip.chunked_linear_cross_entropy import ChunkedLinearCrossEntropyLoss
+    g = torch.Generator().manual_seed(N)
+    H = torch.randn(N, D, generator=g).to(torch.bfloat16)
+    W = (torch.randn(V, D, generator=g) * 0.02).to(torch.bfloat16)
+    lab = torch.randint(0, V, (N,), generator=g)
+    lab[::20] = -100
+    Hc, Wc = H.to(DEV).requires_grad_(True), W.to(DEV).requires_grad_(True)
+    loss = ChunkedLinearCrossEntropyLoss(chunk_size=256)(Hc, Wc, lab.to(DEV))
+    rl, rdh, rdw = O.linear_ce(H, W, lab)
+    assert abs(loss.item() - rl.item()) < 2e-2
+    loss.backward()
+    assert_lowp_close(Hc.grad, rdh, what="dH")
+    assert_lowp_close(Wc.grad, rdw, what="dW")

@@ -1,0 +1,85 @@
+"""autokernel.optimize / report / restore / list_patterns on CPU (no kernel calls)."""
+import torch
+import torch.nn as nn
+
+import autokernel
+from autokernel._patterns import RMSNormPattern, _RMSNormReplacement
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, d, eps=1e-5):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+        self.eps = eps
+
+    def forward(self, x):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
+
+
+class Block(nn.Module):
+    def __init__(self, d=16):
+        super().__init__()
+        self.attention_norm = RMSNorm(d)
+        self.proj = nn.Linear(d, d)
+        self.ffn_norm = nn.RMSNorm(d, eps=1e-6)
+        self.ln = nn.LayerNorm(d)
+
+
+def test_list_patterns():
+    assert autokernel.list_patterns() == ["rmsnorm"]
+
+
+def test_optimize_replaces_rmsnorms_and_keeps_parameters(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    m = nn.Sequential(Block(), Block())
+    w0 = m[0].attention_norm.weight
+    autokernel.optimize(m, training=True)
+    assert isinstance(m[0].attention_norm, _RMSNormReplacement)
+    assert isinstance(m[1].ffn_norm, _RMSNormReplacement)
+    assert isinstance(m[0].ln, nn.LayerNorm)
+    assert m[0].attention_norm.weight is w0  # same Parameter: optimizer/state-dict stay valid
+    assert m[0].attention_norm.eps == 1e-5 and m[0].ffn_norm.eps == 1e-6
+    assert "0.attention_norm.weight" in m.state_dict()
+    rep = autokernel.report(m)
+    assert rep["status"] == "optimized" and rep["patterns"]["rmsnorm"]["modules_replaced"] == 4
+    assert rep["patterns"]["rmsnorm"]["op_speedup"] == "3.3x"
+    autokernel.restore(m)
+    assert isinstance(m[0].attention_norm, RMSNorm)
+    assert autokernel.report(m) == {"status": "not optimized", "patterns": {}}
+
+
+def test_include_exclude(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    m = Block()
+    autokernel.optimize(m, training=True, exclude=["rmsnorm"])
+    assert isinstance(m.attention_norm, RMSNorm)
+    m2 = Block()
+    autokernel.optimize(m2, training=True, include=["rmsnorm"])
+    assert isinstance(m2.attention_norm, _RMSNormReplacement)
+
+
+def test_inference_mode_casts_dtype(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    m = Block()
+    autokernel.optimize(m, dtype=torch.bfloat16)
+    assert m.proj.weight.dtype == torch.bfloat16 and not m.training
+
+
+def test_replacement_refuses_cpu(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    m = Block()
+    autokernel.optimize(m, training=True)
+    try:
+        m.attention_norm(torch.zeros(2, 16))
+    except RuntimeError as e:
+        assert "CUDA" in str(e)
+    else:
+        raise AssertionError("expected a loud failure on CPU")
+
+
+def test_pattern_matching_rules():
+    p = RMSNormPattern()
+    assert p.matches("n", RMSNorm(4), None)
+    assert p.matches("n", nn.RMSNorm(4), None)
+    assert not p.matches("n", nn.LayerNorm(4), None)
+    assert not p.matches("n", nn.Linear(4, 4), None)
