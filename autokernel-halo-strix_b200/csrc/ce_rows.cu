@@ -177,8 +177,9 @@ ce_rows_bwd_kernel(T* __restrict__ grad, const T* __restrict__ logits, const int
           float g = pr;
           if ((int64_t)v * VEC + k == tgt) g -= p.target_coeff;
           g -= p.ls_uniform;
+          g = g * scale + zc * lse * pr;  // z-loss term also flows through the softcap
           if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
-          o[k] = g * scale + zc * lse * pr;
+          o[k] = g;
         }
       }
       store_frag<T, VEC>(grow + (int64_t)v * VEC, o);
@@ -191,8 +192,8 @@ ce_rows_bwd_kernel(T* __restrict__ grad, const T* __restrict__ logits, const int
         g = pr;
         if (i == tgt) g -= p.target_coeff;
         g -= p.ls_uniform;
-        if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
         g = g * scale + zc * lse * pr;
+        if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
       }
       grow[i] = from_f<T>(g);
     }

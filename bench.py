@@ -343,6 +343,36 @@ def time_other_ops(dev, steps, warmup, hbm_peak):
     return res
 
 
+def time_train(dev, steps, warmup, world, rank, micro_batch=16, seq=1024):
+    """124M hybrid training step: kernels swapped in through the
+    reference-facing API, bf16 autocast, AdamW, DDP over NCCL when world > 1."""
+    from halo_training.hybrid_lm import HybridConfig, count_params
+    from halo_training.train_step import HybridTrainer, synthetic_batch
+    cfg = HybridConfig()
+    tr = HybridTrainer(cfg, device=dev, use_kernels=True, ddp=world > 1, seed=0)
+    idx, tgt = synthetic_batch(micro_batch, seq, cfg.vocab_size, seed=1000 + rank, device=dev)
+    st = torch.cuda.current_stream(dev)
+    for _ in range(warmup):
+        tr.step(idx, tgt)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(steps):
+        loss = tr.step(idx, tgt)
+    b.record(st)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(a.elapsed_time(b) / steps, world, dev)
+    out = {"tok_s": round(world * micro_batch * seq / (ms / 1e3), 1), "ms_per_step": round(ms, 3),
+           "params": count_params(tr.raw), "micro_batch_per_gpu": micro_batch, "seq_len": seq,
+           "loss_last": round(float(loss.item()), 4), "steps": steps,
+           "model": "hybrid 12L d768 (6 Mamba N16 + 6 GQA 12q/4kv), SwiGLU 2048, tied 50304 vocab",
+           "parallelism": f"ddp{world} (NCCL)" if world > 1 else "single GPU"}
+    del tr
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -361,6 +391,7 @@ def run_ours(args, world, rank, local):
     e2e_ms = max_over_ranks(e2e_ms, world, dev)
     e2e_value = world * (fwd_b + bwd_b) / (e2e_ms / 1e3) / 1e9
     ops = time_other_ops(dev, args.steps, args.warmup, hbm_peak) if (rank == 0 and not args.no_ops) else None
+    train = None if args.no_train else time_train(dev, args.train_steps, 3, world, rank)
     if rank != 0:
         return
     line = {
@@ -396,6 +427,8 @@ def run_ours(args, world, rank, local):
     }
     if ops is not None:
         line["ops"] = ops
+    if train is not None:
+        line["train"] = train
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_sscan_sample()
     print(json.dumps(line), flush=True)
@@ -432,6 +465,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-train", action="store_true", help="skip the 124M hybrid training step")
+    ap.add_argument("--train-steps", type=int, default=10)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
