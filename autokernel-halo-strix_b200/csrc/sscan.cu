@@ -9,26 +9,32 @@
 // Layout: u, delta, z, out (batch, dim, L) with L contiguous; B, C
 // (batch, groups, N, L); A (dim, N) fp32; state fp32.
 //
-// Forward design.  A CTA owns `cpc` channels of one batch row (all in one
-// B/C group) and walks L in chunks of 32 lanes x ITEMS steps.  The chunk's
-// B and C tiles (N x chunk, shared by every channel of the CTA) are staged
-// into shared memory by the bulk-copy (TMA) engine into a double buffer
-// completed on mbarriers, so HBM/L2 traffic for B/C is paid once per CTA.
-// Each warp scans one channel at a time: per state n every lane runs its
-// ITEMS steps sequentially in registers (one SFU exp2 per step), the 32 lane
-// aggregates are combined with a 5-step shuffle scan, and the chunk carry
-// (one fp32 per channel and state) lives in shared memory.  The state after
-// every kStateStride steps is saved for the backward.
+// Work decomposition.  A CTA owns `cpc` channels of one batch row (all in one
+// B/C group) and walks L in chunks of 32 lanes x ITEMS steps: lane l owns the
+// ITEMS consecutive steps starting at l*ITEMS.  The chunk's B and C tiles
+// (N x chunk, shared by every channel of the CTA) arrive by bulk async copy
+// (TMA engine, mbarrier-completed) as 16-bit values into a staging buffer and
+// are converted once per CTA into an fp32 tile laid out [n][quad][lane][4], so
+// each lane reads its 4-step quads with conflict-free 16-byte shared loads.
+// The staging buffer is refilled with the next chunk as soon as it has been
+// converted, so the copy overlaps the whole chunk's compute.  Each warp scans
+// one channel at a time: per state every lane runs its ITEMS steps
+// sequentially in registers (one SFU exp2 per step; the lane's decay product
+// is one exp2 of the summed delta), the 32 lane aggregates are combined by a
+// 5-round shuffle scan, and the chunk carry (one fp32 per channel and state)
+// lives in shared memory.  Two states are processed together so their
+// independent dependency chains interleave.  The state after every
+// kStateStride steps is saved for the backward.
 //
-// Backward design.  Same CTA/chunk structure, chunks visited in reverse.
-// Per chunk and state the forward states are recomputed from the saved
-// chunk-start state (no full state tensor in HBM), then the adjoint
+// Backward.  Same decomposition, chunks visited in reverse.  Per chunk and
+// state the forward states are recomputed from the saved chunk-start state
+// (no full state tensor in HBM), then the adjoint
 // g_t = dy_t C_t + a_{t+1} g_{t+1} is scanned right-to-left with the same
-// two-level (lane-sequential + shuffle) scheme; the adjoint carry crosses
-// chunks pre-multiplied by a at the chunk's first step.  dB/dC (sums over the
-// channels of a group) are reduced in shared memory across the CTA's channels
-// and flushed once per chunk with fp32 global reductions; dA/dD/dbias are
-// per-(batch, channel) partials reduced in a fixed order by a second kernel.
+// two-level scheme; the adjoint carry crosses chunks pre-multiplied by a at
+// the chunk's first step.  dB/dC (sums over the channels of a group) are
+// reduced in shared memory across the CTA's channels and flushed once per
+// chunk with vectorised fp32 global reductions; dA/dD/dbias are per-(batch,
+// channel) partials reduced in a fixed order by a second kernel.
 #include "ak_common.cuh"
 
 #include <algorithm>
@@ -37,10 +43,8 @@ namespace ak {
 namespace {
 
 constexpr int kStateStride = 256;  // timesteps between saved states
-constexpr int kItemsF = 16;        // forward steps per lane (chunk 512)
-constexpr int kItemsB = 8;         // backward steps per lane (chunk 256 == stride)
-static_assert(32 * kItemsB == kStateStride, "backward chunk must equal the state stride");
-static_assert((32 * kItemsF) % kStateStride == 0, "forward chunk must be a multiple of the stride");
+constexpr int kItems = 8;          // steps per lane: chunk = 256 steps = kStateStride
+static_assert(32 * kItems == kStateStride, "chunk must equal the state stride");
 
 __device__ int g_sscan_err;  // AK_ERR_TIMEOUT if a bounded wait gave up
 
@@ -65,7 +69,7 @@ struct SsParams {
   float* dB_acc;
   float* dC_acc;
   float* part;  // [batch][dim][N+2]
-  int batch, dim, L, N, groups, dpg, nw, cpw, nsaved, nbuf;
+  int batch, dim, L, N, groups, dpg, nw, cpw, nsaved;
   int softplus, bulk, vec_io;
 };
 
@@ -108,36 +112,37 @@ __device__ __forceinline__ void store_items(T* row, const float (&v)[ITEMS], int
   }
 }
 
-// ITEMS consecutive elements of a shared-memory tile row (16-byte aligned).
-template <typename T, int ITEMS>
-__device__ __forceinline__ void load_smem_items(float (&v)[ITEMS], const T* p) {
-  constexpr int VEC = 16 / sizeof(T);
+// fp32 tile row [quad][lane][4]: the lane's ITEMS values, 4 per 16-byte load.
+template <int ITEMS>
+__device__ __forceinline__ void load_tile(float (&v)[ITEMS], const float* row, int lane) {
+  const float4* r4 = reinterpret_cast<const float4*>(row) + lane;
 #pragma unroll
-  for (int i = 0; i < ITEMS; i += VEC) {
-    float f[VEC];
-    load_frag<T, VEC>(f, p + i);
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) v[i + k] = f[k];
+  for (int q = 0; q < ITEMS / 4; ++q) {
+    const float4 f = r4[q * 32];
+    v[4 * q + 0] = f.x;
+    v[4 * q + 1] = f.y;
+    v[4 * q + 2] = f.z;
+    v[4 * q + 3] = f.w;
   }
 }
 
-// Stage the B and C tiles [N][CH] of chunk starting at t0 into buffer `buf`.
-// Bulk path: one thread issues 2N row copies completing on bars[buf].
-// Cooperative path (unaligned L): all threads copy; caller syncs.
+// Issue (one thread, bulk path) or perform (all threads, unaligned rows) the
+// copy of the B and C tiles [N][CH] of the chunk starting at t0 into the
+// staging buffer ([2][N][CH] of T).
 template <typename T, int CH>
-__device__ __forceinline__ void stage_bc(const SsParams& p, T* Bs, T* Cs, uint64_t* bars, int buf, int t0,
-                                         const T* Bg, const T* Cg, bool bulk_issue) {
+__device__ __forceinline__ void stage_bc(const SsParams& p, T* stage, uint64_t* bar, int t0, const T* Bg,
+                                         const T* Cg, bool bulk_issue) {
   const int N = p.N, L = p.L;
   const int len = min(CH, L - t0);
-  T* bdst = Bs + (size_t)buf * N * CH;
-  T* cdst = Cs + (size_t)buf * N * CH;
+  T* bdst = stage;
+  T* cdst = stage + (size_t)N * CH;
   if (p.bulk) {
     if (bulk_issue) {
       const uint32_t bytes = (uint32_t)(len * sizeof(T));
-      mbar_arrive_expect_tx(&bars[buf], 2u * N * bytes);
+      mbar_arrive_expect_tx(bar, 2u * N * bytes);
       for (int n = 0; n < N; ++n) {
-        bulk_g2s(bdst + n * CH, Bg + (int64_t)n * L + t0, bytes, &bars[buf]);
-        bulk_g2s(cdst + n * CH, Cg + (int64_t)n * L + t0, bytes, &bars[buf]);
+        bulk_g2s(bdst + n * CH, Bg + (int64_t)n * L + t0, bytes, bar);
+        bulk_g2s(cdst + n * CH, Cg + (int64_t)n * L + t0, bytes, bar);
       }
     }
   } else {
@@ -150,19 +155,138 @@ __device__ __forceinline__ void stage_bc(const SsParams& p, T* Bs, T* Cs, uint64
   }
 }
 
+// Convert the staging buffer into the fp32 tiles [2][N][CH] laid out
+// [n][quad][lane][4]; steps beyond the sequence end become 0.
+template <typename T, int ITEMS>
+__device__ __forceinline__ void convert_bc(int N, const T* src, float* tile, int len) {
+  constexpr int CH = 32 * ITEMS;
+  const int nquads = 2 * N * CH / 4;
+  for (int qi = threadIdx.x; qi < nquads; qi += blockDim.x) {
+    const int e = qi * 4;  // element index in [which][n][t]
+    const int row = e / CH, t = e - row * CH;
+    const int lane = t / ITEMS, i = t - lane * ITEMS;
+    float4 f;
+    f.x = t + 0 < len ? to_f<T>(src[e + 0]) : 0.f;
+    f.y = t + 1 < len ? to_f<T>(src[e + 1]) : 0.f;
+    f.z = t + 2 < len ? to_f<T>(src[e + 2]) : 0.f;
+    f.w = t + 3 < len ? to_f<T>(src[e + 3]) : 0.f;
+    reinterpret_cast<float4*>(tile + (size_t)row * CH)[(i / 4) * 32 + lane] = f;
+  }
+}
+
+// Wait for the chunk's tiles, convert them, and (bulk path) refill the staging
+// buffer with chunk `next_t0` (< 0: none).  `phase` counts completed copies.
+template <typename T, int ITEMS>
+__device__ __forceinline__ void fetch_chunk(const SsParams& p, T* stage, float* tile, uint64_t* bar, int phase,
+                                            int t0, int next_t0, const T* Bg, const T* Cg) {
+  constexpr int CH = 32 * ITEMS;
+  if (p.bulk) {
+    mbar_wait_bounded(bar, (uint32_t)(phase & 1), &g_sscan_err);
+  } else {
+    stage_bc<T, CH>(p, stage, bar, t0, Bg, Cg, false);
+    __syncthreads();
+  }
+  convert_bc<T, ITEMS>(p.N, stage, tile, min(CH, p.L - t0));
+  __syncthreads();  // tile ready; staging buffer free again
+  if (p.bulk && threadIdx.x == 0 && next_t0 >= 0) stage_bc<T, CH>(p, stage, bar, next_t0, Bg, Cg, true);
+}
+
+// Inclusive scan over lanes of g -> Q g + G (right to left).
+__device__ __forceinline__ void scan_down(float& Q, float& G, int lane) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float Qn = __shfl_down_sync(0xffffffffu, Q, off);
+    const float Gn = __shfl_down_sync(0xffffffffu, G, off);
+    if (lane + off < 32) {
+      G = fmaf(Q, Gn, G);
+      Q *= Qn;
+    }
+  }
+}
+
+// Shared memory: [0,128) mbarrier | staging 2*N*CH*sizeof(T) | fp32 tile 2*N*CH*4 | kernel arrays.
+template <typename T, int CH>
+__host__ __device__ inline size_t stage_bytes(int N) { return (size_t)2 * N * CH * sizeof(T); }
+
 // ============================================================================
 // Forward
 // ============================================================================
-template <typename T, int ITEMS>
-__global__ void __launch_bounds__(256)
+
+// K states n0..n0+K-1 of one channel over one chunk: per lane a sequential pass
+// over its ITEMS steps, a shuffle scan of the lane aggregates, the carry-in
+// fix-up pass accumulating y, and the new carry.  K > 1 interleaves the K
+// independent dependency chains.
+template <int ITEMS, int K>
+__device__ __forceinline__ void fwd_states(int n0, int N, const float (&dlt)[ITEMS], const float (&du)[ITEMS],
+                                           float (&y)[ITEMS], float S, const float* Arow, const float* tile, int lane,
+                                           float* carry_row, float* save) {
+  constexpr int CH = 32 * ITEMS;
+  float a[K][ITEMS], h[K][ITEMS], P[K], H[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float A2 = Arow[n0 + k] * kLog2e;
+    float Bv[ITEMS];
+    load_tile<ITEMS>(Bv, tile + (n0 + k) * CH, lane);
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+      a[k][i] = ex2(dlt[i] * A2);
+      h[k][i] = du[i] * Bv[i];
+    }
+    P[k] = ex2(S * A2);  // = prod of the lane's a
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    H[k] = h[k][0];
+#pragma unroll
+    for (int i = 1; i < ITEMS; ++i) H[k] = fmaf(a[k][i], H[k], h[k][i]);  // lane aggregate from a zero state
+  }
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    float Pp[K], Hp[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      Pp[k] = __shfl_up_sync(0xffffffffu, P[k], off);
+      Hp[k] = __shfl_up_sync(0xffffffffu, H[k], off);
+    }
+    if (lane >= off) {
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        H[k] = fmaf(P[k], Hp[k], H[k]);
+        P[k] *= Pp[k];
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const float carry = carry_row[n0 + k];
+    float Pe = __shfl_up_sync(0xffffffffu, P[k], 1);
+    float He = __shfl_up_sync(0xffffffffu, H[k], 1);
+    if (lane == 0) { Pe = 1.f; He = 0.f; }
+    const float newc = __shfl_sync(0xffffffffu, fmaf(P[k], carry, H[k]), 31);
+    float hh = fmaf(Pe, carry, He);
+    float Cv[ITEMS];
+    load_tile<ITEMS>(Cv, tile + (N + n0 + k) * CH, lane);
+#pragma unroll
+    for (int i = 0; i < ITEMS; ++i) {
+      hh = fmaf(a[k][i], hh, h[k][i]);
+      y[i] = fmaf(Cv[i], hh, y[i]);
+    }
+    if (save != nullptr) save[n0 + k] = hh;
+    if (lane == 0) carry_row[n0 + k] = newc;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256, 3)  // 3 CTAs (24 warps) per SM
 sscan_fwd_kernel(SsParams p) {
+  constexpr int ITEMS = kItems;
   constexpr int CH = 32 * ITEMS;
   extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
   const int N = p.N, L = p.L;
-  T* Bs = reinterpret_cast<T*>(smem + 128);
-  T* Cs = Bs + (size_t)p.nbuf * N * CH;
-  float* scarry = reinterpret_cast<float*>(Cs + (size_t)p.nbuf * N * CH);
+  T* stage = reinterpret_cast<T*>(smem + 128);
+  float* tile = reinterpret_cast<float*>(smem + 128 + stage_bytes<T, CH>(N));
+  float* scarry = tile + 2 * N * CH;  // [cpc][N]
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.y;
@@ -175,100 +299,53 @@ sscan_fwd_kernel(SsParams p) {
 
   for (int i = threadIdx.x; i < cpc * N; i += blockDim.x) scarry[i] = 0.f;
   if (threadIdx.x == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    mbar_init(bar, 1);
     mbar_fence_init();
   }
   __syncthreads();
-  if (p.bulk) {
-    for (int k = 0; k < p.nbuf && k < nch; ++k) stage_bc<T, CH>(p, Bs, Cs, bars, k, k * CH, Bg, Cg, threadIdx.x == 0);
-  }
+  if (p.bulk && threadIdx.x == 0) stage_bc<T, CH>(p, stage, bar, 0, Bg, Cg, true);
 
   for (int k = 0; k < nch; ++k) {
     const int t0 = k * CH;
-    const int buf = k % p.nbuf;
-    if (p.bulk) {
-      mbar_wait_bounded(&bars[buf], (uint32_t)((k / p.nbuf) & 1), &g_sscan_err);
-    } else {
-      stage_bc<T, CH>(p, Bs, Cs, bars, buf, t0, Bg, Cg, false);
-      __syncthreads();
-    }
-    const T* Bt = Bs + (size_t)buf * N * CH + lane * ITEMS;
-    const T* Ct = Cs + (size_t)buf * N * CH + lane * ITEMS;
+    fetch_chunk<T, ITEMS>(p, stage, tile, bar, k, t0, k + 1 < nch ? t0 + CH : -1, Bg, Cg);
     const int tl = t0 + lane * ITEMS;
 
     for (int j = 0; j < p.cpw; ++j) {
       const int cl = warp * p.cpw + j;
       const int d = d0 + cl;
       const int64_t chan = (int64_t)b * p.dim + d;
-      float uu[ITEMS], dlt[ITEMS];
-      load_items<T, ITEMS>(uu, reinterpret_cast<const T*>(p.u) + chan * L, tl, L, p.vec_io);
+      float dlt[ITEMS], du[ITEMS], y[ITEMS];
+      load_items<T, ITEMS>(du, reinterpret_cast<const T*>(p.u) + chan * L, tl, L, p.vec_io);
       load_items<T, ITEMS>(dlt, reinterpret_cast<const T*>(p.delta) + chan * L, tl, L, p.vec_io);
       const float bias = p.bias ? p.bias[d] : 0.f;
+      const float Dd = p.D ? p.D[d] : 0.f;
+      float S = 0.f;
 #pragma unroll
       for (int i = 0; i < ITEMS; ++i) {
         float v = dlt[i] + bias;
         if (p.softplus) v = softplus_f(v);
-        dlt[i] = (tl + i < L) ? v : 0.f;  // padded steps are the identity
+        v = (tl + i < L) ? v : 0.f;  // padded steps are the identity
+        dlt[i] = v;
+        S += v;
+        y[i] = Dd * du[i];
+        du[i] *= v;
       }
-      float y[ITEMS];
-#pragma unroll
-      for (int i = 0; i < ITEMS; ++i) y[i] = 0.f;
-
-      for (int n = 0; n < N; ++n) {
-        const float A2 = p.A[(int64_t)d * N + n] * kLog2e;
-        float a[ITEMS], h[ITEMS], Bv[ITEMS];
-        load_smem_items<T, ITEMS>(Bv, Bt + n * CH);
-        float P = 1.f, H = 0.f;
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-          a[i] = ex2(dlt[i] * A2);
-          h[i] = dlt[i] * uu[i] * Bv[i];
-          H = fmaf(a[i], H, h[i]);
-          P *= a[i];
-        }
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float Pp = __shfl_up_sync(0xffffffffu, P, off);
-          const float Hp = __shfl_up_sync(0xffffffffu, H, off);
-          if (lane >= off) { H = fmaf(P, Hp, H); P *= Pp; }
-        }
-        const float carry = scarry[cl * N + n];
-        float Pe = __shfl_up_sync(0xffffffffu, P, 1);
-        float He = __shfl_up_sync(0xffffffffu, H, 1);
-        if (lane == 0) { Pe = 1.f; He = 0.f; }
-        const float newc = __shfl_sync(0xffffffffu, fmaf(P, carry, H), 31);
-        float hh = fmaf(Pe, carry, He);
-        float Cv[ITEMS];
-        load_smem_items<T, ITEMS>(Cv, Ct + n * CH);
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-          hh = fmaf(a[i], hh, h[i]);
-          y[i] = fmaf(Cv[i], hh, y[i]);
-        }
-        if (p.chunk_states != nullptr && ((tl + ITEMS) % kStateStride) == 0) {
-          const int idx = (tl + ITEMS) / kStateStride - 1;
-          if (idx < p.nsaved) p.chunk_states[(chan * p.nsaved + idx) * N + n] = hh;
-        }
-        if (lane == 0) scarry[cl * N + n] = newc;
-      }
-      // epilogue: out = (y + D u) * silu(z)
-      const float Dd = p.D ? p.D[d] : 0.f;
-      float o[ITEMS];
+      const float* Arow = p.A + (int64_t)d * N;
+      float* carry_row = scarry + cl * N;
+      // lane 31 ends the chunk = one state stride: it saves the states for the backward
+      float* save = (p.chunk_states != nullptr && lane == 31) ? p.chunk_states + (chan * p.nsaved + k) * N : nullptr;
+      int n = 0;
+      for (; n + 2 <= N; n += 2) fwd_states<ITEMS, 2>(n, N, dlt, du, y, S, Arow, tile, lane, carry_row, save);
+      if (n < N) fwd_states<ITEMS, 1>(n, N, dlt, du, y, S, Arow, tile, lane, carry_row, save);
       if (p.z != nullptr) {
         float zz[ITEMS];
         load_items<T, ITEMS>(zz, reinterpret_cast<const T*>(p.z) + chan * L, tl, L, p.vec_io);
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) o[i] = fmaf(Dd, uu[i], y[i]) * (zz[i] * sigmoid_f(zz[i]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) o[i] = fmaf(Dd, uu[i], y[i]);
+        for (int i = 0; i < ITEMS; ++i) y[i] *= zz[i] * sigmoid_f(zz[i]);
       }
-      store_items<T, ITEMS>(reinterpret_cast<T*>(p.out) + chan * L, o, tl, L, p.vec_io);
+      store_items<T, ITEMS>(reinterpret_cast<T*>(p.out) + chan * L, y, tl, L, p.vec_io);
     }
-    __syncthreads();  // buffer `buf` fully consumed; carries visible
-    if (p.bulk && k + p.nbuf < nch)
-      stage_bc<T, CH>(p, Bs, Cs, bars, buf, (k + p.nbuf) * CH, Bg, Cg, threadIdx.x == 0);
+    __syncthreads();  // tile consumed; carries visible
   }
   if (p.last_state != nullptr) {
     for (int i = threadIdx.x; i < cpc * N; i += blockDim.x) {
@@ -281,23 +358,29 @@ sscan_fwd_kernel(SsParams p) {
 // ============================================================================
 // Backward
 // ============================================================================
+__device__ __forceinline__ void red_add_v4(float* addr, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
 template <typename T>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 sscan_bwd_kernel(SsParams p) {
-  constexpr int ITEMS = kItemsB;
+  constexpr int ITEMS = kItems;
   constexpr int CH = 32 * ITEMS;
   extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
   const int N = p.N, L = p.L;
-  T* Bs = reinterpret_cast<T*>(smem + 128);
-  T* Cs = Bs + (size_t)p.nbuf * N * CH;
-  float* sdB = reinterpret_cast<float*>(Cs + (size_t)p.nbuf * N * CH);  // [N][CH]
-  float* sdC = sdB + N * CH;                                           // [N][CH]
+  T* stage = reinterpret_cast<T*>(smem + 128);
+  float* tile = reinterpret_cast<float*>(smem + 128 + stage_bytes<T, CH>(N));
+  float* sdB = tile + 2 * N * CH;  // [N][ITEMS][32]
+  float* sdC = sdB + N * CH;       // [N][ITEMS][32]
   const int cpc = p.nw * p.cpw;
-  float* sg = sdC + N * CH;       // adjoint carries [cpc][N] (pre-multiplied by a)
-  float* sdA = sg + cpc * N;      // dA partials [cpc][N]
-  float* sdD = sdA + cpc * N;     // dD partials [cpc]
-  float* sdb = sdD + cpc;         // dbias partials [cpc]
+  float* sg = sdC + N * CH;        // adjoint carries [cpc][N] (pre-multiplied by a)
+  float* sdA = sg + cpc * N;       // dA partials [cpc][N]
+  float* sdD = sdA + cpc * N;      // dD partials [cpc]
+  float* sdb = sdD + cpc;          // dbias partials [cpc]
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.y;
@@ -312,82 +395,75 @@ sscan_bwd_kernel(SsParams p) {
   for (int i = threadIdx.x; i < 2 * N * CH; i += blockDim.x) sdB[i] = 0.f;
   for (int i = threadIdx.x; i < 2 * cpc * N + 2 * cpc; i += blockDim.x) sg[i] = 0.f;
   if (threadIdx.x == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+    mbar_init(bar, 1);
     mbar_fence_init();
   }
   __syncthreads();
-  if (p.bulk) {
-    for (int it = 0; it < p.nbuf && it < nch; ++it)
-      stage_bc<T, CH>(p, Bs, Cs, bars, it, (nch - 1 - it) * CH, Bg, Cg, threadIdx.x == 0);
-  }
+  if (p.bulk && threadIdx.x == 0) stage_bc<T, CH>(p, stage, bar, (nch - 1) * CH, Bg, Cg, true);
 
   for (int it = 0; it < nch; ++it) {
     const int k = nch - 1 - it;
     const int t0 = k * CH;
-    const int buf = it % p.nbuf;
-    if (p.bulk) {
-      mbar_wait_bounded(&bars[buf], (uint32_t)((it / p.nbuf) & 1), &g_sscan_err);
-    } else {
-      stage_bc<T, CH>(p, Bs, Cs, bars, buf, t0, Bg, Cg, false);
-      __syncthreads();
-    }
-    const T* Bt = Bs + (size_t)buf * N * CH + lane * ITEMS;
-    const T* Ct = Cs + (size_t)buf * N * CH + lane * ITEMS;
+    const int len = min(CH, L - t0);
+    fetch_chunk<T, ITEMS>(p, stage, tile, bar, it, t0, k > 0 ? t0 - CH : -1, Bg, Cg);
     const int tl = t0 + lane * ITEMS;
 
     for (int j = 0; j < p.cpw; ++j) {
       const int cl = warp * p.cpw + j;
       const int d = d0 + cl;
       const int64_t chan = (int64_t)b * p.dim + d;
-      float uu[ITEMS], dlt[ITEMS], dlr[ITEMS], dy[ITEMS], dout[ITEMS];
+      float uu[ITEMS], dlt[ITEMS], dlr[ITEMS], dy[ITEMS];
       load_items<T, ITEMS>(uu, reinterpret_cast<const T*>(p.u) + chan * L, tl, L, p.vec_io);
       load_items<T, ITEMS>(dlr, reinterpret_cast<const T*>(p.delta) + chan * L, tl, L, p.vec_io);
-      load_items<T, ITEMS>(dout, reinterpret_cast<const T*>(p.dout) + chan * L, tl, L, p.vec_io);
+      load_items<T, ITEMS>(dy, reinterpret_cast<const T*>(p.dout) + chan * L, tl, L, p.vec_io);  // dout for now
       const float bias = p.bias ? p.bias[d] : 0.f;
       const float Dd = p.D ? p.D[d] : 0.f;
+      float S = 0.f;
 #pragma unroll
       for (int i = 0; i < ITEMS; ++i) {
         const bool ok = tl + i < L;
         dlr[i] += bias;
         dlt[i] = ok ? (p.softplus ? softplus_f(dlr[i]) : dlr[i]) : 0.f;
-        if (!ok) dout[i] = 0.f;
+        S += dlt[i];
       }
+      // dy = dout * silu(z); the gate factor is recomputed for dz after the state loop
       if (p.z != nullptr) {
         float zz[ITEMS];
         load_items<T, ITEMS>(zz, reinterpret_cast<const T*>(p.z) + chan * L, tl, L, p.vec_io);
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) dy[i] = dout[i] * zz[i] * sigmoid_f(zz[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < ITEMS; ++i) dy[i] = dout[i];
+        for (int i = 0; i < ITEMS; ++i) dy[i] *= zz[i] * sigmoid_f(zz[i]);
       }
       float yacc[ITEMS], ddl[ITEMS], duacc[ITEMS];
 #pragma unroll
       for (int i = 0; i < ITEMS; ++i) { yacc[i] = Dd * uu[i]; ddl[i] = 0.f; duacc[i] = dy[i] * Dd; }
+      const float Sr = S - dlt[0];  // sum of delta' over the lane's steps 1..ITEMS-1
+      const float* Arow = p.A + (int64_t)d * N;
+      const float* hc_row = (k > 0) ? p.chunk_states_in + (chan * p.nsaved + (k - 1)) * N : nullptr;
+      float dAl_keep = 0.f;  // lane n < N keeps state n's dA partial
 
       for (int n = 0; n < N; ++n) {
-        const float An = p.A[(int64_t)d * N + n];
+        const float An = Arow[n];
         const float A2 = An * kLog2e;
         float a[ITEMS], h[ITEMS], Bv[ITEMS], Cv[ITEMS];
-        load_smem_items<T, ITEMS>(Bv, Bt + n * CH);
-        load_smem_items<T, ITEMS>(Cv, Ct + n * CH);
+        load_tile<ITEMS>(Bv, tile + n * CH, lane);
+        load_tile<ITEMS>(Cv, tile + (N + n) * CH, lane);
         // ---- forward recompute of the states inside the chunk
-        float P = 1.f, H = 0.f;
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
           a[i] = ex2(dlt[i] * A2);
           h[i] = dlt[i] * uu[i] * Bv[i];
-          H = fmaf(a[i], H, h[i]);
-          P *= a[i];
         }
+        float H = h[0];
+#pragma unroll
+        for (int i = 1; i < ITEMS; ++i) H = fmaf(a[i], H, h[i]);
+        float P = ex2(S * A2);
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
           const float Pp = __shfl_up_sync(0xffffffffu, P, off);
           const float Hp = __shfl_up_sync(0xffffffffu, H, off);
           if (lane >= off) { H = fmaf(P, Hp, H); P *= Pp; }
         }
-        const float hc = k > 0 ? p.chunk_states_in[(chan * p.nsaved + (k - 1)) * N + n] : 0.f;
+        const float hc = hc_row ? hc_row[n] : 0.f;
         float Pe = __shfl_up_sync(0xffffffffu, P, 1);
         float He = __shfl_up_sync(0xffffffffu, H, 1);
         if (lane == 0) { Pe = 1.f; He = 0.f; }
@@ -404,19 +480,11 @@ sscan_bwd_kernel(SsParams p) {
         // ---- reverse scan of the adjoint g_t = dy_t C_t + a_{t+1} g_{t+1}
         const float a_next_lane = __shfl_down_sync(0xffffffffu, a[0], 1);
         const float ra_last = (lane == 31) ? 1.f : a_next_lane;
-        float Q = 1.f, G = 0.f;
+        float G = dy[ITEMS - 1] * Cv[ITEMS - 1];
 #pragma unroll
-        for (int i = ITEMS - 1; i >= 0; --i) {
-          const float ra = (i == ITEMS - 1) ? ra_last : a[i + 1];
-          G = fmaf(ra, G, dy[i] * Cv[i]);
-          Q *= ra;
-        }
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float Qn = __shfl_down_sync(0xffffffffu, Q, off);
-          const float Gn = __shfl_down_sync(0xffffffffu, G, off);
-          if (lane + off < 32) { G = fmaf(Q, Gn, G); Q *= Qn; }
-        }
+        for (int i = ITEMS - 2; i >= 0; --i) G = fmaf(a[i + 1], G, dy[i] * Cv[i]);
+        float Q = ex2(Sr * A2) * ra_last;  // = prod of the lane's a_{t+1}
+        scan_down(Q, G, lane);
         const float gc = sg[cl * N + n];  // a_{t0+CH} * g_{t0+CH}
         const float Qd = __shfl_down_sync(0xffffffffu, Q, 1);
         const float Gd = __shfl_down_sync(0xffffffffu, G, 1);
@@ -430,61 +498,73 @@ sscan_bwd_kernel(SsParams p) {
           const float hp = (i > 0) ? h[i - 1] : hin;
           const float ea = gg * hp * a[i];  // dL/d(delta' A) of step i
           dAl = fmaf(ea, dlt[i], dAl);
-          ddl[i] = fmaf(ea, An, fmaf(gg * Bv[i], uu[i], ddl[i]));
-          duacc[i] = fmaf(gg * dlt[i], Bv[i], duacc[i]);
-          const int ti = i * 32 + lane;  // [n][item][lane]: conflict-free shared atomics
-          atomicAdd(&sdB[n * CH + ti], gg * dlt[i] * uu[i]);
-          atomicAdd(&sdC[n * CH + ti], dy[i] * h[i]);
+          const float gB = gg * Bv[i];
+          ddl[i] = fmaf(ea, An, fmaf(gB, uu[i], ddl[i]));
+          duacc[i] = fmaf(gB, dlt[i], duacc[i]);
+          const int si = n * CH + i * 32 + lane;  // [n][item][lane]: conflict-free
+          atomicAdd(&sdB[si], gg * dlt[i] * uu[i]);
+          atomicAdd(&sdC[si], dy[i] * h[i]);
         }
         dAl = warp_sum(dAl);
-        if (lane == 0) {
-          sdA[cl * N + n] += dAl;
-          sg[cl * N + n] = gfirst0;
-        }
+        if (lane == n) dAl_keep += dAl;
+        if (lane == 0) sg[cl * N + n] = gfirst0;
       }
       // ---- per-step outputs
       float dDl = 0.f, dbl = 0.f;
-      float odl[ITEMS];
 #pragma unroll
       for (int i = 0; i < ITEMS; ++i) {
-        const float s = p.softplus ? sigmoid_f(dlr[i]) : 1.f;
-        const float v = (p.softplus && dlr[i] > 20.f) ? ddl[i] : ddl[i] * s;
-        odl[i] = (tl + i < L) ? v : 0.f;
-        dbl += odl[i];
+        const float s = p.softplus ? (dlr[i] > 20.f ? 1.f : sigmoid_f(dlr[i])) : 1.f;
+        const float v = (tl + i < L) ? ddl[i] * s : 0.f;
+        ddl[i] = v;
+        dbl += v;
         dDl = fmaf(dy[i], uu[i], dDl);
       }
       store_items<T, ITEMS>(reinterpret_cast<T*>(p.du) + chan * L, duacc, tl, L, p.vec_io);
-      store_items<T, ITEMS>(reinterpret_cast<T*>(p.ddelta) + chan * L, odl, tl, L, p.vec_io);
+      store_items<T, ITEMS>(reinterpret_cast<T*>(p.ddelta) + chan * L, ddl, tl, L, p.vec_io);
       if (p.z != nullptr) {
-        float zz[ITEMS], odz[ITEMS];
+        float zz[ITEMS], dout[ITEMS];
         load_items<T, ITEMS>(zz, reinterpret_cast<const T*>(p.z) + chan * L, tl, L, p.vec_io);
+        load_items<T, ITEMS>(dout, reinterpret_cast<const T*>(p.dout) + chan * L, tl, L, p.vec_io);
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) {
           const float sgz = sigmoid_f(zz[i]);
-          odz[i] = dout[i] * yacc[i] * sgz * (1.f + zz[i] * (1.f - sgz));
+          zz[i] = dout[i] * yacc[i] * sgz * (1.f + zz[i] * (1.f - sgz));
         }
-        store_items<T, ITEMS>(reinterpret_cast<T*>(p.dz) + chan * L, odz, tl, L, p.vec_io);
+        store_items<T, ITEMS>(reinterpret_cast<T*>(p.dz) + chan * L, zz, tl, L, p.vec_io);
       }
       dDl = warp_sum(dDl);
       dbl = warp_sum(dbl);
       if (lane == 0) { sdD[cl] += dDl; sdb[cl] += dbl; }
+      if (lane < N) sdA[cl * N + lane] += dAl_keep;
     }
     __syncthreads();  // chunk consumed; sdB/sdC complete
-    const int len = min(CH, L - t0);
-    for (int idx = threadIdx.x; idx < N * CH; idx += blockDim.x) {
-      const int n = idx / CH, t = idx - n * CH;
-      const int si = n * CH + (t % ITEMS) * 32 + t / ITEMS;
-      if (t < len) {
-        atomicAdd(&dBg[(int64_t)n * L + t0 + t], sdB[si]);
-        atomicAdd(&dCg[(int64_t)n * L + t0 + t], sdC[si]);
+    // flush the [n][item][lane] accumulators: 4 consecutive steps per thread, v4 reductions
+    const int nq = N * CH / 4;
+    for (int q = threadIdx.x; q < nq; q += blockDim.x) {
+      const int n = q / (CH / 4), t = (q - n * (CH / 4)) * 4;
+      const int ln = t / ITEMS, i = t - ln * ITEMS;
+      const int base = n * CH + ln;
+      const float4 vb = make_float4(sdB[base + (i + 0) * 32], sdB[base + (i + 1) * 32], sdB[base + (i + 2) * 32],
+                                    sdB[base + (i + 3) * 32]);
+      const float4 vc = make_float4(sdC[base + (i + 0) * 32], sdC[base + (i + 1) * 32], sdC[base + (i + 2) * 32],
+                                    sdC[base + (i + 3) * 32]);
+      const int64_t off = (int64_t)n * L + t0 + t;
+      if (t + 4 <= len && ((reinterpret_cast<uintptr_t>(dBg + off) & 15) == 0)) {
+        red_add_v4(dBg + off, vb);
+        red_add_v4(dCg + off, vc);
+      } else {
+        const float eb[4] = {vb.x, vb.y, vb.z, vb.w}, ec[4] = {vc.x, vc.y, vc.z, vc.w};
+        for (int e = 0; e < 4; ++e)
+          if (t + e < len) {
+            atomicAdd(dBg + off + e, eb[e]);
+            atomicAdd(dCg + off + e, ec[e]);
+          }
       }
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < 2 * N * CH; idx += blockDim.x) sdB[idx] = 0.f;
-    __syncthreads();
-    if (p.bulk && it + p.nbuf < nch)
-      stage_bc<T, CH>(p, Bs, Cs, bars, buf, (nch - 1 - (it + p.nbuf)) * CH, Bg, Cg, threadIdx.x == 0);
   }
+  __syncthreads();
   for (int i = threadIdx.x; i < cpc; i += blockDim.x) {
     float* pr = p.part + ((int64_t)b * p.dim + d0 + i) * (N + 2);
     for (int n = 0; n < N; ++n) pr[n] = sdA[i * N + n];
@@ -527,12 +607,22 @@ int validate(int64_t batch, int64_t dim, int64_t L, int64_t N, int64_t groups, i
   AK_REQUIRE(valid_dtype(dt), AK_ERR_DTYPE, "selective_scan: unsupported dtype %d", dt);
   AK_REQUIRE(batch >= 0 && batch < 65536 && dim >= 0 && L >= 0 && L < (1LL << 31), AK_ERR_SHAPE,
              "selective_scan: bad shape");
-  AK_REQUIRE(N >= 1 && N <= 64, AK_ERR_SHAPE, "selective_scan: dstate must be in [1, 64], got %lld", (long long)N);
+  AK_REQUIRE(N >= 1 && N <= 32, AK_ERR_SHAPE, "selective_scan: dstate must be in [1, 32], got %lld", (long long)N);
   AK_REQUIRE(groups >= 1 && dim % groups == 0, AK_ERR_SHAPE, "selective_scan: dim %% groups != 0");
   return AK_OK;
 }
 
 int nsaved_of(int64_t L) { return (int)((L + kStateStride - 1) / kStateStride); }
+
+template <typename T, int CH>
+size_t fwd_smem(int N, int cpc) {
+  return 128 + stage_bytes<T, CH>(N) + (size_t)2 * N * CH * 4 + (size_t)cpc * N * 4;
+}
+
+template <typename T, int CH>
+size_t bwd_smem(int N, int cpc) {
+  return 128 + stage_bytes<T, CH>(N) + (size_t)4 * N * CH * 4 + (size_t)(2 * cpc * N + 2 * cpc) * 4;
+}
 
 }  // namespace
 }  // namespace ak
@@ -569,14 +659,13 @@ extern "C" int ak_selective_scan_fwd(void* out, float* last_state, float* chunk_
   p.bulk = (((seqlen * es) % 16) == 0 && aligned16(Bm) && aligned16(Cm)) ? 1 : 0;
   p.vec_io = (((seqlen * es) % 16) == 0 && aligned16(u) && aligned16(delta) && aligned16(out) &&
               (z == nullptr || aligned16(z))) ? 1 : 0;
-  constexpr int CH = 32 * kItemsF;
-  size_t tile = (size_t)dstate * CH * es * 2;  // B + C, one buffer
-  p.nbuf = (128 + 2 * tile + (size_t)p.nw * p.cpw * dstate * 4) <= 200 * 1024 ? 2 : 1;
-  const size_t smem = 128 + p.nbuf * tile + (size_t)p.nw * p.cpw * dstate * 4;
-  AK_REQUIRE(smem <= 227 * 1024, AK_ERR_SHAPE, "selective_scan_fwd: dstate too large for shared memory");
-  dim3 grid((unsigned)(dim / (p.nw * p.cpw)), (unsigned)batch);
+  constexpr int CH = 32 * kItems;
+  const int cpc = p.nw * p.cpw;
+  dim3 grid((unsigned)(dim / cpc), (unsigned)batch);
   AK_DISPATCH_DTYPE(dt, T, {
-    auto kern = sscan_fwd_kernel<T, kItemsF>;
+    const size_t smem = fwd_smem<T, CH>(p.N, cpc);
+    AK_REQUIRE(smem <= 227 * 1024, AK_ERR_SHAPE, "selective_scan_fwd: dstate too large for shared memory");
+    auto kern = sscan_fwd_kernel<T>;
     AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "selective_scan_fwd: smem attribute");
     kern<<<grid, p.nw * 32, smem, st>>>(p);
@@ -638,21 +727,18 @@ extern "C" int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB
   p.dpg = (int)(dim / groups);
   p.softplus = delta_softplus ? 1 : 0;
   p.nsaved = nsaved_of(seqlen);
-  pick_layout(p.dpg, 32, &p.nw, &p.cpw);
+  pick_layout(p.dpg, 16, &p.nw, &p.cpw);
   const int es = elem_size(dt);
   p.bulk = (((seqlen * es) % 16) == 0 && aligned16(Bm) && aligned16(Cm)) ? 1 : 0;
   p.vec_io = (((seqlen * es) % 16) == 0 && aligned16(u) && aligned16(delta) && aligned16(dout) && aligned16(du) &&
               aligned16(ddelta) && (z == nullptr || (aligned16(z) && aligned16(dz)))) ? 1 : 0;
-  constexpr int CH = 32 * kItemsB;
+  constexpr int CH = 32 * kItems;
   const int cpc = p.nw * p.cpw;
-  const size_t tile = (size_t)dstate * CH * es * 2;
-  const size_t fixed = 128 + 2 * (size_t)dstate * CH * 4 + (2 * (size_t)cpc * dstate + 2 * cpc) * 4;
-  p.nbuf = (fixed + 2 * tile) <= 200 * 1024 ? 2 : 1;
-  const size_t smem = fixed + p.nbuf * tile;
-  AK_REQUIRE(smem <= 227 * 1024, AK_ERR_SHAPE, "selective_scan_bwd: dstate too large for shared memory");
   AK_CUDA_TRY(cudaMemsetAsync(ws, 0, 2 * nbc * sizeof(float), st), "selective_scan_bwd: workspace clear");
   dim3 grid((unsigned)(dim / cpc), (unsigned)batch);
   AK_DISPATCH_DTYPE(dt, T, {
+    const size_t smem = bwd_smem<T, CH>(p.N, cpc);
+    AK_REQUIRE(smem <= 227 * 1024, AK_ERR_SHAPE, "selective_scan_bwd: dstate too large for shared memory");
     auto kern = sscan_bwd_kernel<T>;
     AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "selective_scan_bwd: smem attribute");

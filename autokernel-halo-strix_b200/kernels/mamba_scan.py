@@ -10,7 +10,7 @@ last_state (batch, dim, N) fp32, whose gradient is not propagated (as in the
 reference).  The forward saves the state every `state_stride()` steps so the
 backward recomputes instead of storing the full state tensor.
 
-Supported: real A, input-dependent (3-D/4-D) B and C, N <= 64, dtypes
+Supported: real A, input-dependent (3-D/4-D) B and C, N <= 32, dtypes
 fp32/bf16/fp16.  Complex A and constant (dim, N) B/C raise NotImplementedError.
 """
 import torch

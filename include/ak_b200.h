@@ -165,7 +165,7 @@ AK_API int ak_selective_scan_state_stride(void);
  *   h_t[n] = exp(delta'_t * A[d,n]) h_{t-1}[n] + delta'_t * B[b,g,n,t] * u_t
  *   y_t = sum_n C[b,g,n,t] h_t[n] + D[d] u_t;  out = y * silu(z)  (if z)
  * u, delta, z, out: (batch, dim, L) dt; A: fp32 (dim, dstate);
- * B, C: (batch, groups, dstate, L) dt, g = d / (dim / groups);
+ * B, C: (batch, groups, dstate, L) dt, g = d / (dim / groups); 1 <= dstate <= 32;
  * D, delta_bias: fp32 (dim) nullable; last_state: fp32 (batch, dim, dstate)
  * nullable; chunk_states: fp32 (batch, dim, n_saved, dstate) nullable
  * (required for the backward).
