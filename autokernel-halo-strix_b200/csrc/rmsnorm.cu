@@ -12,6 +12,8 @@
 // in a fixed order, so dw is bitwise deterministic.
 #include "ak_common.cuh"
 
+#include <mutex>
+
 namespace ak {
 namespace {
 
@@ -385,5 +387,97 @@ extern "C" int ak_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspace, si
   AK_DISPATCH_XW(dt_x, dt_w,
                  return bwd_impl<T, TW>(dx, dw, dt_dw, (float*)workspace, dy, x, w, M, (int)N, eps,
                                         (cudaStream_t)stream));
+  return AK_OK;
+}
+
+// ============================================================================
+// RMSNorm backward that allocates nothing (no counterpart in the reference).
+//
+// Some callers cannot hand this library a workspace: code running where
+// cudaMalloc is off limits (a custom allocator that owns all device memory,
+// a host runtime that forbids allocation after start-up, a plugin ABI that
+// passes only inputs and outputs).  ak_rmsnorm_bwd_noalloc serves them: its
+// per-CTA dw partial rows live in the file-scope device array below instead
+// of a caller workspace.
+// ============================================================================
+namespace ak {
+namespace {
+
+// 4 MiB of fp32 partial rows, resident on every GPU that loads the library.
+constexpr size_t kNoAllocFloats = (size_t)1 << 20;
+static __device__ __align__(256) float g_rms_noalloc_scratch[kNoAllocFloats];
+
+// Device address of g_rms_noalloc_scratch per device (host code cannot use the
+// symbol's name as a device pointer); resolved once per device.
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {nullptr};
+
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  AK_CUDA_TRY(cudaGetDevice(&dev), "ak_rmsnorm_bwd_noalloc: cudaGetDevice");
+  AK_REQUIRE(dev >= 0 && dev < 64, AK_ERR_ARG, "ak_rmsnorm_bwd_noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    AK_CUDA_TRY(cudaGetSymbolAddress(&p, g_rms_noalloc_scratch), "ak_rmsnorm_bwd_noalloc: cudaGetSymbolAddress");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return AK_OK;
+}
+
+// Same kernels as ak_rmsnorm_bwd with the CTA count G chosen so that G partial
+// rows of N floats fit the static scratch.  Every CTA overwrites its whole row
+// before the reduction reads it, so nothing in the scratch needs clearing.
+template <typename T, typename TW>
+int bwd_noalloc_impl(void* dx, void* dw, int dt_dw, float* ws, int G, const void* dy, const void* x, const void* w,
+                     int64_t M, int N, float eps, cudaStream_t st) {
+  RmsPlan p = plan<T, TW>(M, N, x, dx, w);
+  if (!aligned16(dy)) p.warp_path = false;
+  if (p.nit * p.vec > 32) p.warp_path = false;
+  constexpr int VEC = 16 / sizeof(T);
+  if (M > 0) {
+    if (p.warp_path) {
+      const size_t smem = (size_t)kWarps * N * sizeof(float);
+      AK_NIT_SWITCH(p.nit, NIT, {
+        auto kern = rmsnorm_bwd_warp<T, TW, VEC, NIT>;
+        if (smem > 48 * 1024)
+          AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                      "ak_rmsnorm_bwd_noalloc: smem attribute");
+        kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps);
+      });
+    } else {
+      rmsnorm_bwd_block<T, TW><<<G, 256, 0, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps);
+    }
+    AK_CHECK_LAUNCH("ak_rmsnorm_bwd_noalloc");
+  }
+  dim3 rb(32, 8);
+  const unsigned rg = (unsigned)((N + 31) / 32);
+  AK_DISPATCH_DTYPE(dt_dw, TD, rmsnorm_dw_reduce<TD><<<rg, rb, 0, st>>>((TD*)dw, ws, M > 0 ? G : 0, N));
+  AK_CHECK_LAUNCH("ak_rmsnorm_bwd_noalloc(dw reduce)");
+  return AK_OK;
+}
+
+}  // namespace
+}  // namespace ak
+
+extern "C" int ak_rmsnorm_bwd_noalloc(void* dx, void* dw, int dt_dw, const void* dy, const void* x, const void* w,
+                                      int64_t M, int64_t N, float eps, int dt_x, int dt_w, void* stream) {
+  clear_error();
+  AK_REQUIRE(M >= 0 && N > 0, AK_ERR_SHAPE, "ak_rmsnorm_bwd_noalloc: bad shape");
+  AK_REQUIRE((size_t)N <= kNoAllocFloats, AK_ERR_SHAPE,
+             "ak_rmsnorm_bwd_noalloc: N=%lld exceeds the static scratch (%zu floats); use ak_rmsnorm_bwd",
+             (long long)N, kNoAllocFloats);
+  AK_REQUIRE(dw && w, AK_ERR_ARG, "ak_rmsnorm_bwd_noalloc: null pointer");
+  AK_REQUIRE(M == 0 || (dx && dy && x), AK_ERR_ARG, "ak_rmsnorm_bwd_noalloc: null pointer");
+  float* ws = nullptr;
+  int rc = noalloc_scratch(&ws);
+  if (rc) return rc;
+  int64_t G = bwd_grid(M, (int)N);
+  const int64_t fit = (int64_t)(kNoAllocFloats / (size_t)N);
+  if (G > fit) G = fit;
+  AK_DISPATCH_XW(dt_x, dt_w,
+                 return bwd_noalloc_impl<T, TW>(dx, dw, dt_dw, ws, (int)G, dy, x, w, M, (int)N, eps,
+                                                (cudaStream_t)stream));
   return AK_OK;
 }

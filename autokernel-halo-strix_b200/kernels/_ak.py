@@ -28,6 +28,7 @@ SIGNATURES = {
     "ak_rmsnorm_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
     "ak_rmsnorm_bwd_workspace_size": [_i64, _i64, ctypes.POINTER(_sz)],
     "ak_rmsnorm_bwd": [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
+    "ak_rmsnorm_bwd_noalloc": [_vp, _vp, _i, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
     "ak_softmax_fwd": [_vp, _vp, _i64, _i64, _i, _vp],
     "ak_softmax_bwd": [_vp, _vp, _vp, _i64, _i64, _i, _vp],
     "ak_ce_rows_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _i, _vp],

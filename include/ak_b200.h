@@ -75,6 +75,20 @@ AK_API int ak_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspace, size_t
                    int64_t M, int64_t N, float eps, int dt_x, int dt_w,
                    void* stream);
 
+/* ak_rmsnorm_bwd without a workspace argument, for callers that cannot
+ * allocate device memory (e.g. hosts whose own allocator owns all of it, or
+ * plugin ABIs that pass only inputs and outputs).  No counterpart in the
+ * reference.  The dw partial rows live in a 4 MiB static device array
+ * (2^20 floats) that every GPU loading the library keeps until exit; N up to
+ * 2^20 is accepted, larger N returns AK_ERR_SHAPE.  The first call on a device
+ * looks up that array's device address (cudaGetSymbolAddress), so make it
+ * before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU (different streams, or several host threads) race on it and must
+ * be serialised by the caller.  Allocates nothing. */
+AK_API int ak_rmsnorm_bwd_noalloc(void* dx, void* dw, int dt_dw, const void* dy,
+                   const void* x, const void* w, int64_t M, int64_t N, float eps,
+                   int dt_x, int dt_w, void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Row softmax over the last dimension
  * ------------------------------------------------------------------------ */
