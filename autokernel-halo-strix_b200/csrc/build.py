@@ -74,7 +74,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False, e
     newest = max(o.stat().st_mtime for o in objs)
     if force or not LIB.exists() or LIB.stat().st_mtime < newest:
         cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(LIB),
-               "-lcuda", "-lcudart"]
+               "-lcudart"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stderr}\n{res.stdout}")

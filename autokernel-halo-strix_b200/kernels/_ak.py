@@ -35,6 +35,8 @@ SIGNATURES = {
     "ak_ce_rows_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _f, _i, _vp],
     "ak_ce_rows_reduce": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp],
     "ak_ce_inv_valid": [_vp, _vp, _i64, _i64, _vp],
+    "ak_linear_ce_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
+    "ak_linear_ce_fwdbwd": [_vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_scan1_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ak_scan1_bwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_scan1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
@@ -242,6 +244,32 @@ def ce_inv_valid(targets: torch.Tensor, ignore_index: int = -100) -> torch.Tenso
     inv = torch.empty((), dtype=torch.float32, device=dev)
     call("ak_ce_inv_valid", ptr(inv), ptr(targets), targets.numel(), int(ignore_index), stream(dev))
     return inv
+
+
+def linear_ce_supported(hidden: torch.Tensor, weight: torch.Tensor) -> bool:
+    N, D = hidden.shape
+    V = weight.shape[0]
+    return (hidden.dtype in (torch.bfloat16, torch.float16) and weight.dtype == hidden.dtype
+            and N % 8 == 0 and D % 8 == 0 and V % 8 == 0 and N > 0)
+
+
+def linear_ce_fwdbwd(hidden, weight, labels, ignore_index=-100, need_dh=True, need_dw=True):
+    """Fused tcgen05 linear + CE: returns (loss 0-d fp32, lse [N] fp32, dH or None, dW or None)."""
+    dev = require_cuda(hidden, weight, labels)
+    h = hidden.contiguous()
+    w = weight.contiguous()
+    lab = labels.to(torch.int64).contiguous()
+    N, D = h.shape
+    V = w.shape[0]
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    lse = torch.empty(N, dtype=torch.float32, device=dev)
+    dH = torch.empty_like(h) if need_dh else None
+    dW = torch.empty_like(w) if need_dw else None
+    ws_bytes = _size_query("ak_linear_ce_workspace_size", N, D, V)
+    ws = workspace(ws_bytes, dev)
+    call("ak_linear_ce_fwdbwd", ptr(loss), ptr(lse), ptr(dH), ptr(dW), ptr(ws), ws_bytes, ptr(h), ptr(w), ptr(lab),
+         N, D, V, int(ignore_index), dtype_code(h), stream(dev))
+    return loss, lse, dH, dW
 
 
 # ---------------------------------------------------------------------------

@@ -7,6 +7,12 @@ loss, lse and the pre-scaled gradient G, then dH = G W and dW += G^T h (fp32
 accumulation).  All gradients are produced in the forward; the backward
 returns them scaled by grad_output.
 
+For bf16/fp16 inputs without softcap, label smoothing or z-loss the whole
+computation is one call into the tcgen05 kernel (`ak_linear_ce_fwdbwd`): logits
+tiles stay in tensor memory, the gradient is formed in the GEMM epilogue, and
+dH / dW come from the same tensor-core GEMM.  Other feature combinations use the
+row-chunked path below (cuBLAS GEMMs around the fused CE row kernel).
+
 Differences, all deliberate: inputs keep their dtype (the reference coerces to
 fp16, :219-223); the valid-row count and 1/n_valid stay on the device (the
 reference syncs with `.item()`, :73).
@@ -69,6 +75,31 @@ class _ChunkedLinearCrossEntropy(torch.autograd.Function):
         return gh, gw, None, None, None, None, None, None
 
 
+class _FusedLinearCrossEntropy(torch.autograd.Function):
+    """tcgen05 path: logits tiles live only in TMEM; loss, dH and dW come out of one C-ABI call."""
+
+    @staticmethod
+    @custom_fwd(device_type="cuda")
+    def forward(ctx, hidden, weight, targets, ignore_index):
+        w = weight.to(hidden.dtype)
+        loss, _lse, dh, dw = _ak.linear_ce_fwdbwd(hidden, w, targets, ignore_index, need_dh=hidden.requires_grad,
+                                                   need_dw=weight.requires_grad)
+        ctx.save_for_backward(dh, dw.to(weight.dtype) if dw is not None else None)
+        ctx.req = (hidden.requires_grad, weight.requires_grad)
+        return loss
+
+    @staticmethod
+    @custom_bwd(device_type="cuda")
+    def backward(ctx, grad_output):
+        gh, gw = ctx.saved_tensors
+        one = grad_output.dim() == 0 and grad_output.item() == 1.0
+        if ctx.req[0] and not one:
+            gh = gh * grad_output.to(gh.dtype)
+        if ctx.req[1] and not one:
+            gw = gw * grad_output.to(gw.dtype)
+        return (gh if ctx.req[0] else None), (gw if ctx.req[1] else None), None, None
+
+
 class ChunkedLinearCrossEntropyLoss(nn.Module):
     """`nn.Linear + nn.CrossEntropyLoss` without materialising all logits.
 
@@ -84,11 +115,16 @@ class ChunkedLinearCrossEntropyLoss(nn.Module):
         self.ignore_index = int(ignore_index)
         self.label_smoothing = float(label_smoothing)
         self.z_loss_weight = float(z_loss_weight)
+        # tcgen05 fused kernel for bf16/fp16 without softcap / smoothing / z-loss
+        self.use_fused = True
 
     def forward(self, hidden, weight, targets):
         if hidden.dim() == 3:
             hidden = hidden.reshape(-1, hidden.shape[-1])
         if targets.dim() == 2:
             targets = targets.reshape(-1)
+        if (self.use_fused and self.softcap == 0.0 and self.label_smoothing == 0.0 and self.z_loss_weight == 0.0
+                and hidden.is_cuda and _ak.linear_ce_supported(hidden, weight.to(hidden.dtype))):
+            return _FusedLinearCrossEntropy.apply(hidden, weight, targets, self.ignore_index)
         return _ChunkedLinearCrossEntropy.apply(hidden, weight, targets, self.chunk_size, self.softcap,
                                                 self.ignore_index, self.label_smoothing, self.z_loss_weight)

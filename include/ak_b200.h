@@ -145,6 +145,27 @@ AK_API int ak_ce_inv_valid(float* inv_out, const int64_t* targets, int64_t B,
                     int64_t ignore_index, void* stream);
 
 /* ------------------------------------------------------------------------ *
+ * Fused linear + cross-entropy on the tensor cores (tcgen05 / TMEM / TMA)
+ * ------------------------------------------------------------------------ */
+
+/* Workspace bytes for ak_linear_ce_fwdbwd on H[N, D], W[V, D]. */
+AK_API int ak_linear_ce_workspace_size(int64_t N, int64_t D, int64_t V, size_t* bytes);
+
+/* loss[0] = mean over rows with labels != ignore_index of CE(H W^T) (fp32,
+ * n_valid counted on the device), lse[N] fp32 per-row logsumexp, and the
+ * gradients of that mean: dH[N, D] (dt, nullable) and dW[V, D] (dt, nullable).
+ * H, W: bf16 or fp16 (dt), row-major; labels int64[N].  N, D, V multiples of 8.
+ * Logits are never materialised: tcgen05 GEMM tiles feed per-row softmax
+ * statistics and the gradient directly from TMEM.
+ * Replaces _ChunkedLinearCrossEntropy.forward / .backward
+ * (kernels/hip/chunked_linear_cross_entropy.py:55-175) for softcap = 0,
+ * label_smoothing = 0, z_loss_weight = 0. */
+AK_API int ak_linear_ce_fwdbwd(float* loss, float* lse, void* dH, void* dW, void* workspace,
+                   size_t ws_bytes, const void* H, const void* W, const int64_t* labels,
+                   int64_t N, int64_t D, int64_t V, int64_t ignore_index, int dt,
+                   void* stream);
+
+/* ------------------------------------------------------------------------ *
  * Collapsed (single-state) selective scan, fp32, layout (B, L, d)
  * ------------------------------------------------------------------------ */
 

@@ -89,3 +89,36 @@ def test_chunked_linear_ce_bf16(N, D, V):
     loss.backward()
     assert_lowp_close(Hc.grad, rdh, what="dH")
     assert_lowp_close(Wc.grad, rdw, what="dW")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("N,D,V", [(1024, 256, 32768), (200, 72, 1000), (384, 768, 50304), (8, 64, 8)])
+def test_fused_tcgen05_linear_ce(dtype, N, D, V):
+    from kernels import _ak
+    g = torch.Generator().manual_seed(N + D + V)
+    H = torch.randn(N, D, generator=g).to(dtype)
+    W = (torch.randn(V, D, generator=g) * 0.05).to(dtype)
+    lab = torch.randint(0, V, (N,), generator=g)
+    lab[::7] = -100
+    loss, lse, dH, dW = _ak.linear_ce_fwdbwd(H.to(DEV), W.to(DEV), lab.to(DEV), -100)
+    rl, rdh, rdw = O.linear_ce(H, W, lab)
+    logits = H.double() @ W.double().t()
+    assert_fp32_close(lse, torch.logsumexp(logits, -1), rtol=2e-4, what="lse")
+    assert abs(loss.item() - rl.item()) <= 2e-3 * max(1.0, abs(rl.item()))
+    assert_lowp_close(dH, rdh, what="dH")
+    assert_lowp_close(dW, rdw, what="dW")
+
+
+def test_fused_linear_ce_module_autograd():
+    from kernels.hip.chunked_linear_cross_entropy import ChunkedLinearCrossEntropyLoss
+    g = torch.Generator().manual_seed(0)
+    H = torch.randn(512, 128, generator=g).to(torch.bfloat16)
+    W = (torch.randn(4096, 128, generator=g) * 0.05).to(torch.bfloat16)
+    lab = torch.randint(0, 4096, (512,), generator=g)
+    Hc, Wc = H.to(DEV).requires_grad_(True), W.to(DEV).requires_grad_(True)
+    loss = ChunkedLinearCrossEntropyLoss()(Hc, Wc, lab.to(DEV))
+    (2.0 * loss).backward()
+    rl, rdh, rdw = O.linear_ce(H, W, lab)
+    assert abs(loss.item() - rl.item()) < 2e-3 * abs(rl.item())
+    assert_lowp_close(Hc.grad, 2 * rdh, what="dH")
+    assert_lowp_close(Wc.grad, 2 * rdw, what="dW")
