@@ -16,12 +16,12 @@
 //      once so every GEMM reads K-major tiles).
 //
 // GEMM kernel: C[M,N] = A[M,K] B[N,K]^T with bf16/fp16 A, B (K contiguous) and
-// fp32 accumulation in TMEM.  Persistent CTAs of 6 warps: warp 0 issues TMA
+// fp32 accumulation in TMEM.  Persistent CTAs of 10 warps: warp 0 issues TMA
 // loads (128B-swizzled 128x64 and 256x64 boxes) into a 4-stage ring, warp 1
 // issues tcgen05.mma (M=128, N=256, K=16) from one thread into one of two TMEM
-// accumulators (2 x 256 columns), warps 2-5 run the epilogue on the other
-// accumulator via tcgen05.ld, so a tile's epilogue overlaps the next tile's
-// MMAs.  All mbarrier waits are bounded (error flag + return, never a hang).
+// accumulators (2 x 256 columns), warps 2-9 (two warpgroups, one per 128-column
+// half) run the epilogue on the other accumulator via tcgen05.ld, so a tile's
+// epilogue overlaps the next tile's MMAs.  All mbarrier waits are bounded (error flag + return, never a hang).
 // No cluster, no TMA multicast.
 #include "ak_common.cuh"
 
@@ -35,10 +35,13 @@ namespace ak {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (2 warpgroups)
+constexpr int kEpiThreads = 256;
+constexpr int kHalf = BN / 2;   // columns per epilogue warpgroup
 constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+constexpr int kTPitch = BM + 8;    // transpose staging row pitch (16-byte aligned rows)
 
 __device__ int g_lce_err;
 
@@ -147,6 +150,7 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* tfull = empty + STAGES;  // [2]
   uint64_t* tempty = tfull + 2;      // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  T* sT = reinterpret_cast<T*>(smem + STAGES * STAGE_BYTES + 256);  // [2][32][kTPitch] transpose staging
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mtiles = (g.M + BM - 1) / BM, ntiles = (g.N + BN - 1) / BN;
@@ -155,7 +159,7 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 128); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], kEpiThreads); }
     mbar_fence_init();
   }
   if (warp == 1) {
@@ -213,6 +217,8 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   } else {
     // ---------------- epilogue: warps 2..5 own TMEM lanes 32*(warp%4) ...
     const int quad = warp & 3;
+    const int eg = (warp - 2) >> 2;           // epilogue warpgroup: column half
+    T* sTg = sT + eg * 32 * kTPitch;
     const int rl = quad * 32 + lane;  // row within the tile
     int local = 0;
     for (int t = blockIdx.x; t < ntile_total; t += gridDim.x, ++local) {
@@ -227,7 +233,7 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if constexpr (EPI == EPI_STATS) {
         const int64_t lab = rv ? g.labels[row] : -1;
         float m = -INFINITY, s = 0.f;  // s: sum of exp2(x*log2e - m) with m in log2 units
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = eg * kHalf; c < (eg + 1) * kHalf; c += 32) {
           float v[32];
           tmem_ld32(tbase + (uint32_t)c, v);
           float lm = -INFINITY;
@@ -247,7 +253,7 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             m = mn;
           }
         }
-        if (rv) g.part[(int64_t)row * ntiles + nt] = make_float2(m, s);
+        if (rv) g.part[(int64_t)row * (2 * ntiles) + 2 * nt + eg] = make_float2(m, s);
       } else if constexpr (EPI == EPI_GRAD) {
         const int64_t lab = rv ? g.labels[row] : g.ignore_index;
         const bool ign = (lab == g.ignore_index);
@@ -255,7 +261,7 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const float lse2 = rv ? g.lse[row] * kLog2e : 0.f;
         T* grow = reinterpret_cast<T*>(g.G) + (int64_t)row * g.N;
         T* gt = reinterpret_cast<T*>(g.GT);
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = eg * kHalf; c < (eg + 1) * kHalf; c += 32) {
           float v[32];
           tmem_ld32(tbase + (uint32_t)c, v);
 #pragma unroll
@@ -279,21 +285,43 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               for (int j = 0; j < 32; ++j)
                 if (cbase + j < g.N) grow[cbase + j] = from_f<T>(v[j]);
             }
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (cbase + j < g.N) gt[(int64_t)(cbase + j) * g.ldgt + g.gt_col0 + row] = from_f<T>(v[j]);
           }
+          // G^T: transpose the 128x32 block through shared memory, then 16-byte
+          // coalesced stores of 8 consecutive rows per thread.
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sTg[j * kTPitch + rl] = from_f<T>(v[j]);
+          asm volatile("bar.sync %0, 128;" ::"r"(1 + eg) : "memory");
+          const int e = (threadIdx.x - 64) & 127;
+#pragma unroll
+          for (int q = e; q < 32 * (BM / 8); q += 128) {
+            const int cj = q / (BM / 8), rc = q - cj * (BM / 8);
+            const int r0 = mt * BM + rc * 8;
+            if (cbase + cj < g.N && r0 < g.M)
+              *reinterpret_cast<int4*>(gt + (int64_t)(cbase + cj) * g.ldgt + g.gt_col0 + r0) =
+                  *reinterpret_cast<const int4*>(sTg + cj * kTPitch + rc * 8);
+          }
+          asm volatile("bar.sync %0, 128;" ::"r"(1 + eg) : "memory");
         }
       } else {
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = eg * kHalf; c < (eg + 1) * kHalf; c += 32) {
           float v[32];
           tmem_ld32(tbase + (uint32_t)c, v);
           const int cbase = col0 + c;
           if (!rv) continue;
           if constexpr (EPI == EPI_STORE_BF16) {
             T* crow = reinterpret_cast<T*>(g.C) + (int64_t)row * g.ldc;
-            for (int j = 0; j < 32; ++j)
-              if (cbase + j < g.N) crow[cbase + j] = from_f<T>(v[j]);
+            if (cbase + 32 <= g.N) {
+#pragma unroll
+              for (int q = 0; q < 32; q += 8) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = v[q + e];
+                store_frag<T, 8>(crow + cbase + q, f);
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (cbase + j < g.N) crow[cbase + j] = from_f<T>(v[j]);
+            }
           } else {
             float* crow = reinterpret_cast<float*>(g.C) + (int64_t)row * g.ldc;
             if (cbase + 32 <= g.N) {
@@ -426,7 +454,7 @@ int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
   return AK_OK;
 }
 
-constexpr size_t kSmem = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+constexpr size_t kSmem = (size_t)STAGES * STAGE_BYTES + 1024 + 256 + 2 * 32 * kTPitch * 2;
 
 template <typename T, int EPI>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
@@ -453,7 +481,8 @@ struct Ws {
   size_t bytes;
 };
 
-int64_t chunk_rows(int64_t N) { return std::min<int64_t>(N, 8192); }
+// Rows per gradient chunk: large chunks keep the dH / dW GEMMs several waves deep.
+int64_t chunk_rows(int64_t N) { return std::min<int64_t>(N, 32768); }
 
 Ws carve(void* base, int64_t N, int64_t D, int64_t V) {
   Ws w{};
@@ -466,7 +495,7 @@ Ws carve(void* base, int64_t N, int64_t D, int64_t V) {
     off += bytes;
     return p;
   };
-  w.part = reinterpret_cast<float2*>(take((size_t)N * ntiles * sizeof(float2)));
+  w.part = reinterpret_cast<float2*>(take((size_t)N * ntiles * 2 * sizeof(float2)));  // one per column half
   w.tlogit = reinterpret_cast<float*>(take((size_t)N * 4));
   w.losses = reinterpret_cast<float*>(take((size_t)N * 4));
   w.inv_valid = reinterpret_cast<float*>(take(4));
@@ -506,7 +535,7 @@ int run(float* loss, float* lse, void* dH, void* dW, const Ws& w, const void* H,
   }
   // 2. lse, per-row loss, mean and 1/n_valid on the device
   lce_rows_reduce<<<(unsigned)((N * 32 + 255) / 256), 256, 0, st>>>(lse, w.losses, w.part, w.tlogit, labels, (int)N,
-                                                                    ntiles, ignore_index);
+                                                                    2 * ntiles, ignore_index);
   lce_mean<<<1, 1024, 0, st>>>(loss, w.inv_valid, w.losses, labels, N, ignore_index);
   AK_CHECK_LAUNCH("linear_ce: reduce");
   // 3-4. per row chunk: G tiles, dH = G W, dW += G^T H

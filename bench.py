@@ -266,7 +266,7 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
                       f"of the same sample"}
 
 
-def time_other_ops(dev, steps, warmup, hbm_peak):
+def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak):
     """Device-timed GB/s of the other swapped ops at their BASELINE configs."""
     from kernels import _ak
     res = {}
@@ -330,6 +330,32 @@ def time_other_ops(dev, steps, warmup, hbm_peak):
     timeit(lambda: _ak.softmax_bwd(y, dys), 3 * T, "softmax_bwd_bf16_196608x2048", steps)
     del s, dys, y
 
+    # Fused linear + CE (config 2): H [32768, 768], W [50304, 768] bf16, 5% ignored.
+    # Algorithmic FLOPs 3 * 2NDV (logits, dH, dW); the kernel executes 4 * 2NDV (logits recomputed).
+    Nt, Dh, Vv = 32768, 768, 50304
+    g = torch.Generator().manual_seed(0)
+    H = torch.randn(Nt, Dh, generator=g).to(torch.bfloat16).to(dev)
+    W = (torch.randn(Vv, Dh, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    lab = torch.randint(0, 50257, (Nt,), generator=g)
+    lab[torch.randperm(Nt, generator=g)[: Nt // 20]] = -100
+    lab = lab.to(dev)
+    flops = 3 * 2 * Nt * Dh * Vv
+    timeit(lambda: _ak.linear_ce_fwdbwd(H, W, lab, -100), 1, "linear_ce_fused_tcgen05_bf16_32768x768x50304",
+           max(2, steps // 4))
+    ms = res["linear_ce_fused_tcgen05_bf16_32768x768x50304"]["ms"]
+    tf = flops / (ms / 1e3) / 1e12
+    res["linear_ce_fused_tcgen05_bf16_32768x768x50304"] = {
+        "ms": ms, "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / bf16_peak, 3),
+        "executed_TFLOP/s": round(tf * 4 / 3, 1), "note": "algorithmic 3*2NDV; executes 4*2NDV (recompute)"}
+    from kernels.hip.chunked_linear_cross_entropy import _ChunkedLinearCrossEntropy
+    timeit(lambda: _ChunkedLinearCrossEntropy.apply(H.requires_grad_(True), W.requires_grad_(True), lab, 4096, 0.0,
+                                                    -100, 0.0, 0.0), 1, "linear_ce_chunked_cublas_bf16", 2)
+    ms2 = res["linear_ce_chunked_cublas_bf16"]["ms"]
+    res["linear_ce_chunked_cublas_bf16"] = {"ms": ms2, "TFLOP/s": round(flops / (ms2 / 1e3) / 1e12, 1),
+                                            "note": "library comparator: cuBLAS GEMMs + CE row kernel, 4096-row chunks"}
+    del H, W, lab
+    torch.cuda.empty_cache()
+
     # Collapsed scan fp32 (8, 2048, 1536): 100 MB per tensor.
     Bsz, L, d = 8, 2048, 1536
     dA = torch.rand(Bsz, L, d, device=dev) * 0.5 + 0.5
@@ -377,6 +403,10 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     hbm_peak, tf_peak, peak_kind = peaks()
+    if args.only_ops:
+        if rank == 0:
+            print(json.dumps({"ops": time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak)}), flush=True)
+        return
     cfg = dict(HEADLINE)
     if args.batch:
         cfg["batch"] = args.batch  # profiling / small-case runs only
@@ -395,7 +425,7 @@ def run_ours(args, world, rank, local):
         e2e_ms, h2d, d2h = time_sscan_e2e(cfg, dev, max(2, args.steps // 2), 2, host)
         e2e_ms = max_over_ranks(e2e_ms, world, dev)
         e2e_value = round(world * (fwd_b + bwd_b) / (e2e_ms / 1e3) / 1e9, 2)
-    ops = time_other_ops(dev, args.steps, args.warmup, hbm_peak) if (rank == 0 and not args.no_ops) else None
+    ops = time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak) if (rank == 0 and not args.no_ops) else None
     train = None if args.no_train else time_train(dev, args.train_steps, 3, world, rank)
     if rank != 0:
         return
@@ -473,6 +503,7 @@ def main():
     ap.add_argument("--no-train", action="store_true", help="skip the 124M hybrid training step")
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
     ap.add_argument("--batch", type=int, default=0, help="override the headline batch (small-case profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
