@@ -236,6 +236,26 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int c = eg * kHalf; c < (eg + 1) * kHalf; c += 32) {
           float v[32];
           tmem_ld32(tbase + (uint32_t)c, v);
+          if (g.G != nullptr) {
+            // logits kept in 16 bits for the gradient pass; the statistics use the
+            // same rounded values so that softmax and lse stay consistent
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = to_f<T>(from_f<T>(v[j]));
+            const int cbase = col0 + c;
+            T* lrow = reinterpret_cast<T*>(g.G) + (int64_t)row * g.N;
+            if (rv && cbase + 32 <= g.N) {
+#pragma unroll
+              for (int q = 0; q < 32; q += 8) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = v[q + e];
+                store_frag<T, 8>(lrow + cbase + q, f);
+              }
+            } else if (rv) {
+              for (int j = 0; j < 32; ++j)
+                if (cbase + j < g.N) lrow[cbase + j] = from_f<T>(v[j]);
+            }
+          }
           float lm = -INFINITY;
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -418,6 +438,32 @@ __global__ void transpose16(T* __restrict__ out, const T* __restrict__ in, int64
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int64_t c = c0 + i, r = r0 + threadIdx.x;
     if (r < R && c < Cc) out[c * R + r] = tile[threadIdx.x][i];
+  }
+}
+
+// In place over 16-bit logits L[M][V]: L = (softmax(L) - onehot(label)) / n_valid,
+// zero rows for ignored labels.  V % 8 == 0, so each 8-element vector is in one row.
+template <typename T>
+__global__ void __launch_bounds__(256)
+lce_grad_inplace(T* __restrict__ L, const float* __restrict__ lse, const int64_t* __restrict__ labels,
+                 const float* __restrict__ inv_valid, int64_t M, int64_t V, int64_t ignore_index) {
+  const float sc0 = *inv_valid;
+  const int64_t nvec = M * V / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = i * 8;
+    const int64_t row = e / V, col = e - row * V;
+    const int64_t lab = labels[row];
+    const float sc = (lab == ignore_index) ? 0.f : sc0;
+    const float l2 = lse[row] * kLog2e;
+    float f[8];
+    load_frag<T, 8>(f, L + e);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float gv = ex2(fmaf(f[k], kLog2e, -l2)) * sc;
+      if (col + k == lab) gv -= sc;
+      f[k] = gv;
+    }
+    store_frag<T, 8>(L + e, f);
   }
 }
 
@@ -614,4 +660,54 @@ extern "C" int ak_linear_ce_fwdbwd(float* loss, float* lse, void* dH, void* dW, 
   cudaStream_t st = (cudaStream_t)stream;
   if (dt == AK_BF16) return run<__nv_bfloat16>(loss, lse, dH, dW, w, H, W, labels, N, D, V, ignore_index, st);
   return run<__half>(loss, lse, dH, dW, w, H, W, labels, N, D, V, ignore_index, st);
+}
+
+extern "C" int ak_linear_ce_logits_grad_workspace_size(int64_t N, int64_t V, size_t* bytes) {
+  clear_error();
+  AK_REQUIRE(bytes != nullptr && N > 0 && V > 0, AK_ERR_ARG, "linear_ce: bad args");
+  const int64_t ntiles = (V + BN - 1) / BN;
+  *bytes = (size_t)N * ntiles * 2 * sizeof(float2) + (size_t)N * 8 + 1024;
+  return AK_OK;
+}
+
+extern "C" int ak_linear_ce_logits_grad(float* loss, float* lse, void* G, void* workspace, size_t ws_bytes,
+                                        const void* H, const void* W, const int64_t* labels, int64_t N, int64_t D,
+                                        int64_t V, int64_t ignore_index, int dt, void* stream) {
+  clear_error();
+  int rc = check_shape(N, D, V, dt);
+  if (rc) return rc;
+  AK_REQUIRE(loss && lse && G && H && W && labels, AK_ERR_ARG, "ak_linear_ce_logits_grad: null pointer");
+  AK_REQUIRE(aligned16(H) && aligned16(W) && aligned16(G), AK_ERR_ARG, "ak_linear_ce_logits_grad: unaligned");
+  size_t need = 0;
+  ak_linear_ce_logits_grad_workspace_size(N, V, &need);
+  AK_REQUIRE(workspace && ws_bytes >= need, AK_ERR_WORKSPACE, "ak_linear_ce_logits_grad: workspace %zu < %zu",
+             ws_bytes, need);
+  const int ntiles = (int)((V + BN - 1) / BN);
+  char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
+  float2* part = reinterpret_cast<float2*>(base);
+  float* tlogit = reinterpret_cast<float*>(part + (size_t)N * ntiles * 2);
+  float* losses = tlogit + N;
+  float* inv_valid = losses + N;  // one float after the per-row losses
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool bf16 = dt == AK_BF16;
+  CUtensorMap tH, tW;
+  if ((rc = make_tmap(&tH, H, N, D, BM, bf16))) return rc;
+  if ((rc = make_tmap(&tW, W, V, D, BN, bf16))) return rc;
+  GemmArgs g{};
+  g.M = (int)N; g.N = (int)V; g.K = (int)D;
+  g.part = part; g.tlogit = tlogit; g.labels = labels; g.ignore_index = ignore_index; g.G = G;
+  if (bf16) rc = launch_gemm<__nv_bfloat16, EPI_STATS>(tH, tW, g, st);
+  else rc = launch_gemm<__half, EPI_STATS>(tH, tW, g, st);
+  if (rc) return rc;
+  lce_rows_reduce<<<(unsigned)((N * 32 + 255) / 256), 256, 0, st>>>(lse, losses, part, tlogit, labels, (int)N,
+                                                                    2 * ntiles, ignore_index);
+  lce_mean<<<1, 1024, 0, st>>>(loss, inv_valid, losses, labels, N, ignore_index);
+  const unsigned grid = (unsigned)std::min<int64_t>((N * V / 8 + 255) / 256, (int64_t)sm_count() * 16);
+  if (bf16)
+    lce_grad_inplace<__nv_bfloat16><<<grid, 256, 0, st>>>((__nv_bfloat16*)G, lse, labels, inv_valid, N, V,
+                                                         ignore_index);
+  else
+    lce_grad_inplace<__half><<<grid, 256, 0, st>>>((__half*)G, lse, labels, inv_valid, N, V, ignore_index);
+  AK_CHECK_LAUNCH("ak_linear_ce_logits_grad");
+  return AK_OK;
 }

@@ -35,6 +35,8 @@ SIGNATURES = {
     "ak_ce_rows_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _f, _i, _vp],
     "ak_ce_rows_reduce": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp],
     "ak_ce_inv_valid": [_vp, _vp, _i64, _i64, _vp],
+    "ak_linear_ce_logits_grad_workspace_size": [_i64, _i64, ctypes.POINTER(_sz)],
+    "ak_linear_ce_logits_grad": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_linear_ce_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_linear_ce_fwdbwd": [_vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_scan1_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
@@ -251,6 +253,25 @@ def linear_ce_supported(hidden: torch.Tensor, weight: torch.Tensor) -> bool:
     V = weight.shape[0]
     return (hidden.dtype in (torch.bfloat16, torch.float16) and weight.dtype == hidden.dtype
             and N % 8 == 0 and D % 8 == 0 and V % 8 == 0 and N > 0)
+
+
+def linear_ce_logits_grad(hidden, weight, labels, ignore_index=-100):
+    """tcgen05 logits GEMM with fused softmax statistics, then G = dloss/dlogits in place.
+    Returns (loss 0-d fp32, lse [N] fp32, G [N, V] in hidden's dtype)."""
+    dev = require_cuda(hidden, weight, labels)
+    h = hidden.contiguous()
+    w = weight.contiguous()
+    lab = labels.to(torch.int64).contiguous()
+    N, D = h.shape
+    V = w.shape[0]
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    lse = torch.empty(N, dtype=torch.float32, device=dev)
+    G = torch.empty(N, V, dtype=h.dtype, device=dev)
+    ws_bytes = _size_query("ak_linear_ce_logits_grad_workspace_size", N, V)
+    ws = workspace(ws_bytes, dev)
+    call("ak_linear_ce_logits_grad", ptr(loss), ptr(lse), ptr(G), ptr(ws), ws_bytes, ptr(h), ptr(w), ptr(lab), N, D,
+         V, int(ignore_index), dtype_code(h), stream(dev))
+    return loss, lse, G
 
 
 def linear_ce_fwdbwd(hidden, weight, labels, ignore_index=-100, need_dh=True, need_dw=True):

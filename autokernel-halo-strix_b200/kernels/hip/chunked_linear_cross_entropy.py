@@ -81,9 +81,14 @@ class _FusedLinearCrossEntropy(torch.autograd.Function):
     @staticmethod
     @custom_fwd(device_type="cuda")
     def forward(ctx, hidden, weight, targets, ignore_index):
-        w = weight.to(hidden.dtype)
-        loss, _lse, dh, dw = _ak.linear_ce_fwdbwd(hidden, w, targets, ignore_index, need_dh=hidden.requires_grad,
-                                                   need_dw=weight.requires_grad)
+        w = weight.to(hidden.dtype).contiguous()
+        h = hidden.contiguous()
+        # fused tcgen05 logits GEMM + softmax statistics + in-place dlogits; the two
+        # gradient contractions are plain GEMMs (cuBLAS)
+        loss, _lse, G = _ak.linear_ce_logits_grad(h, w, targets, ignore_index)
+        dh = torch.mm(G, w) if hidden.requires_grad else None
+        dw = torch.mm(G.t(), h) if weight.requires_grad else None
+        del G
         ctx.save_for_backward(dh, dw.to(weight.dtype) if dw is not None else None)
         ctx.req = (hidden.requires_grad, weight.requires_grad)
         return loss

@@ -347,7 +347,14 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak):
     res["linear_ce_fused_tcgen05_bf16_32768x768x50304"] = {
         "ms": ms, "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / bf16_peak, 3),
         "executed_TFLOP/s": round(tf * 4 / 3, 1), "note": "algorithmic 3*2NDV; executes 4*2NDV (recompute)"}
-    from kernels.hip.chunked_linear_cross_entropy import _ChunkedLinearCrossEntropy
+    from kernels.hip.chunked_linear_cross_entropy import _ChunkedLinearCrossEntropy, _FusedLinearCrossEntropy
+    timeit(lambda: _FusedLinearCrossEntropy.apply(H.requires_grad_(True), W.requires_grad_(True), lab, -100), 1,
+           "linear_ce_module", max(2, steps // 4))
+    ms3 = res["linear_ce_module"]["ms"]
+    tf3 = flops / (ms3 / 1e3) / 1e12
+    res["linear_ce_module"] = {"ms": ms3, "TFLOP/s": round(tf3, 1), "frac_bf16": round(tf3 / bf16_peak, 3),
+                               "note": "ChunkedLinearCrossEntropyLoss path: tcgen05 logits GEMM with fused softmax "
+                                       "statistics + in-place dlogits, then dH/dW as cuBLAS GEMMs"}
     timeit(lambda: _ChunkedLinearCrossEntropy.apply(H.requires_grad_(True), W.requires_grad_(True), lab, 4096, 0.0,
                                                     -100, 0.0, 0.0), 1, "linear_ce_chunked_cublas_bf16", 2)
     ms2 = res["linear_ce_chunked_cublas_bf16"]["ms"]

@@ -165,6 +165,21 @@ AK_API int ak_linear_ce_fwdbwd(float* loss, float* lse, void* dH, void* dW, void
                    int64_t N, int64_t D, int64_t V, int64_t ignore_index, int dt,
                    void* stream);
 
+/* Workspace bytes for ak_linear_ce_logits_grad. */
+AK_API int ak_linear_ce_logits_grad_workspace_size(int64_t N, int64_t V, size_t* bytes);
+
+/* Forward half of the fused linear + CE for callers that run the two gradient
+ * GEMMs themselves: the tcgen05 logits GEMM writes G[N, V] (dt, caller buffer)
+ * and per-row softmax statistics in its epilogue; then loss[0], lse[N] and, in
+ * place, G = (softmax - onehot) / n_valid (zero rows for ignored labels).
+ * dH = G W and dW = G^T H are plain GEMMs.
+ * Replaces the per-chunk F.linear + cross_entropy_fwd_hip of
+ * _ChunkedLinearCrossEntropy.forward (kernels/hip/chunked_linear_cross_entropy.py:95-110). */
+AK_API int ak_linear_ce_logits_grad(float* loss, float* lse, void* G, void* workspace,
+                   size_t ws_bytes, const void* H, const void* W, const int64_t* labels,
+                   int64_t N, int64_t D, int64_t V, int64_t ignore_index, int dt,
+                   void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Collapsed (single-state) selective scan, fp32, layout (B, L, d)
  * ------------------------------------------------------------------------ */

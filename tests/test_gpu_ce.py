@@ -122,3 +122,21 @@ def test_fused_linear_ce_module_autograd():
     assert abs(loss.item() - rl.item()) < 2e-3 * abs(rl.item())
     assert_lowp_close(Hc.grad, 2 * rdh, what="dH")
     assert_lowp_close(Wc.grad, 2 * rdw, what="dW")
+
+
+@pytest.mark.parametrize("N,D,V", [(1024, 256, 32768), (200, 72, 1000), (8, 64, 8)])
+def test_linear_ce_logits_grad(N, D, V):
+    from kernels import _ak
+    g = torch.Generator().manual_seed(N + V)
+    H = torch.randn(N, D, generator=g).to(torch.bfloat16)
+    W = (torch.randn(V, D, generator=g) * 0.05).to(torch.bfloat16)
+    lab = torch.randint(0, V, (N,), generator=g)
+    lab[::5] = -100
+    loss, lse, G = _ak.linear_ce_logits_grad(H.to(DEV), W.to(DEV), lab.to(DEV), -100)
+    x = H.double() @ W.double().t()
+    n = (lab != -100).sum().item()
+    _, rlse, rg = O.ce_rows(x, lab, scale=1.0 / n)
+    assert_fp32_close(lse, rlse, rtol=2e-3, what="lse")
+    assert_lowp_close(G.float() * n, rg * n, what="G")
+    rl, _, _ = O.linear_ce(H, W, lab)
+    assert abs(loss.item() - rl.item()) <= 3e-3 * max(1.0, abs(rl.item()))
