@@ -131,6 +131,8 @@ def setup_dist():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1 and not dist.is_initialized():
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
             dist.init_process_group("nccl", device_id=torch.device("cuda", local))
@@ -412,7 +414,7 @@ def run_ours(args, world, rank, local):
     hbm_peak, tf_peak, peak_kind = peaks()
     if args.only_ops:
         if rank == 0:
-            print(json.dumps({"ops": time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak)}), flush=True)
+            emit({"ops": time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak)})
         return
     cfg = dict(HEADLINE)
     if args.batch:
@@ -473,7 +475,7 @@ def run_ours(args, world, rank, local):
         line["train"] = train
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_sscan_sample()
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_reference(args, world, rank):
@@ -496,10 +498,25 @@ def run_reference(args, world, rank):
             "config": {"workload": "mamba selective_scan fwd+bwd, bounded CPU sample of B=8 D=1536 L=2048 N=16"},
             "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+# The JSON result goes to the original stdout; everything else the process writes
+# to fd 1 (library banners such as NCCL's version line) is sent to stderr.
+_JSON_OUT = None
+
+
+def emit(obj) -> None:
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
 
 
 def main():
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
