@@ -268,11 +268,15 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
                       f"of the same sample"}
 
 
-def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak):
-    """Device-timed GB/s of the other swapped ops at their BASELINE configs."""
+def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768):
+    """Device-timed throughput of the other swapped ops at their BASELINE configs.
+    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1"} (None = all)."""
     from kernels import _ak
     res = {}
     st = torch.cuda.current_stream(dev)
+
+    def want(name):
+        return which is None or name in which
 
     def timeit(fn, nbytes, name, reps):
         for _ in range(warmup):
@@ -288,93 +292,87 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak):
         gbs = nbytes / ms / 1e6
         res[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3)}
 
-    # RMSNorm fp32 [8192, 768] (config 0); rows > L2 is false here (25 MB), so a 256 MB
-    # scratch write flushes L2 between repetitions and is excluded by timing fwd/bwd separately.
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn(8192, 768, generator=g).to(dev)
-    w = (1 + 0.02 * torch.randn(768, generator=g)).to(dev)
-    dy = torch.randn(8192, 768, generator=g).to(dev)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    E = 8192 * 768
-    fw_b, bw_b = 2 * E * 4 + 768 * 4, 3 * E * 4 + 2 * 768 * 4
+    if want("rmsnorm"):
+        # RMSNorm fp32 [8192, 768] (config 0): 25 MB per tensor < L2, so a 256 MB scratch
+        # write flushes L2 before each repetition and its own time is subtracted.
+        g = torch.Generator().manual_seed(0)
+        x = torch.randn(8192, 768, generator=g).to(dev)
+        w = (1 + 0.02 * torch.randn(768, generator=g)).to(dev)
+        dy = torch.randn(8192, 768, generator=g).to(dev)
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        E = 8192 * 768
+        fw_b, bw_b = 2 * E * 4 + 768 * 4, 3 * E * 4 + 2 * 768 * 4
+        timeit(lambda: flush.zero_(), 1, "_flush", steps * 4)
+        fl = res.pop("_flush")["ms"]
+        timeit(lambda: (flush.zero_(), _ak.rmsnorm_fwd(x, w, 1e-6)), fw_b, "rmsnorm_fwd_fp32_8192x768", steps * 4)
+        timeit(lambda: (flush.zero_(), _ak.rmsnorm_bwd(x, w, dy, 1e-6)), bw_b, "rmsnorm_bwd_fp32_8192x768", steps * 4)
+        for k, nb in (("rmsnorm_fwd_fp32_8192x768", fw_b), ("rmsnorm_bwd_fp32_8192x768", bw_b)):
+            ms = max(res[k]["ms"] - fl, 1e-6)
+            gbs = nb / ms / 1e6
+            res[k] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
+                      "note": "L2 flushed (256 MB write) before each rep; flush time subtracted"}
+        del x, dy, flush
 
-    def rms_f():
-        flush.zero_()
-        _ak.rmsnorm_fwd(x, w, 1e-6)
+    if want("softmax"):
+        # Softmax causal scores bf16 [96*2048, 2048] (config 3): 805 MB per tensor > L2.
+        rows, cols = 96 * 2048, 2048
+        s = (torch.randn(rows, cols, device=dev) / 8).to(torch.bfloat16)
+        r = torch.arange(rows, device=dev) % cols
+        s.masked_fill_(torch.arange(cols, device=dev)[None, :] > r[:, None], float("-inf"))
+        dys = torch.randn(rows, cols, device=dev).to(torch.bfloat16)
+        y = _ak.softmax_fwd(s)
+        T = rows * cols * 2
+        timeit(lambda: _ak.softmax_fwd(s), 2 * T, "softmax_fwd_bf16_196608x2048", steps)
+        timeit(lambda: _ak.softmax_bwd(y, dys), 3 * T, "softmax_bwd_bf16_196608x2048", steps)
+        del s, dys, y
 
-    def rms_b():
-        flush.zero_()
-        _ak.rmsnorm_bwd(x, w, dy, 1e-6)
+    if want("linear_ce"):
+        # Fused linear + CE (config 2): H [32768, 768], W [50304, 768] bf16, 5% ignored.
+        # Algorithmic FLOPs 3 * 2NDV (logits, dH, dW).
+        Nt, Dh, Vv = ce_rows, 768, 50304
+        g = torch.Generator().manual_seed(0)
+        H = torch.randn(Nt, Dh, generator=g).to(torch.bfloat16).to(dev)
+        W = (torch.randn(Vv, Dh, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+        lab = torch.randint(0, 50257, (Nt,), generator=g)
+        lab[torch.randperm(Nt, generator=g)[: Nt // 20]] = -100
+        lab = lab.to(dev)
+        flops = 3 * 2 * Nt * Dh * Vv
+        tag = f"bf16_{Nt}x{Dh}x{Vv}"
+        from kernels.hip.chunked_linear_cross_entropy import _ChunkedLinearCrossEntropy, _FusedLinearCrossEntropy
+        timeit(lambda: _FusedLinearCrossEntropy.apply(H.requires_grad_(True), W.requires_grad_(True), lab, -100), 1,
+               "linear_ce_module", max(2, steps // 4))
+        ms3 = res.pop("linear_ce_module")["ms"]
+        tf3 = flops / (ms3 / 1e3) / 1e12
+        res[f"linear_ce_{tag}"] = {
+            "ms": ms3, "TFLOP/s": round(tf3, 1), "frac_bf16": round(tf3 / bf16_peak, 3),
+            "note": "ChunkedLinearCrossEntropyLoss path: tcgen05 logits GEMM with fused softmax statistics and "
+                    "in-place dlogits, then dH/dW as plain cuBLAS GEMMs; algorithmic 3*2NDV"}
+        timeit(lambda: _ak.linear_ce_fwdbwd(H, W, lab, -100), 1, "x", max(2, steps // 4))
+        ms = res.pop("x")["ms"]
+        tf = flops / (ms / 1e3) / 1e12
+        res[f"linear_ce_all_tcgen05_{tag}"] = {
+            "ms": ms, "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / bf16_peak, 3),
+            "note": "ak_linear_ce_fwdbwd: all four GEMMs on our tcgen05 kernel (logits recomputed for G)"}
+        timeit(lambda: _ChunkedLinearCrossEntropy.apply(H.requires_grad_(True), W.requires_grad_(True), lab, 4096,
+                                                        0.0, -100, 0.0, 0.0), 1, "x", 2)
+        ms2 = res.pop("x")["ms"]
+        res[f"linear_ce_chunked_cublas_{tag}"] = {
+            "ms": ms2, "TFLOP/s": round(flops / (ms2 / 1e3) / 1e12, 1),
+            "note": "library comparator: cuBLAS GEMMs around the CE row kernel, 4096-row chunks"}
+        del H, W, lab
+        torch.cuda.empty_cache()
 
-    def flush_only():
-        flush.zero_()
-
-    timeit(flush_only, 1, "_flush", steps * 4)
-    fl = res.pop("_flush")["ms"]
-    timeit(rms_f, fw_b, "rmsnorm_fwd_fp32_8192x768", steps * 4)
-    timeit(rms_b, bw_b, "rmsnorm_bwd_fp32_8192x768", steps * 4)
-    for k, nb in (("rmsnorm_fwd_fp32_8192x768", fw_b), ("rmsnorm_bwd_fp32_8192x768", bw_b)):
-        ms = max(res[k]["ms"] - fl, 1e-6)
-        gbs = nb / ms / 1e6
-        res[k] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
-                  "note": "L2 flushed (256 MB write) before each rep; flush time subtracted"}
-    del x, dy, flush
-
-    # Softmax causal scores bf16 [96*2048, 2048] (config 3): 805 MB per tensor > L2.
-    rows, cols = 96 * 2048, 2048
-    s = (torch.randn(rows, cols, device=dev) / 8).to(torch.bfloat16)
-    r = torch.arange(rows, device=dev) % cols
-    s.masked_fill_(torch.arange(cols, device=dev)[None, :] > r[:, None], float("-inf"))
-    dys = torch.randn(rows, cols, device=dev).to(torch.bfloat16)
-    y = _ak.softmax_fwd(s)
-    T = rows * cols * 2
-    timeit(lambda: _ak.softmax_fwd(s), 2 * T, "softmax_fwd_bf16_196608x2048", steps)
-    timeit(lambda: _ak.softmax_bwd(y, dys), 3 * T, "softmax_bwd_bf16_196608x2048", steps)
-    del s, dys, y
-
-    # Fused linear + CE (config 2): H [32768, 768], W [50304, 768] bf16, 5% ignored.
-    # Algorithmic FLOPs 3 * 2NDV (logits, dH, dW); the kernel executes 4 * 2NDV (logits recomputed).
-    Nt, Dh, Vv = 32768, 768, 50304
-    g = torch.Generator().manual_seed(0)
-    H = torch.randn(Nt, Dh, generator=g).to(torch.bfloat16).to(dev)
-    W = (torch.randn(Vv, Dh, generator=g) * 0.02).to(torch.bfloat16).to(dev)
-    lab = torch.randint(0, 50257, (Nt,), generator=g)
-    lab[torch.randperm(Nt, generator=g)[: Nt // 20]] = -100
-    lab = lab.to(dev)
-    flops = 3 * 2 * Nt * Dh * Vv
-    timeit(lambda: _ak.linear_ce_fwdbwd(H, W, lab, -100), 1, "linear_ce_fused_tcgen05_bf16_32768x768x50304",
-           max(2, steps // 4))
-    ms = res["linear_ce_fused_tcgen05_bf16_32768x768x50304"]["ms"]
-    tf = flops / (ms / 1e3) / 1e12
-    res["linear_ce_fused_tcgen05_bf16_32768x768x50304"] = {
-        "ms": ms, "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / bf16_peak, 3),
-        "executed_TFLOP/s": round(tf * 4 / 3, 1), "note": "algorithmic 3*2NDV; executes 4*2NDV (recompute)"}
-    from kernels.hip.chunked_linear_cross_entropy import _ChunkedLinearCrossEntropy, _FusedLinearCrossEntropy
-    timeit(lambda: _FusedLinearCrossEntropy.apply(H.requires_grad_(True), W.requires_grad_(True), lab, -100), 1,
-           "linear_ce_module", max(2, steps // 4))
-    ms3 = res["linear_ce_module"]["ms"]
-    tf3 = flops / (ms3 / 1e3) / 1e12
-    res["linear_ce_module"] = {"ms": ms3, "TFLOP/s": round(tf3, 1), "frac_bf16": round(tf3 / bf16_peak, 3),
-                               "note": "ChunkedLinearCrossEntropyLoss path: tcgen05 logits GEMM with fused softmax "
-                                       "statistics + in-place dlogits, then dH/dW as cuBLAS GEMMs"}
-    timeit(lambda: _ChunkedLinearCrossEntropy.apply(H.requires_grad_(True), W.requires_grad_(True), lab, 4096, 0.0,
-                                                    -100, 0.0, 0.0), 1, "linear_ce_chunked_cublas_bf16", 2)
-    ms2 = res["linear_ce_chunked_cublas_bf16"]["ms"]
-    res["linear_ce_chunked_cublas_bf16"] = {"ms": ms2, "TFLOP/s": round(flops / (ms2 / 1e3) / 1e12, 1),
-                                            "note": "library comparator: cuBLAS GEMMs + CE row kernel, 4096-row chunks"}
-    del H, W, lab
-    torch.cuda.empty_cache()
-
-    # Collapsed scan fp32 (8, 2048, 1536): 100 MB per tensor.
-    Bsz, L, d = 8, 2048, 1536
-    dA = torch.rand(Bsz, L, d, device=dev) * 0.5 + 0.5
-    dBx, C, xx, gy = (torch.randn(Bsz, L, d, device=dev) for _ in range(4))
-    Dv = torch.randn(d, device=dev)
-    E = Bsz * L * d
-    timeit(lambda: _ak.scan1_fwd(dA, dBx, C, Dv, xx), 20 * E, "scan1_fwd_fp32_8x2048x1536", steps)
-    timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy), 36 * E, "scan1_bwd_fp32_8x2048x1536", steps)
-    del dA, dBx, C, xx, gy
-    torch.cuda.empty_cache()
+    if want("scan1"):
+        # Collapsed scan fp32 (8, 2048, 1536): 100 MB per tensor.
+        Bsz, L, d = 8, 2048, 1536
+        dA = torch.rand(Bsz, L, d, device=dev) * 0.5 + 0.5
+        dBx, C, xx, gy = (torch.randn(Bsz, L, d, device=dev) for _ in range(4))
+        Dv = torch.randn(d, device=dev)
+        E = Bsz * L * d
+        timeit(lambda: _ak.scan1_fwd(dA, dBx, C, Dv, xx), 20 * E, "scan1_fwd_fp32_8x2048x1536", steps)
+        timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy), 36 * E, "scan1_bwd_fp32_8x2048x1536", steps)
+        del dA, dBx, C, xx, gy
+        torch.cuda.empty_cache()
     return res
 
 
@@ -414,7 +412,9 @@ def run_ours(args, world, rank, local):
     hbm_peak, tf_peak, peak_kind = peaks()
     if args.only_ops:
         if rank == 0:
-            emit({"ops": time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak)})
+            emit({"ops": time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak,
+                                        which=set(args.ops.split(",")) if args.ops else None,
+                                        ce_rows=args.ce_rows)})
         return
     cfg = dict(HEADLINE)
     if args.batch:
@@ -528,6 +528,8 @@ def main():
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
+    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1")
+    ap.add_argument("--ce-rows", type=int, default=32768, help="with --only-ops: rows of the linear+CE case")
     ap.add_argument("--batch", type=int, default=0, help="override the headline batch (small-case profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
