@@ -64,6 +64,10 @@ softmax_fwd_warp(T* __restrict__ y, const T* __restrict__ x, int64_t rows, int c
   }
 }
 
+// Two passes over the row: the first reduces sum(dy*y), the second re-reads
+// y and dy (L1/L2 hits, the row was just read) and writes dx.  Keeping no row
+// in registers leaves room for many resident warps, which is what a pure
+// streaming kernel needs to cover HBM latency.
 template <typename T, int VEC, int NIT>
 __global__ void __launch_bounds__(kWarps * 32)
 softmax_bwd_warp(T* __restrict__ dx, const T* __restrict__ y, const T* __restrict__ dy,
@@ -71,29 +75,30 @@ softmax_bwd_warp(T* __restrict__ dx, const T* __restrict__ y, const T* __restric
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < rows; row += (int64_t)gridDim.x * kWarps) {
-    float yv[NIT][VEC], gv[NIT][VEC];
+    const T* yr = y + row * cols;
+    const T* gr = dy + row * cols;
     float s = 0.f;
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
       if (c < cols) {
-        load_frag_stream<T, VEC>(yv[it], y + row * cols + c);
-        load_frag_stream<T, VEC>(gv[it], dy + row * cols + c);
-      } else {
+        float yv[VEC], gv[VEC];
+        load_frag<T, VEC>(yv, yr + c);
+        load_frag<T, VEC>(gv, gr + c);
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) { yv[it][k] = 0.f; gv[it][k] = 0.f; }
+        for (int k = 0; k < VEC; ++k) s = fmaf(yv[k], gv[k], s);
       }
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) s = fmaf(yv[it][k], gv[it][k], s);
     }
     s = warp_sum(s);
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
       if (c < cols) {
-        float o[VEC];
+        float yv[VEC], gv[VEC], o[VEC];
+        load_frag<T, VEC>(yv, yr + c);
+        load_frag<T, VEC>(gv, gr + c);
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) o[k] = yv[it][k] * (gv[it][k] - s);
+        for (int k = 0; k < VEC; ++k) o[k] = yv[k] * (gv[k] - s);
         store_frag<T, VEC>(dx + row * cols + c, o);
       }
     }
@@ -190,7 +195,6 @@ template <typename T>
 int bwd_impl(void* dx, const void* y, const void* dy, int64_t rows, int cols, cudaStream_t st) {
   constexpr int VEC = 16 / sizeof(T);
   int nit = (cols % VEC == 0 && aligned16(dx) && aligned16(y) && aligned16(dy)) ? pick_nit(cols, VEC) : 0;
-  if (nit * VEC > 64) nit = 0;  // y and dy both in registers: wider rows would spill
   if (nit > 0) {
     AK_SMX_NIT_SWITCH(nit, NIT, softmax_bwd_warp<T, VEC, NIT><<<warp_grid(rows), kWarps * 32, 0, st>>>(
                                     (T*)dx, (const T*)y, (const T*)dy, rows, cols));
