@@ -127,6 +127,8 @@ class MambaBlock(nn.Module):
         self.D = nn.Parameter(torch.ones(self.d_inner))
         self.out_proj = nn.Linear(self.d_inner, d, bias=False)
         self._scan = scan_fn
+        # fused causal conv + SiLU kernel (torch.ops.autokernel.causal_conv1d_silu) when set
+        self.fused_conv = False
 
     def reset_dt(self, generator: Optional[torch.Generator] = None):
         dt_min, dt_max, floor = 1e-3, 1e-1, 1e-4
@@ -141,7 +143,11 @@ class MambaBlock(nn.Module):
         B, T, _ = h.shape
         xz = self.in_proj(h).transpose(1, 2)                    # (B, 2*d_inner, T)
         x, z = xz.chunk(2, dim=1)
-        x = F.silu(self.conv1d(x)[..., :T])
+        if self.fused_conv:
+            x = torch.ops.autokernel.causal_conv1d_silu(x.contiguous(), self.conv1d.weight.squeeze(1),
+                                                        self.conv1d.bias)
+        else:
+            x = F.silu(self.conv1d(x)[..., :T])
         x_dbl = self.x_proj(x.transpose(1, 2))                  # (B, T, dt_rank + 2N)
         dt, Bm, Cm = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         dt = (dt @ self.dt_proj.weight.t().to(dt.dtype)).transpose(1, 2)   # (B, d_inner, T), bias in the scan

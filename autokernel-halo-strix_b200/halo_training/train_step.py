@@ -16,7 +16,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from halo_training.hybrid_lm import HybridConfig, HybridLM
+from halo_training.hybrid_lm import HybridConfig, HybridLM, MambaBlock
 
 
 def kernel_loss_fn():
@@ -44,6 +44,10 @@ class HybridTrainer:
         if use_kernels:
             import autokernel
             model = autokernel.optimize(model, training=True)
+            import kernels.hip._torch_ops  # noqa: F401  (torch.ops.autokernel.causal_conv1d_silu)
+            for m in model.modules():
+                if isinstance(m, MambaBlock):
+                    m.fused_conv = True
         self.raw = model
         if ddp:
             from torch.nn.parallel import DistributedDataParallel as DDP

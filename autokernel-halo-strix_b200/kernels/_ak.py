@@ -42,6 +42,9 @@ SIGNATURES = {
     "ak_scan1_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ak_scan1_bwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_scan1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "ak_causal_conv1d_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _i, _vp],
+    "ak_causal_conv1d_bwd_workspace_size": [_i64, _i64, _i64, _i64, ctypes.POINTER(_sz)],
+    "ak_causal_conv1d_bwd": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _i, _vp],
     "ak_selective_scan_state_stride": [],
     "ak_selective_scan_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                               _i64, _i64, _i64, _i64, _i64, _i, _vp],
@@ -407,6 +410,44 @@ def selective_scan_bwd(dout, u, delta, A, B, C, D, z, delta_bias, delta_softplus
     if C.dim() == 3:
         dC = dC.squeeze(1)
     return du, ddelta, dA, dB, dC, dD, dz, dbias
+
+
+# ---------------------------------------------------------------------------
+# Depthwise causal conv1d (B, D, T)
+# ---------------------------------------------------------------------------
+def causal_conv1d_fwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                      silu: bool = False) -> torch.Tensor:
+    dev = require_cuda(x, weight, bias)
+    if x.dim() != 3 or weight.dim() != 2 or weight.shape[0] != x.shape[1]:
+        raise ValueError(f"causal_conv1d: x {tuple(x.shape)} / weight {tuple(weight.shape)} mismatch")
+    x = x.contiguous()
+    B, D, T = x.shape
+    K = weight.shape[1]
+    w32 = weight.float().contiguous()
+    b32 = bias.float().contiguous() if bias is not None else None
+    y = torch.empty_like(x)
+    call("ak_causal_conv1d_fwd", ptr(y), ptr(x), ptr(w32), ptr(b32), B, D, T, K, int(bool(silu)), dtype_code(x), stream(dev))
+    return y
+
+
+def causal_conv1d_bwd(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], dy: torch.Tensor,
+                      silu: bool = False):
+    """Returns (dx, dweight fp32 (D, K), dbias fp32 (D) or None)."""
+    dev = require_cuda(x, weight, bias, dy)
+    x = x.contiguous()
+    dy = dy.to(x.dtype).contiguous()
+    B, D, T = x.shape
+    K = weight.shape[1]
+    w32 = weight.float().contiguous()
+    b32 = bias.float().contiguous() if bias is not None else None
+    dx = torch.empty_like(x)
+    dw = torch.empty(D, K, dtype=torch.float32, device=dev)
+    db = torch.empty(D, dtype=torch.float32, device=dev) if bias is not None else None
+    ws_bytes = _size_query("ak_causal_conv1d_bwd_workspace_size", B, D, T, K)
+    ws = workspace(ws_bytes, dev)
+    call("ak_causal_conv1d_bwd", ptr(dx), ptr(dw), ptr(db), ptr(ws), ws_bytes, ptr(x), ptr(w32), ptr(b32), ptr(dy), B, D, T, K, int(bool(silu)), dtype_code(x),
+         stream(dev))
+    return dx, dw, db
 
 
 def exported_symbols() -> Sequence[str]:

@@ -20,7 +20,7 @@ PyTorch backward there; here the backward is always the CUDA custom op, so the
 switch is accepted for compatibility and has no effect.
 """
 import os
-from typing import List, Tuple
+from typing import List, Optional, Tuple
 
 import torch
 
@@ -189,3 +189,72 @@ def _selective_scan_backward(ctx, grad_y):
 
 
 selective_scan_op.register_autograd(_selective_scan_backward, setup_context=_selective_scan_setup)
+
+
+# ---------------------------------------------------------------------------
+# Depthwise causal conv1d — reference _torch_ops.py:883-975
+# (`autokernel::causal_conv1d(x (B, D, T), weight (D, K), bias (D,))`, fake =
+# empty like x, grads (dx, dweight, dbias), autocast rule cuda/fp16).  The
+# reference forward is causal_conv1d_fn or F.pad + F.conv1d(groups=D) and its
+# backward replays that under autograd; here both directions are the CUDA
+# kernels.  `causal_conv1d_silu` (added) fuses the SiLU of the Mamba block.
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::causal_conv1d_bwd", mutates_args=())
+def causal_conv1d_bwd_op(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], grad: torch.Tensor,
+                         silu: bool) -> List[torch.Tensor]:
+    dx, dw, db = _ak.causal_conv1d_bwd(x, weight, bias, grad, silu)
+    out = [dx, dw.to(weight.dtype)]
+    if db is not None:
+        out.append(db.to(bias.dtype))
+    return out
+
+
+@causal_conv1d_bwd_op.register_fake
+def _(x, weight, bias, grad, silu):
+    out = [torch.empty_like(x), torch.empty_like(weight)]
+    if bias is not None:
+        out.append(torch.empty_like(bias))
+    return out
+
+
+def _conv_setup(ctx, inputs, output):
+    x, weight, bias = inputs[:3]
+    ctx.save_for_backward(x, weight, bias)
+
+
+def _conv_backward(ctx, grad_out, silu):
+    x, weight, bias = ctx.saved_tensors
+    g = causal_conv1d_bwd_op(x, weight, bias, grad_out.contiguous(), silu)
+    return g[0], g[1], (g[2] if bias is not None else None)
+
+
+@torch.library.custom_op("autokernel::causal_conv1d", mutates_args=())
+def causal_conv1d_op(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+    return _ak.causal_conv1d_fwd(x, weight, bias, silu=False)
+
+
+@causal_conv1d_op.register_fake
+def _(x, weight, bias):
+    return x.new_empty(x.shape)
+
+
+causal_conv1d_op.register_autograd(lambda ctx, g: _conv_backward(ctx, g, False), setup_context=_conv_setup)
+try:
+    causal_conv1d_op.register_autocast("cuda", torch.float16)
+except AttributeError:  # pragma: no cover - older torch
+    pass
+
+
+@torch.library.custom_op("autokernel::causal_conv1d_silu", mutates_args=())
+def causal_conv1d_silu_op(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
+    return _ak.causal_conv1d_fwd(x, weight, bias, silu=True)
+
+
+@causal_conv1d_silu_op.register_fake
+def _(x, weight, bias):
+    return x.new_empty(x.shape)
+
+
+causal_conv1d_silu_op.register_autograd(lambda ctx, g: _conv_backward(ctx, g, True), setup_context=_conv_setup)

@@ -270,7 +270,7 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
 
 def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768):
     """Device-timed throughput of the other swapped ops at their BASELINE configs.
-    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1"} (None = all)."""
+    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "conv1d"} (None = all)."""
     from kernels import _ak
     res = {}
     st = torch.cuda.current_stream(dev)
@@ -278,14 +278,25 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
     def want(name):
         return which is None or name in which
 
-    def timeit(fn, nbytes, name, reps):
+    def timeit(fn, nbytes, name, reps, graph=False):
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize(dev)
+        run = fn
+        if graph:
+            # short kernels: replay the calls from a CUDA graph so host-side argument
+            # marshalling does not starve the GPU; the graph holds exactly the launches
+            # one call makes
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                fn()
+            run = gr.replay
+            run()
+            torch.cuda.synchronize(dev)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(st)
         for _ in range(reps):
-            fn()
+            run()
         b.record(st)
         torch.cuda.synchronize(dev)
         ms = a.elapsed_time(b) / reps
@@ -372,6 +383,21 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         timeit(lambda: _ak.scan1_fwd(dA, dBx, C, Dv, xx), 20 * E, "scan1_fwd_fp32_8x2048x1536", steps)
         timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy), 36 * E, "scan1_bwd_fp32_8x2048x1536", steps)
         del dA, dBx, C, xx, gy
+        torch.cuda.empty_cache()
+
+    if want("conv1d"):
+        # Depthwise causal conv1d + SiLU bf16 (16, 1536, 2048), K=4 (the Mamba block's
+        # conv at the hybrid model's d_inner): 100 MB per tensor, x + y > L2.
+        Bsz, Dc, T = 16, 1536, 2048
+        xc = torch.randn(Bsz, Dc, T, device=dev).to(torch.bfloat16)
+        dyc = torch.randn(Bsz, Dc, T, device=dev).to(torch.bfloat16)
+        wc, bc = torch.randn(Dc, 4, device=dev), torch.randn(Dc, device=dev)
+        E = Bsz * Dc * T
+        timeit(lambda: _ak.causal_conv1d_fwd(xc, wc, bc, True), 4 * E, "conv1d_silu_fwd_bf16_16x1536x2048", steps,
+               graph=True)
+        timeit(lambda: _ak.causal_conv1d_bwd(xc, wc, bc, dyc, True), 6 * E, "conv1d_silu_bwd_bf16_16x1536x2048",
+               steps, graph=True)
+        del xc, dyc
         torch.cuda.empty_cache()
     return res
 
@@ -528,7 +554,7 @@ def main():
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
-    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1")
+    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,conv1d")
     ap.add_argument("--ce-rows", type=int, default=32768, help="with --only-ops: rows of the linear+CE case")
     ap.add_argument("--batch", type=int, default=0, help="override the headline batch (small-case profiling)")
     args = ap.parse_args()

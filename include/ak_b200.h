@@ -249,6 +249,31 @@ AK_API int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB, vo
                           int64_t batch, int64_t dim, int64_t seqlen,
                           int64_t dstate, int64_t groups, int dt, void* stream);
 
+/* ---- Depthwise causal conv1d (+ optional SiLU) --------------------------
+ * y[b,d,t] = act(bias[d] + sum_k w[d,k] x[b,d,t-K+1+k]), x = 0 before t = 0;
+ * act = SiLU when silu != 0, identity otherwise.  x, y: (B, D, T) dt, T
+ * contiguous; weight: fp32 (D, K), 2 <= K <= 8; bias: fp32 (D) nullable.
+ * Replaces the forward of autokernel::causal_conv1d
+ * (kernels/hip/_torch_ops.py:883-902: F.pad + F.conv1d groups=D, or
+ * causal_conv1d_fn) and causal_conv1d_fn(x, w, b, activation="silu") as
+ * called from the Mamba block. */
+AK_API int ak_causal_conv1d_fwd(void* y, const void* x, const float* weight,
+                                const float* bias, int64_t B, int64_t D,
+                                int64_t T, int64_t K, int silu, int dt,
+                                void* stream);
+
+AK_API int ak_causal_conv1d_bwd_workspace_size(int64_t B, int64_t D, int64_t T,
+                                               int64_t K, size_t* bytes);
+
+/* Gradients of ak_causal_conv1d_fwd: dx (B, D, T) dt; dweight fp32 (D, K);
+ * dbias fp32 (D) nullable.  Deterministic (fixed-order weight reduction).
+ * Replaces _causal_conv1d_shim_backward (kernels/hip/_torch_ops.py:910-965). */
+AK_API int ak_causal_conv1d_bwd(void* dx, float* dweight, float* dbias,
+                                void* workspace, size_t ws_bytes, const void* x,
+                                const float* weight, const float* bias,
+                                const void* dy, int64_t B, int64_t D, int64_t T,
+                                int64_t K, int silu, int dt, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

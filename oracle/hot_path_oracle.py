@@ -210,3 +210,34 @@ def linear_ce(H, W, targets, ignore_index=-100, softcap=0.0, label_smoothing=0.0
     loss = F.cross_entropy(logits, t, ignore_index=ignore_index, label_smoothing=label_smoothing)
     loss.backward()
     return loss.detach(), h.grad, w.grad
+
+
+# ---------------------------------------------------------------------------
+# Depthwise causal conv1d — autokernel::causal_conv1d, kernels/hip/_torch_ops.py:883-902
+# (F.pad(x, (K-1, 0)) then F.conv1d(groups=D)); backward = autograd of it as in
+# :910-965.  silu=True appends the SiLU that causal_conv1d_fn(activation="silu")
+# applies.
+# ---------------------------------------------------------------------------
+def causal_conv1d(x, weight, bias=None, silu: bool = False, dt=DEFAULT):
+    return _conv1d(_c(x, dt), _c(weight, dt), _c(bias, dt), silu)
+
+
+def _conv1d(x, w, b, silu):
+    K = w.shape[1]
+    T = x.shape[-1]
+    xp = F.pad(x, (K - 1, 0))
+    y = sum(w[None, :, k, None] * xp[..., k:k + T] for k in range(K))
+    if b is not None:
+        y = y + b[None, :, None]
+    return y * torch.sigmoid(y) if silu else y
+
+
+def causal_conv1d_grads(x, weight, bias, dy, silu: bool = False, dt=DEFAULT):
+    """Returns (dx, dweight, dbias or None)."""
+    xr = _c(x, dt).requires_grad_(True)
+    wr = _c(weight, dt).requires_grad_(True)
+    br = _c(bias, dt).requires_grad_(True) if bias is not None else None
+    with torch.enable_grad():
+        y = _conv1d(xr, wr, br, silu)
+        y.backward(_c(dy, dt))
+    return xr.grad, wr.grad, (br.grad if br is not None else None)

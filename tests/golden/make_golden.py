@@ -14,6 +14,9 @@ read-only is fine).  Every output stored here comes from the reference's code:
                    + autograd (the mamba test's reference, tests/ops/test_selective_scan.py)
   ce.npz           kernels/ce_fused.ce_full fp32 path (:755-777) + autograd, cases
                    plain / softcap / label smoothing / ignore / z-loss
+  conv1d.npz       kernels/hip/_torch_ops.causal_conv1d_shim_op (:883-902, the
+                   F.pad + F.conv1d branch) and _causal_conv1d_shim_backward
+                   (:910-965); the "silu" case adds F.silu + autograd on top
   linear_ce.npz    F.linear + F.cross_entropy(ignore_index) fp32 + autograd, the
                    oracle of scripts/test_chunked_ce.py:13-39
 The fixtures are committed; the GPU box never needs the reference.
@@ -178,6 +181,25 @@ def main() -> None:
     lossl.backward()
     np.savez_compressed(HERE / "linear_ce.npz", H=_np(H), W=_np(W), labels=_np(lab), loss=np.float64(lossl.item()),
                         dH=_np(Hr.grad), dW=_np(Wr.grad))
+    # ---------------- causal conv1d (reference op; T crosses the 256-step kernel chunk)
+    g = torch.Generator().manual_seed(5)
+    payload = {}
+    for tag, (B, D, T, K) in {"k4": (2, 16, 300, 4), "k3": (2, 8, 37, 3)}.items():
+        xc = torch.randn(B, D, T, generator=g)
+        wc = 0.5 * torch.randn(D, K, generator=g)
+        bc = 0.1 * torch.randn(D, generator=g)
+        dyc = torch.randn(B, D, T, generator=g)
+        yc = rops.causal_conv1d_shim_op(xc, wc, bc)
+        gxc, gwc, gbc = rops._causal_conv1d_shim_backward(_Ctx((xc, wc, bc)), dyc)
+        xs, ws, bs = (t.clone().requires_grad_(True) for t in (xc, wc, bc))
+        with torch.enable_grad():
+            ys = torch.nn.functional.silu(rops.causal_conv1d_shim_op(xs, ws, bs))
+            ys.backward(dyc)
+        payload.update({f"{tag}_x": _np(xc), f"{tag}_w": _np(wc), f"{tag}_b": _np(bc), f"{tag}_dy": _np(dyc),
+                        f"{tag}_y": _np(yc), f"{tag}_dx": _np(gxc), f"{tag}_dw": _np(gwc), f"{tag}_db": _np(gbc),
+                        f"{tag}_silu_y": _np(ys), f"{tag}_silu_dx": _np(xs.grad), f"{tag}_silu_dw": _np(ws.grad),
+                        f"{tag}_silu_db": _np(bs.grad)})
+    np.savez_compressed(HERE / "conv1d.npz", **payload)
     print("golden fixtures written to", HERE)
 
 

@@ -93,3 +93,16 @@ def test_linear_ce_golden():
     assert abs(loss.item() - float(g["loss"])) <= 1e-6 * abs(float(g["loss"]))
     assert_fp32_close(dH, g["dH"], 1e-5, "dH")
     assert_fp32_close(dW, g["dW"], 1e-5, "dW")
+
+
+@pytest.mark.parametrize("tag", ["k4", "k3"])
+@pytest.mark.parametrize("silu", [False, True])
+def test_causal_conv1d_golden(tag, silu):
+    g = golden("conv1d")
+    x, w, b, dy = (torch.from_numpy(g[f"{tag}_{k}"]) for k in ("x", "w", "b", "dy"))
+    p = f"{tag}_silu_" if silu else f"{tag}_"
+    assert_fp32_close(O.causal_conv1d(x, w, b, silu=silu), g[p + "y"], what="y")
+    dx, dw, db = O.causal_conv1d_grads(x, w, b, dy, silu=silu)
+    assert_fp32_close(dx, g[p + "dx"], what="dx")
+    assert_fp32_close(dw, g[p + "dw"], what="dw")
+    assert_fp32_close(db, g[p + "db"], what="db")
