@@ -3,7 +3,9 @@
 `Pattern(name, priority, op_speedup)` with `matches(name, module, model)` /
 `apply(name, module, model)` keeps the reference's contract
 (autokernel/_patterns.py:22-33).  The pattern set here is the hot-path one:
-RMSNorm (reference RMSNormPattern, _patterns.py:508-529).
+  * FusedResidualRMSNormPattern (reference _patterns.py:473-485, replacement
+    :364-398, block detection :51-56,102-118), priority 100;
+  * RMSNormPattern (reference _patterns.py:508-529), priority 50.
 """
 from __future__ import annotations
 
@@ -79,6 +81,78 @@ class RMSNormPattern(Pattern):
         return _RMSNormReplacement(module)
 
 
+# (attention, attention_norm, feed_forward, ffn_norm) attribute names of a
+# pre-norm residual block; the first four are the reference's aliases
+# (_patterns.py:51-56), the last one is the hybrid Mamba/attention layer.
+_BLOCK_ALIASES = [
+    ("attention", "attention_norm", "feed_forward", "ffn_norm"),
+    ("self_attn", "input_layernorm", "mlp", "post_attention_layernorm"),
+    ("attn", "pre_norm", "ffn", "ffn_norm"),
+    ("conv", "pre_norm", "ffn", "ffn_norm"),
+    ("mixer", "pre_norm", "ffn", "ffn_norm"),
+]
+
+
+def _find_block_attrs(module: nn.Module):
+    """Alias tuple if `module` is a pre-norm residual block, else None; momentum
+    blocks (`log_beta`) and modules flagged `_skip_autokernel` are rejected as in
+    the reference (_patterns.py:102-118)."""
+    if hasattr(module, "log_beta") or getattr(module, "_skip_autokernel", False):
+        return None
+    for alias in _BLOCK_ALIASES:
+        attn, attn_norm, ffn, ffn_norm = alias
+        if all(hasattr(module, a) for a in alias) and isinstance(getattr(getattr(module, ffn_norm), "weight", None),
+                                                                 torch.Tensor):
+            return alias
+    return None
+
+
+class _FusedResidualRMSNormBlockReplacement(nn.Module):
+    """x -> hidden = x + attn(attn_norm(x)); out = hidden + ffn(rmsnorm(hidden)),
+    with the residual add and the second norm in one kernel
+    (`torch.ops.autokernel.fused_res_rmsnorm_eps`, hidden and normed out of one pass).
+
+    Submodules keep their original attribute names, so state-dict keys and
+    optimizer state are unchanged.  Extra forward arguments (e.g. freqs_cis in
+    the reference's `forward(x, freqs_cis)`) are passed to the attention
+    module.  When the residual stream and the attention output differ in dtype
+    (autocast), both are promoted to the wider one, which keeps eager
+    semantics; the reference instead casts to fp16 (_patterns.py:386-392).
+    """
+
+    def __init__(self, original: nn.Module, alias):
+        super().__init__()
+        self._alias = tuple(alias)
+        for a in alias:
+            setattr(self, a, getattr(original, a))
+        import kernels.hip._torch_ops  # noqa: F401  (registers the ops)
+        self._op = torch.ops.autokernel.fused_res_rmsnorm_eps
+
+    def forward(self, x: torch.Tensor, *args, **kwargs) -> torch.Tensor:
+        attn, attn_norm, ffn, ffn_norm = (getattr(self, a) for a in self._alias)
+        a = attn(attn_norm(x), *args, **kwargs)
+        if not a.is_cuda:
+            raise RuntimeError("autokernel fused residual RMSNorm needs CUDA tensors")
+        dt = torch.promote_types(a.dtype, x.dtype)
+        eps = float(getattr(ffn_norm, "eps", 1e-6) or 1e-6)
+        hidden, normed = self._op(a.to(dt), x.to(dt), ffn_norm.weight, eps)
+        return hidden + ffn(normed)
+
+
+class FusedResidualRMSNormPattern(Pattern):
+    def __init__(self):
+        super().__init__("fused_residual_rmsnorm", priority=100, op_speedup=6.6)
+
+    def matches(self, name: str, module: nn.Module, model: nn.Module) -> bool:
+        if isinstance(module, _FusedResidualRMSNormBlockReplacement):
+            return False
+        return _find_block_attrs(module) is not None
+
+    def apply(self, name: str, module: nn.Module, model: nn.Module) -> nn.Module:
+        return _FusedResidualRMSNormBlockReplacement(module, _find_block_attrs(module))
+
+
 ALL_PATTERNS: List[Pattern] = [
+    FusedResidualRMSNormPattern(),
     RMSNormPattern(),
 ]

@@ -4,6 +4,9 @@
 //   y = x * rsqrt(mean(x^2) + eps) * w
 // Backward (kernels/hip/_torch_ops.py:73-97):
 //   dx = r*dy*w - x * r^3 * sum(dy*w*x)/N,   dw = sum_rows dy*x*r
+// Fused residual variant (kernels/hip/fused_residual_add_rmsnorm.py,
+// fused_residual_rmsnorm_backward.py): hidden = x + residual feeds the norm and
+// is a second output; its backward adds grad_hidden to dx.
 //
 // Design: one warp per row, the row held in registers (16-byte vector loads,
 // one HBM read of x / dy), fp32 accumulation, warp-shuffle reductions only.
@@ -22,10 +25,13 @@ constexpr int kWarps = 8;  // rows in flight per CTA
 // ----------------------------------------------------------------------------
 // Forward, row in registers
 // ----------------------------------------------------------------------------
-template <typename T, typename TW, int VEC, int NIT>
+// RES: fused residual add (hidden = x + res, rounded to T, stored to h_out when
+// non-null, then normalised).
+template <typename T, typename TW, int VEC, int NIT, bool RES = false>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __restrict__ x,
-                 const TW* __restrict__ w, int64_t M, int N, float eps) {
+                 const TW* __restrict__ w, int64_t M, int N, float eps, const T* __restrict__ res = nullptr,
+                 T* __restrict__ h_out = nullptr) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   float wr[NIT][VEC];
@@ -48,6 +54,13 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
       const int c = (it * 32 + lane) * VEC;
       if (c < N) {
         load_frag<T, VEC>(xv[it], xr + c);
+        if constexpr (RES) {
+          float rv[VEC];
+          load_frag<T, VEC>(rv, res + row * N + c);
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) xv[it][k] = to_f<T>(from_f<T>(xv[it][k] + rv[k]));
+          if (h_out != nullptr) store_frag<T, VEC>(h_out + row * N + c, xv[it]);
+        }
       } else {
 #pragma unroll
         for (int k = 0; k < VEC; ++k) xv[it][k] = 0.f;
@@ -74,16 +87,23 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
 
 // Forward fallback for rows that do not fit the register path (very wide or
 // unaligned rows): one CTA per row, scalar accesses, two passes (second from L2).
-template <typename T, typename TW>
+template <typename T, typename TW, bool RES = false>
 __global__ void __launch_bounds__(256)
 rmsnorm_fwd_block(T* __restrict__ y, float* __restrict__ rstd_out, const T* __restrict__ x,
-                  const TW* __restrict__ w, int64_t M, int N, float eps) {
+                  const TW* __restrict__ w, int64_t M, int N, float eps, const T* __restrict__ res = nullptr,
+                  T* __restrict__ h_out = nullptr) {
   __shared__ float red[32];
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const T* xr = x + row * N;
+    const T* rr = RES ? res + row * N : nullptr;
     float ss = 0.f;
     for (int c = threadIdx.x; c < N; c += blockDim.x) {
-      const float v = to_f<T>(xr[c]);
+      float v = to_f<T>(xr[c]);
+      if constexpr (RES) {
+        const T h = from_f<T>(v + to_f<T>(rr[c]));
+        if (h_out != nullptr) h_out[row * N + c] = h;
+        v = to_f<T>(h);
+      }
       ss = fmaf(v, v, ss);
     }
     ss = warp_sum(ss);
@@ -94,8 +114,11 @@ rmsnorm_fwd_block(T* __restrict__ y, float* __restrict__ rstd_out, const T* __re
     const float r = rsqrtf(tot / (float)N + eps);
     if (rstd_out != nullptr && threadIdx.x == 0) rstd_out[row] = r;
     T* yr = y + row * N;
-    for (int c = threadIdx.x; c < N; c += blockDim.x)
-      yr[c] = from_f<T>(to_f<T>(xr[c]) * r * to_f<TW>(w[c]));
+    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+      float v = to_f<T>(xr[c]);
+      if constexpr (RES) v = to_f<T>(from_f<T>(v + to_f<T>(rr[c])));
+      yr[c] = from_f<T>(v * r * to_f<TW>(w[c]));
+    }
     __syncthreads();
   }
 }
@@ -103,10 +126,13 @@ rmsnorm_fwd_block(T* __restrict__ y, float* __restrict__ rstd_out, const T* __re
 // ----------------------------------------------------------------------------
 // Backward, row in registers; per-CTA dw partial row into the workspace.
 // ----------------------------------------------------------------------------
-template <typename T, typename TW, int VEC, int NIT>
+// RES: dx += gh (the gradient reaching the un-normalised output of the fused
+// residual add), loaded only at store time.
+template <typename T, typename TW, int VEC, int NIT, bool RES = false>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __restrict__ dy,
-                 const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps) {
+                 const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps,
+                 const T* __restrict__ gh = nullptr) {
   extern __shared__ float s_dw[];  // [kWarps][N]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -156,6 +182,14 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
           o[k] = r * gv[it][k] * wr[it][k] - xv[it][k] * c3;
           acc[it][k] = fmaf(gv[it][k], xv[it][k] * r, acc[it][k]);
         }
+        if constexpr (RES) {
+          if (gh != nullptr) {
+            float hv[VEC];
+            load_frag<T, VEC>(hv, gh + row * N + c);
+#pragma unroll
+            for (int k = 0; k < VEC; ++k) o[k] += hv[k];
+          }
+        }
         store_frag<T, VEC>(dx + row * N + c, o);
       }
     }
@@ -180,10 +214,11 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
 
 // Backward fallback (wide / unaligned rows): one CTA per row at a time, the
 // CTA owns partial row blockIdx.x of the workspace exclusively.
-template <typename T, typename TW>
+template <typename T, typename TW, bool RES = false>
 __global__ void __launch_bounds__(256)
 rmsnorm_bwd_block(T* __restrict__ dx, float* __restrict__ dw_part, const T* __restrict__ dy,
-                  const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps) {
+                  const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps,
+                  const T* __restrict__ gh = nullptr) {
   __shared__ float red1[32], red2[32];
   float* part = dw_part + (int64_t)blockIdx.x * N;
   for (int c = threadIdx.x; c < N; c += blockDim.x) part[c] = 0.f;
@@ -206,7 +241,11 @@ rmsnorm_bwd_block(T* __restrict__ dx, float* __restrict__ dw_part, const T* __re
     const float c3 = r * r * r * t2 / (float)N;
     for (int c = threadIdx.x; c < N; c += blockDim.x) {
       const float xv = to_f<T>(xr[c]), gv = to_f<T>(gr[c]);
-      dx[row * N + c] = from_f<T>(r * gv * to_f<TW>(w[c]) - xv * c3);
+      float o = r * gv * to_f<TW>(w[c]) - xv * c3;
+      if constexpr (RES) {
+        if (gh != nullptr) o += to_f<T>(gh[row * N + c]);
+      }
+      dx[row * N + c] = from_f<T>(o);
       part[c] = fmaf(gv, xv * r, part[c]);
     }
     __syncthreads();
@@ -284,34 +323,36 @@ int bwd_grid(int64_t M, int N) {
   return (int)g;
 }
 
-template <typename T, typename TW>
+template <typename T, typename TW, bool RES = false>
 int fwd_impl(void* y, float* rstd, const void* x, const void* w, int64_t M, int N, float eps,
-             cudaStream_t st) {
+             cudaStream_t st, const void* res = nullptr, void* h_out = nullptr) {
   RmsPlan p = plan<T, TW>(M, N, x, y, w);
+  if (RES && !(aligned16(res) && (h_out == nullptr || aligned16(h_out)))) p.warp_path = false;
   constexpr int VEC = 16 / sizeof(T);
   if (p.warp_path) {
     int64_t g = (M + kWarps - 1) / kWarps;
     const int64_t cap = (int64_t)sm_count() * 16;
     if (g > cap) g = cap;
     AK_NIT_SWITCH(p.nit, NIT,
-                  rmsnorm_fwd_warp<T, TW, VEC, NIT><<<(unsigned)g, kWarps * 32, 0, st>>>(
-                      (T*)y, rstd, (const T*)x, (const TW*)w, M, N, eps));
+                  rmsnorm_fwd_warp<T, TW, VEC, NIT, RES><<<(unsigned)g, kWarps * 32, 0, st>>>(
+                      (T*)y, rstd, (const T*)x, (const TW*)w, M, N, eps, (const T*)res, (T*)h_out));
   } else {
     int64_t g = M;
     const int64_t cap = (int64_t)sm_count() * 8;
     if (g > cap) g = cap;
-    rmsnorm_fwd_block<T, TW><<<(unsigned)g, 256, 0, st>>>((T*)y, rstd, (const T*)x,
-                                                          (const TW*)w, M, N, eps);
+    rmsnorm_fwd_block<T, TW, RES><<<(unsigned)g, 256, 0, st>>>((T*)y, rstd, (const T*)x, (const TW*)w, M, N,
+                                                               eps, (const T*)res, (T*)h_out);
   }
   AK_CHECK_LAUNCH("ak_rmsnorm_fwd");
   return AK_OK;
 }
 
-template <typename T, typename TW>
+template <typename T, typename TW, bool RES = false>
 int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const void* x, const void* w,
-             int64_t M, int N, float eps, cudaStream_t st) {
+             int64_t M, int N, float eps, cudaStream_t st, const void* gh = nullptr) {
   RmsPlan p = plan<T, TW>(M, N, x, dx, w);
   if (!aligned16(dy)) p.warp_path = false;
+  if (RES && gh != nullptr && !aligned16(gh)) p.warp_path = false;
   // x, dy, w and the dw accumulator all live in registers: beyond 32 elements
   // per lane the register path spills, so wider rows take the CTA fallback.
   if (p.nit * p.vec > 32) p.warp_path = false;
@@ -321,15 +362,16 @@ int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const voi
     if (p.warp_path) {
       const size_t smem = (size_t)kWarps * N * sizeof(float);
       AK_NIT_SWITCH(p.nit, NIT, {
-        auto kern = rmsnorm_bwd_warp<T, TW, VEC, NIT>;
+        auto kern = rmsnorm_bwd_warp<T, TW, VEC, NIT, RES>;
         if (smem > 48 * 1024)
           AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                       "ak_rmsnorm_bwd: smem attribute");
-        kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps);
+        kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps,
+                                           (const T*)gh);
       });
     } else {
-      rmsnorm_bwd_block<T, TW><<<G, 256, 0, st>>>((T*)dx, ws, (const T*)dy, (const T*)x,
-                                                  (const TW*)w, M, N, eps);
+      rmsnorm_bwd_block<T, TW, RES><<<G, 256, 0, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N,
+                                                       eps, (const T*)gh);
     }
     AK_CHECK_LAUNCH("ak_rmsnorm_bwd");
   }
@@ -390,6 +432,39 @@ extern "C" int ak_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspace, si
   return AK_OK;
 }
 
+// ---- Fused residual add + RMSNorm (kernels/hip/fused_residual_add_rmsnorm.py,
+// autokernel::fused_res_rmsnorm in kernels/hip/_torch_ops.py:238-296)
+extern "C" int ak_fused_res_rmsnorm_fwd(void* hidden, void* normed, const void* x, const void* residual,
+                                        const void* w, int64_t M, int64_t N, float eps, int dt_x, int dt_w,
+                                        void* stream) {
+  clear_error();
+  AK_REQUIRE(M >= 0 && N > 0 && N <= (1 << 24), AK_ERR_SHAPE, "ak_fused_res_rmsnorm_fwd: bad shape M=%lld N=%lld",
+             (long long)M, (long long)N);
+  if (M == 0) return AK_OK;
+  AK_REQUIRE(normed && x && residual && w, AK_ERR_ARG, "ak_fused_res_rmsnorm_fwd: null pointer");
+  AK_DISPATCH_XW(dt_x, dt_w,
+                 return fwd_impl<T, TW, true>(normed, nullptr, x, w, M, (int)N, eps, (cudaStream_t)stream, residual,
+                                              hidden));
+  return AK_OK;
+}
+
+extern "C" int ak_fused_res_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspace, size_t ws_bytes,
+                                        const void* grad_hidden, const void* grad_normed, const void* hidden,
+                                        const void* w, int64_t M, int64_t N, float eps, int dt_x, int dt_w,
+                                        void* stream) {
+  clear_error();
+  AK_REQUIRE(M >= 0 && N > 0 && N <= (1 << 24), AK_ERR_SHAPE, "ak_fused_res_rmsnorm_bwd: bad shape");
+  AK_REQUIRE(dw && w, AK_ERR_ARG, "ak_fused_res_rmsnorm_bwd: null pointer");
+  AK_REQUIRE(M == 0 || (dx && grad_normed && hidden), AK_ERR_ARG, "ak_fused_res_rmsnorm_bwd: null pointer");
+  const size_t need = (size_t)bwd_grid(M, (int)N) * (size_t)N * sizeof(float);
+  AK_REQUIRE(M == 0 || (workspace && ws_bytes >= need), AK_ERR_WORKSPACE,
+             "ak_fused_res_rmsnorm_bwd: workspace %zu < %zu bytes", ws_bytes, need);
+  AK_DISPATCH_XW(dt_x, dt_w,
+                 return bwd_impl<T, TW, true>(dx, dw, dt_dw, (float*)workspace, grad_normed, hidden, w, M, (int)N,
+                                              eps, (cudaStream_t)stream, grad_hidden));
+  return AK_OK;
+}
+
 // ============================================================================
 // RMSNorm backward that allocates nothing (no counterpart in the reference).
 //
@@ -444,7 +519,8 @@ int bwd_noalloc_impl(void* dx, void* dw, int dt_dw, float* ws, int G, const void
         if (smem > 48 * 1024)
           AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                       "ak_rmsnorm_bwd_noalloc: smem attribute");
-        kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps);
+        kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps,
+                                           nullptr);
       });
     } else {
       rmsnorm_bwd_block<T, TW><<<G, 256, 0, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps);

@@ -29,6 +29,8 @@ SIGNATURES = {
     "ak_rmsnorm_bwd_workspace_size": [_i64, _i64, ctypes.POINTER(_sz)],
     "ak_rmsnorm_bwd": [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
     "ak_rmsnorm_bwd_noalloc": [_vp, _vp, _i, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
+    "ak_fused_res_rmsnorm_fwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
+    "ak_fused_res_rmsnorm_bwd": [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
     "ak_softmax_fwd": [_vp, _vp, _i64, _i64, _i, _vp],
     "ak_softmax_bwd": [_vp, _vp, _vp, _i64, _i64, _i, _vp],
     "ak_ce_rows_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _i, _vp],
@@ -161,6 +163,47 @@ def rmsnorm_bwd(x: torch.Tensor, w: torch.Tensor, dy: torch.Tensor, eps: float =
     ws = workspace(ws_bytes, dev)
     call("ak_rmsnorm_bwd", ptr(dx), ptr(dw), _DT[dw_dtype], ptr(ws), ws_bytes, ptr(dy), ptr(x), ptr(w), M, N,
          float(eps), dtype_code(x), dtype_code(w), stream(dev))
+    return dx, dw
+
+
+# ---------------------------------------------------------------------------
+# Fused residual add + RMSNorm
+# ---------------------------------------------------------------------------
+def fused_res_rmsnorm_fwd(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
+                          want_hidden: bool = True):
+    """Returns (hidden or None, normed), both shaped and typed like x."""
+    dev = require_cuda(x, residual, w)
+    if residual.shape != x.shape:
+        raise ValueError(f"fused_res_rmsnorm: residual {tuple(residual.shape)} != x {tuple(x.shape)}")
+    x = x.contiguous()
+    residual = residual.to(x.dtype).contiguous()
+    w = w.contiguous()
+    N = x.shape[-1]
+    M = x.numel() // N if N else 0
+    normed = torch.empty_like(x)
+    hidden = torch.empty_like(x) if want_hidden else None
+    call("ak_fused_res_rmsnorm_fwd", ptr(hidden), ptr(normed), ptr(x), ptr(residual), ptr(w), M, N, float(eps),
+         dtype_code(x), dtype_code(w), stream(dev))
+    return hidden, normed
+
+
+def fused_res_rmsnorm_bwd(hidden: torch.Tensor, w: torch.Tensor, grad_hidden: Optional[torch.Tensor],
+                          grad_normed: torch.Tensor, eps: float = 1e-6, dw_dtype: Optional[torch.dtype] = None):
+    """Returns (dx, dw); dx is also the residual's gradient. dw defaults to fp32."""
+    dev = require_cuda(hidden, w, grad_hidden, grad_normed)
+    dw_dtype = dw_dtype or torch.float32
+    hidden = hidden.contiguous()
+    w = w.contiguous()
+    gn = grad_normed.to(hidden.dtype).contiguous()
+    gh = grad_hidden.to(hidden.dtype).contiguous() if grad_hidden is not None else None
+    N = hidden.shape[-1]
+    M = hidden.numel() // N if N else 0
+    dx = torch.empty_like(hidden)
+    dw = torch.empty(N, dtype=dw_dtype, device=dev)
+    ws_bytes = _size_query("ak_rmsnorm_bwd_workspace_size", M, N)
+    ws = workspace(ws_bytes, dev)
+    call("ak_fused_res_rmsnorm_bwd", ptr(dx), ptr(dw), _DT[dw_dtype], ptr(ws), ws_bytes, ptr(gh), ptr(gn),
+         ptr(hidden), ptr(w), M, N, float(eps), dtype_code(hidden), dtype_code(w), stream(dev))
     return dx, dw
 
 

@@ -6,11 +6,17 @@ Mirrors kernels/hip/_torch_ops.py of the reference:
     (dx, dw), autocast rule cuda/fp16, eps fixed at 1e-6 as in :70);
   * `torch.ops.autokernel.selective_scan(Tensor dA, Tensor dBx, Tensor C,
     Tensor D, Tensor x) -> Tensor` (reference :312-394, grads
-    (d dA, d dBx, dC, dD, dx)).
+    (d dA, d dBx, dC, dD, dx));
+  * `torch.ops.autokernel.fused_res_rmsnorm(x, residual, weight) ->
+    (hidden, normed)` (reference :238-303);
+  * `torch.ops.autokernel.causal_conv1d(x, weight, bias) -> y` (reference
+    :883-975).
 Added here (no reference counterpart):
   * `autokernel::rmsnorm_eps(x, weight, eps)` — same op with the module's eps
     and no autocast cast, used by the module replacement;
   * `autokernel::softmax(x)` — differentiable row softmax;
+  * `autokernel::fused_res_rmsnorm_eps(x, residual, weight, eps)` and
+    `autokernel::causal_conv1d_silu(x, weight, bias)`;
   * the backward passes as their own custom ops (`*_bwd`), so torch.compile
     sees opaque nodes in both directions instead of tracing into ctypes calls.
 
@@ -189,6 +195,76 @@ def _selective_scan_backward(ctx, grad_y):
 
 
 selective_scan_op.register_autograd(_selective_scan_backward, setup_context=_selective_scan_setup)
+
+
+# ---------------------------------------------------------------------------
+# Fused residual add + RMSNorm (dual output) — reference _torch_ops.py:238-303:
+# `autokernel::fused_res_rmsnorm(x, residual, weight) -> (hidden, normed)`, eps
+# 1e-6, grads (grad_x, grad_residual = grad_x, grad_weight), autocast cuda/fp16.
+# `fused_res_rmsnorm_eps` (added) carries the norm module's own eps.
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::fused_res_rmsnorm_bwd", mutates_args=())
+def fused_res_rmsnorm_bwd_op(hidden: torch.Tensor, weight: torch.Tensor, grad_hidden: Optional[torch.Tensor],
+                             grad_normed: torch.Tensor, eps: float) -> List[torch.Tensor]:
+    dx, dw = _ak.fused_res_rmsnorm_bwd(hidden, weight, grad_hidden, grad_normed, eps)
+    return [dx, dw.to(weight.dtype)]
+
+
+@fused_res_rmsnorm_bwd_op.register_fake
+def _(hidden, weight, grad_hidden, grad_normed, eps):
+    return [torch.empty_like(hidden), torch.empty_like(weight)]
+
+
+def _res_setup(ctx, inputs, output):
+    x, residual, weight = inputs[:3]
+    ctx.eps = inputs[3] if len(inputs) > 3 else RMSNORM_EPS
+    ctx.save_for_backward(output[0], weight)
+
+
+def _res_backward(ctx, grad_hidden, grad_normed):
+    hidden, weight = ctx.saved_tensors
+    if grad_normed is None:
+        grad_normed = torch.zeros_like(hidden)
+    dx, dw = fused_res_rmsnorm_bwd_op(hidden, weight, grad_hidden, grad_normed.contiguous(), ctx.eps)
+    return dx, dx, dw
+
+
+def _res_backward_eps(ctx, grad_hidden, grad_normed):
+    return (*_res_backward(ctx, grad_hidden, grad_normed), None)
+
+
+@torch.library.custom_op("autokernel::fused_res_rmsnorm", mutates_args=())
+def fused_res_rmsnorm_op(x: torch.Tensor, residual: torch.Tensor,
+                         weight: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    return _ak.fused_res_rmsnorm_fwd(x, residual, weight, RMSNORM_EPS)
+
+
+@fused_res_rmsnorm_op.register_fake
+def _(x, residual, weight):
+    return x.new_empty(x.shape), x.new_empty(x.shape)
+
+
+fused_res_rmsnorm_op.register_autograd(_res_backward, setup_context=_res_setup)
+try:
+    fused_res_rmsnorm_op.register_autocast("cuda", torch.float16)
+except AttributeError:  # pragma: no cover - older torch
+    pass
+
+
+@torch.library.custom_op("autokernel::fused_res_rmsnorm_eps", mutates_args=())
+def fused_res_rmsnorm_eps_op(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                             eps: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    return _ak.fused_res_rmsnorm_fwd(x, residual, weight, eps)
+
+
+@fused_res_rmsnorm_eps_op.register_fake
+def _(x, residual, weight, eps):
+    return x.new_empty(x.shape), x.new_empty(x.shape)
+
+
+fused_res_rmsnorm_eps_op.register_autograd(_res_backward_eps, setup_context=_res_setup)
 
 
 # ---------------------------------------------------------------------------

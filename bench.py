@@ -270,7 +270,7 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
 
 def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768):
     """Device-timed throughput of the other swapped ops at their BASELINE configs.
-    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "conv1d"} (None = all)."""
+    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "fused_res", "conv1d"} (None = all)."""
     from kernels import _ak
     res = {}
     st = torch.cuda.current_stream(dev)
@@ -383,6 +383,22 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         timeit(lambda: _ak.scan1_fwd(dA, dBx, C, Dv, xx), 20 * E, "scan1_fwd_fp32_8x2048x1536", steps)
         timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy), 36 * E, "scan1_bwd_fp32_8x2048x1536", steps)
         del dA, dBx, C, xx, gy
+        torch.cuda.empty_cache()
+
+    if want("fused_res"):
+        # Fused residual add + RMSNorm bf16 [65536, 768] (the hybrid's d_model; 100 MB per tensor):
+        # fwd reads x, residual and writes hidden, normed; bwd reads hidden, grad_hidden,
+        # grad_normed and writes dx.
+        Mr, Nr = 65536, 768
+        xr_, rr_, ghr, gnr = (torch.randn(Mr, Nr, device=dev).to(torch.bfloat16) for _ in range(4))
+        wr_ = torch.randn(Nr, device=dev).to(torch.bfloat16)
+        hr_, _ = _ak.fused_res_rmsnorm_fwd(xr_, rr_, wr_)
+        E = Mr * Nr
+        timeit(lambda: _ak.fused_res_rmsnorm_fwd(xr_, rr_, wr_), 8 * E, "fused_res_rmsnorm_fwd_bf16_65536x768", steps,
+               graph=True)
+        timeit(lambda: _ak.fused_res_rmsnorm_bwd(hr_, wr_, ghr, gnr), 8 * E, "fused_res_rmsnorm_bwd_bf16_65536x768",
+               steps, graph=True)
+        del xr_, rr_, ghr, gnr, hr_
         torch.cuda.empty_cache()
 
     if want("conv1d"):
@@ -554,7 +570,7 @@ def main():
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
-    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,conv1d")
+    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,fused_res,conv1d")
     ap.add_argument("--ce-rows", type=int, default=32768, help="with --only-ops: rows of the linear+CE case")
     ap.add_argument("--batch", type=int, default=0, help="override the headline batch (small-case profiling)")
     args = ap.parse_args()

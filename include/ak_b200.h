@@ -249,6 +249,30 @@ AK_API int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB, vo
                           int64_t batch, int64_t dim, int64_t seqlen,
                           int64_t dstate, int64_t groups, int dt, void* stream);
 
+/* ---- Fused residual add + RMSNorm (dual output) --------------------------
+ * hidden = x + residual (rounded to dt_x); normed = hidden * rsqrt(mean(hidden^2)
+ * + eps) * w.  hidden is nullable (single-output form).  x, residual, hidden,
+ * normed: (M, N) dt_x; w: (N) dt_w, with the (dt_x, dt_w) pairs of
+ * ak_rmsnorm_fwd.  Replaces fused_residual_add_rmsnorm_hip /
+ * fused_residual_add_rmsnorm_dual_hip (kernels/hip/fused_residual_add_rmsnorm.py:
+ * 340-418) behind autokernel::fused_res_rmsnorm (kernels/hip/_torch_ops.py:238-251). */
+AK_API int ak_fused_res_rmsnorm_fwd(void* hidden, void* normed, const void* x,
+                                    const void* residual, const void* w,
+                                    int64_t M, int64_t N, float eps, int dt_x,
+                                    int dt_w, void* stream);
+
+/* Backward: dx (= d residual) = grad_hidden + RMSNorm-backward(hidden, w,
+ * grad_normed); dw (dt_dw) = sum over rows of grad_normed * hidden * rstd.
+ * grad_hidden nullable (zero).  Workspace: ak_rmsnorm_bwd_workspace_size(M, N).
+ * Replaces fused_residual_rmsnorm_backward_hip
+ * (kernels/hip/fused_residual_rmsnorm_backward.py:248-300) and the fp32 branch
+ * of _fused_res_rmsnorm_backward (kernels/hip/_torch_ops.py:262-290). */
+AK_API int ak_fused_res_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspace,
+                                    size_t ws_bytes, const void* grad_hidden,
+                                    const void* grad_normed, const void* hidden,
+                                    const void* w, int64_t M, int64_t N, float eps,
+                                    int dt_x, int dt_w, void* stream);
+
 /* ---- Depthwise causal conv1d (+ optional SiLU) --------------------------
  * y[b,d,t] = act(bias[d] + sum_k w[d,k] x[b,d,t-K+1+k]), x = 0 before t = 0;
  * act = SiLU when silu != 0, identity otherwise.  x, y: (B, D, T) dt, T

@@ -241,3 +241,27 @@ def causal_conv1d_grads(x, weight, bias, dy, silu: bool = False, dt=DEFAULT):
         y = _conv1d(xr, wr, br, silu)
         y.backward(_c(dy, dt))
     return xr.grad, wr.grad, (br.grad if br is not None else None)
+
+
+# ---------------------------------------------------------------------------
+# Fused residual add + RMSNorm — reference.fused_residual_add_rmsnorm_ref
+# (reference.py:72-78), dual form kernels/hip/fused_residual_add_rmsnorm.py:377-391;
+# backward kernels/hip/_torch_ops.py:262-290 (= fused_residual_rmsnorm_backward.py:265-281).
+# `round_to`: dtype the sum x + residual is rounded to before the norm (the
+# activation dtype; None keeps it exact).
+# ---------------------------------------------------------------------------
+def fused_res_rmsnorm(x, residual, w, eps: float = 1e-6, round_to=None, dt=DEFAULT):
+    if round_to is not None:
+        # the activation-dtype add: exact fp32 sum of the two inputs, one rounding
+        h = _c((_c(x, torch.float32) + _c(residual, torch.float32)).to(round_to), dt)
+    else:
+        h = _c(x, dt) + _c(residual, dt)
+    return h, rmsnorm_fwd(h, w, eps, dt=dt)
+
+
+def fused_res_rmsnorm_bwd(hidden, w, grad_hidden, grad_normed, eps: float = 1e-6, dt=DEFAULT):
+    """Returns (dx = d residual, dw)."""
+    dx, dw = rmsnorm_bwd(hidden, w, grad_normed, eps, dt=dt)
+    if grad_hidden is not None:
+        dx = dx + _c(grad_hidden, dt)
+    return dx, dw

@@ -17,6 +17,11 @@ read-only is fine).  Every output stored here comes from the reference's code:
   conv1d.npz       kernels/hip/_torch_ops.causal_conv1d_shim_op (:883-902, the
                    F.pad + F.conv1d branch) and _causal_conv1d_shim_backward
                    (:910-965); the "silu" case adds F.silu + autograd on top
+  fused_res.npz    kernels/hip/fused_residual_add_rmsnorm.kernel_fn_dual / kernel_fn
+                   (fp32 branch, :340-391), reference.fused_residual_add_rmsnorm_ref
+                   (+ autograd, plus grad_hidden for the hidden output),
+                   _torch_ops._fused_res_rmsnorm_backward (:262-290) and
+                   kernels/hip/fused_residual_rmsnorm_backward.kernel_fn (:265-281)
   linear_ce.npz    F.linear + F.cross_entropy(ignore_index) fp32 + autograd, the
                    oracle of scripts/test_chunked_ce.py:13-39
 The fixtures are committed; the GPU box never needs the reference.
@@ -181,6 +186,28 @@ def main() -> None:
     lossl.backward()
     np.savez_compressed(HERE / "linear_ce.npz", H=_np(H), W=_np(W), labels=_np(lab), loss=np.float64(lossl.item()),
                         dH=_np(Hr.grad), dW=_np(Wr.grad))
+    # ---------------- fused residual add + RMSNorm (fp32 branches of the reference)
+    from kernels.hip import fused_residual_add_rmsnorm as rfra
+    from kernels.hip import fused_residual_rmsnorm_backward as rfrb
+    g = torch.Generator().manual_seed(6)
+    xa = torch.randn(24, 768, generator=g)
+    ra = torch.randn(24, 768, generator=g)
+    wa = 1 + 0.1 * torch.randn(768, generator=g)
+    gha = torch.randn(24, 768, generator=g)
+    gna = torch.randn(24, 768, generator=g)
+    hid, nrm = rfra.kernel_fn_dual(_on_cuda(xa), _on_cuda(ra), _on_cuda(wa))
+    single = rfra.kernel_fn(_on_cuda(xa), _on_cuda(ra), _on_cuda(wa))
+    ref_fn = reference.fused_residual_add_rmsnorm_ref(xa, ra, wa)
+    gx, gr, gw = rops._fused_res_rmsnorm_backward(_Ctx((hid.as_subclass(torch.Tensor), wa), eps=1e-6), gha, gna)
+    bx, br, bw = rfrb.kernel_fn(_on_cuda(hid.as_subclass(torch.Tensor)), _on_cuda(wa), _on_cuda(gha), _on_cuda(gna))
+    xg, rg, wg = (t.clone().requires_grad_(True) for t in (xa, ra, wa))
+    reference.fused_residual_add_rmsnorm_ref(xg, rg, wg).backward(gna)
+    np.savez_compressed(HERE / "fused_res.npz", x=_np(xa), residual=_np(ra), w=_np(wa), grad_hidden=_np(gha),
+                        dx_autograd=_np(xg.grad + gha), dres_autograd=_np(rg.grad + gha), dw_autograd=_np(wg.grad),
+                        grad_normed=_np(gna), hidden=_np(hid), normed=_np(nrm), single=_np(single),
+                        ref_fn=_np(ref_fn), dx_op=_np(gx), dres_op=_np(gr), dw_op=_np(gw), dx_kfn=_np(bx),
+                        dres_kfn=_np(br), dw_kfn=_np(bw))
+
     # ---------------- causal conv1d (reference op; T crosses the 256-step kernel chunk)
     g = torch.Generator().manual_seed(5)
     payload = {}

@@ -106,3 +106,34 @@ def test_causal_conv1d_golden(tag, silu):
     assert_fp32_close(dx, g[p + "dx"], what="dx")
     assert_fp32_close(dw, g[p + "dw"], what="dw")
     assert_fp32_close(db, g[p + "db"], what="db")
+
+
+def test_fused_res_rmsnorm_golden():
+    g = golden("fused_res")
+    x, r, w, gh, gn = (torch.from_numpy(g[k]) for k in ("x", "residual", "w", "grad_hidden", "grad_normed"))
+    h, y = O.fused_res_rmsnorm(x, r, w)
+    assert_fp32_close(h, g["hidden"], what="hidden")
+    for k in ("normed", "single", "ref_fn"):
+        assert_fp32_close(y, g[k], what=k)
+    dx, dw = O.fused_res_rmsnorm_bwd(torch.from_numpy(g["hidden"]), w, gh, gn)
+    assert_fp32_close(dx, g["dx_autograd"], what="dx")
+    assert_fp32_close(dx, g["dres_autograd"], what="dres")
+    for k in ("dw_autograd", "dw_op", "dw_kfn"):
+        assert_fp32_close(dw, g[k], what=k)
+
+
+def test_reference_fused_res_fallback_dx_differs_by_missing_rstd():
+    """Pins a reference bug: the fp32 branches of _fused_res_rmsnorm_backward
+    (kernels/hip/_torch_ops.py:285) and fused_residual_rmsnorm_backward.kernel_fn
+    (:277) drop the outer rstd on the mean term, unlike the fp16 HIP kernel
+    (:169-170) and autograd.  The oracle follows the HIP kernel and autograd."""
+    g = golden("fused_res")
+    h = torch.from_numpy(g["hidden"]).double()
+    w, gh, gn = (torch.from_numpy(g[k]).double() for k in ("w", "grad_hidden", "grad_normed"))
+    r = (h.pow(2).mean(-1, keepdim=True) + 1e-6).rsqrt()
+    nh = h * r
+    gs = gn * w
+    buggy = gh + gs * r - nh * (gs * nh).sum(-1, keepdim=True) / h.shape[-1]
+    for k in ("dx_op", "dres_op", "dx_kfn", "dres_kfn"):
+        assert_fp32_close(buggy, g[k], rtol=1e-5, what=k)
+    assert (torch.from_numpy(g["dx_op"]).double() - torch.from_numpy(g["dx_autograd"]).double()).abs().max() > 1e-3

@@ -3,7 +3,8 @@ import torch
 import torch.nn as nn
 
 import autokernel
-from autokernel._patterns import RMSNormPattern, _RMSNormReplacement
+from autokernel._patterns import (FusedResidualRMSNormPattern, RMSNormPattern, _FusedResidualRMSNormBlockReplacement,
+                                  _RMSNormReplacement)
 
 
 class RMSNorm(nn.Module):
@@ -26,7 +27,7 @@ class Block(nn.Module):
 
 
 def test_list_patterns():
-    assert autokernel.list_patterns() == ["rmsnorm"]
+    assert autokernel.list_patterns() == ["fused_residual_rmsnorm", "rmsnorm"]
 
 
 def test_optimize_replaces_rmsnorms_and_keeps_parameters(monkeypatch):
@@ -83,3 +84,38 @@ def test_pattern_matching_rules():
     assert p.matches("n", nn.RMSNorm(4), None)
     assert not p.matches("n", nn.LayerNorm(4), None)
     assert not p.matches("n", nn.Linear(4, 4), None)
+
+
+class TransformerBlock(nn.Module):
+    """Reference-style block: attention / attention_norm / feed_forward / ffn_norm, forward(x, freqs_cis)."""
+
+    def __init__(self, d=16):
+        super().__init__()
+        self.attention_norm = RMSNorm(d)
+        self.attention = nn.Linear(d, d)
+        self.ffn_norm = RMSNorm(d, eps=1e-6)
+        self.feed_forward = nn.Linear(d, d)
+
+
+class MomentumBlock(TransformerBlock):
+    def __init__(self, d=16):
+        super().__init__(d)
+        self.log_beta = nn.Parameter(torch.zeros(1))
+
+
+def test_fused_residual_block_pattern(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    m = nn.Sequential(TransformerBlock(), MomentumBlock())
+    keys = set(m.state_dict())
+    autokernel.optimize(m, training=True)
+    assert isinstance(m[0], _FusedResidualRMSNormBlockReplacement)
+    assert not isinstance(m[1], _FusedResidualRMSNormBlockReplacement)  # momentum blocks are rejected
+    # the norms inside the replaced block are replaced by the RMSNorm pattern afterwards
+    assert isinstance(m[0].attention_norm, _RMSNormReplacement)
+    assert set(m.state_dict()) == keys
+    rep = autokernel.report(m)
+    assert rep["patterns"]["fused_residual_rmsnorm"] == {"modules_replaced": 1, "op_speedup": "6.6x"}
+    autokernel.restore(m)
+    assert isinstance(m[0], TransformerBlock) and isinstance(m[0].attention_norm, RMSNorm)
+    p = FusedResidualRMSNormPattern()
+    assert p.matches("b", TransformerBlock(), None) and not p.matches("b", Block(), None)
