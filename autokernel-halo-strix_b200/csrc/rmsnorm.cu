@@ -128,26 +128,36 @@ rmsnorm_fwd_block(T* __restrict__ y, float* __restrict__ rstd_out, const T* __re
 // ----------------------------------------------------------------------------
 // RES: dx += gh (the gradient reaching the un-normalised output of the fused
 // residual add), loaded only at store time.
+// Registers hold only the row being processed (x, dy); w and the per-warp dw
+// accumulators live in shared memory, each lane owning its columns (no
+// atomics).  Shared layout is lane-contiguous: column (it*32 + lane)*VEC + k
+// sits at slot (it*VEC + k)*32 + lane, so every access is bank-conflict free.
+template <int VEC>
+__device__ __forceinline__ int bwd_slot(int c) {
+  const int it = c / (32 * VEC), rem = c - it * 32 * VEC;
+  const int lane = rem / VEC, k = rem - lane * VEC;
+  return (it * VEC + k) * 32 + lane;
+}
+
 template <typename T, typename TW, int VEC, int NIT, bool RES = false>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, (NIT * VEC <= 24) ? 3 : 2)
 rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __restrict__ dy,
                  const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps,
                  const T* __restrict__ gh = nullptr) {
-  extern __shared__ float s_dw[];  // [kWarps][N]
+  constexpr int kSlots = NIT * VEC * 32;
+  extern __shared__ float s_dw[];  // [kWarps][kSlots] accumulators, then [kSlots] weights
+  float* s_w = s_dw + (size_t)kWarps * kSlots;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  float wr[NIT][VEC], acc[NIT][VEC];
-#pragma unroll
-  for (int it = 0; it < NIT; ++it) {
-    const int c = (it * 32 + lane) * VEC;
-    if (c < N) load_frag<TW, VEC>(wr[it], w + c);
-    else {
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) wr[it][k] = 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) acc[it][k] = 0.f;
+  for (int q = threadIdx.x; q < kSlots; q += blockDim.x) {  // every slot: columns >= N read as 0
+    const int j = q >> 5, ln = q & 31, it = j / VEC, k = j - it * VEC;
+    const int c = (it * 32 + ln) * VEC + k;
+    s_w[q] = c < N ? to_f<TW>(w[c]) : 0.f;
   }
+  float* my = s_dw + (size_t)warp * kSlots;
+#pragma unroll
+  for (int j = 0; j < NIT * VEC; ++j) my[j * 32 + lane] = 0.f;
+  __syncthreads();
   const float inv_n = 1.f / (float)N;
   for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < M; row += (int64_t)gridDim.x * kWarps) {
     float xv[NIT][VEC], gv[NIT][VEC];
@@ -162,10 +172,14 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
 #pragma unroll
         for (int k = 0; k < VEC; ++k) { xv[it][k] = 0.f; gv[it][k] = 0.f; }
       }
+    }
+#pragma unroll
+    for (int it = 0; it < NIT; ++it) {
 #pragma unroll
       for (int k = 0; k < VEC; ++k) {
+        // columns >= N hold x = dy = 0 and contribute nothing
         s1 = fmaf(xv[it][k], xv[it][k], s1);
-        s2 = fmaf(gv[it][k] * wr[it][k], xv[it][k], s2);
+        s2 = fmaf(gv[it][k] * s_w[(it * VEC + k) * 32 + lane], xv[it][k], s2);
       }
     }
     s1 = warp_sum(s1);
@@ -179,8 +193,9 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
         float o[VEC];
 #pragma unroll
         for (int k = 0; k < VEC; ++k) {
-          o[k] = r * gv[it][k] * wr[it][k] - xv[it][k] * c3;
-          acc[it][k] = fmaf(gv[it][k], xv[it][k] * r, acc[it][k]);
+          const int sl = (it * VEC + k) * 32 + lane;
+          o[k] = r * gv[it][k] * s_w[sl] - xv[it][k] * c3;
+          my[sl] = fmaf(gv[it][k], xv[it][k] * r, my[sl]);
         }
         if constexpr (RES) {
           if (gh != nullptr) {
@@ -195,19 +210,12 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
     }
   }
   // Fold the kWarps per-warp partials in a fixed order (deterministic).
-#pragma unroll
-  for (int it = 0; it < NIT; ++it) {
-    const int c = (it * 32 + lane) * VEC;
-    if (c < N) {
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) s_dw[warp * N + c + k] = acc[it][k];
-    }
-  }
   __syncthreads();
   for (int c = threadIdx.x; c < N; c += blockDim.x) {
+    const int sl = bwd_slot<VEC>(c);
     float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < kWarps; ++i) s += s_dw[i * N + c];
+    for (int i = 0; i < kWarps; ++i) s += s_dw[i * kSlots + sl];
     dw_part[(int64_t)blockIdx.x * N + c] = s;
   }
 }
@@ -252,22 +260,23 @@ rmsnorm_bwd_block(T* __restrict__ dx, float* __restrict__ dw_part, const T* __re
   }
 }
 
-// dw[c] = sum_g part[g][c] in a fixed order.  Block (32, 8): 32 columns x 8
-// row-groups, folded through shared memory in index order.
+// dw[c] = sum_g part[g][c] in a fixed order.  Block (32, 32): 32 columns x 32
+// row-groups (32 loads in flight per column), folded through shared memory in
+// index order.
 template <typename TD>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(1024)
 rmsnorm_dw_reduce(TD* __restrict__ dw, const float* __restrict__ part, int G, int N) {
-  __shared__ float s[8][33];
+  __shared__ float s[32][33];
   const int c = blockIdx.x * 32 + threadIdx.x;
   float acc = 0.f;
   if (c < N)
-    for (int g = threadIdx.y; g < G; g += 8) acc += part[(int64_t)g * N + c];
+    for (int g = threadIdx.y; g < G; g += 32) acc += part[(int64_t)g * N + c];
   s[threadIdx.y][threadIdx.x] = acc;
   __syncthreads();
   if (threadIdx.y == 0 && c < N) {
     float t = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) t += s[i][threadIdx.x];
+    for (int i = 0; i < 32; ++i) t += s[i][threadIdx.x];
     dw[c] = from_f<TD>(t);
   }
 }
@@ -313,10 +322,22 @@ RmsPlan plan(int64_t M, int N, const void* a, const void* b, const void* w) {
   return p;
 }
 
+// Grid of a backward kernel capped at the CTAs that are resident at once (one
+// wave: every CTA gets the same number of rows through the grid-stride loop).
+template <typename K>
+int resident_grid(K kern, size_t smem, int G) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, smem) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int cap = per_sm * sm_count();
+  return G < cap ? G : cap;
+}
+
 int bwd_grid(int64_t M, int N) {
-  const int64_t rows_per_cta = kWarps;
+  // at least 4 rows per warp, so the per-CTA set-up and dw fold are amortised
+  const int64_t rows_per_cta = 4 * kWarps;
   int64_t g = (M + rows_per_cta - 1) / rows_per_cta;
-  const int64_t cap = 2LL * sm_count();
+  const int64_t cap = 3LL * sm_count();  // CTAs resident per SM on the register path
   if (g > cap) g = cap;
   if (g < 1) g = 1;
   (void)N;
@@ -353,19 +374,21 @@ int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const voi
   RmsPlan p = plan<T, TW>(M, N, x, dx, w);
   if (!aligned16(dy)) p.warp_path = false;
   if (RES && gh != nullptr && !aligned16(gh)) p.warp_path = false;
-  // x, dy, w and the dw accumulator all live in registers: beyond 32 elements
-  // per lane the register path spills, so wider rows take the CTA fallback.
+  // x and dy live in registers (w and the dw accumulators in shared memory):
+  // beyond 32 elements per lane the register path spills, so wider rows take
+  // the CTA fallback.
   if (p.nit * p.vec > 32) p.warp_path = false;
   constexpr int VEC = 16 / sizeof(T);
-  const int G = bwd_grid(M, N);
+  int G = bwd_grid(M, N);
   if (M > 0) {
     if (p.warp_path) {
-      const size_t smem = (size_t)kWarps * N * sizeof(float);
-      AK_NIT_SWITCH(p.nit, NIT, {
+      AK_NIT_SWITCH(p.nit, NIT, if constexpr (NIT * VEC <= 32) {
         auto kern = rmsnorm_bwd_warp<T, TW, VEC, NIT, RES>;
+        const size_t smem = (size_t)(kWarps + 1) * NIT * VEC * 32 * sizeof(float);
         if (smem > 48 * 1024)
           AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                       "ak_rmsnorm_bwd: smem attribute");
+        G = resident_grid(kern, smem, G);
         kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps,
                                            (const T*)gh);
       });
@@ -376,7 +399,7 @@ int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const voi
     AK_CHECK_LAUNCH("ak_rmsnorm_bwd");
   }
   const int Gred = M > 0 ? G : 0;
-  dim3 rb(32, 8);
+  dim3 rb(32, 32);
   const unsigned rg = (unsigned)((N + 31) / 32);
   AK_DISPATCH_DTYPE(dt_dw, TD, rmsnorm_dw_reduce<TD><<<rg, rb, 0, st>>>((TD*)dw, ws, Gred, N));
   AK_CHECK_LAUNCH("ak_rmsnorm_bwd(dw reduce)");
@@ -513,12 +536,13 @@ int bwd_noalloc_impl(void* dx, void* dw, int dt_dw, float* ws, int G, const void
   constexpr int VEC = 16 / sizeof(T);
   if (M > 0) {
     if (p.warp_path) {
-      const size_t smem = (size_t)kWarps * N * sizeof(float);
-      AK_NIT_SWITCH(p.nit, NIT, {
+      AK_NIT_SWITCH(p.nit, NIT, if constexpr (NIT * VEC <= 32) {
         auto kern = rmsnorm_bwd_warp<T, TW, VEC, NIT>;
+        const size_t smem = (size_t)(kWarps + 1) * NIT * VEC * 32 * sizeof(float);
         if (smem > 48 * 1024)
           AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                       "ak_rmsnorm_bwd_noalloc: smem attribute");
+        G = resident_grid(kern, smem, G);
         kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps,
                                            nullptr);
       });
@@ -527,7 +551,7 @@ int bwd_noalloc_impl(void* dx, void* dw, int dt_dw, float* ws, int G, const void
     }
     AK_CHECK_LAUNCH("ak_rmsnorm_bwd_noalloc");
   }
-  dim3 rb(32, 8);
+  dim3 rb(32, 32);
   const unsigned rg = (unsigned)((N + 31) / 32);
   AK_DISPATCH_DTYPE(dt_dw, TD, rmsnorm_dw_reduce<TD><<<rg, rb, 0, st>>>((TD*)dw, ws, M > 0 ? G : 0, N));
   AK_CHECK_LAUNCH("ak_rmsnorm_bwd_noalloc(dw reduce)");
