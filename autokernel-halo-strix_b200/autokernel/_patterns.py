@@ -5,7 +5,9 @@
 (autokernel/_patterns.py:22-33).  The pattern set here is the hot-path one:
   * FusedResidualRMSNormPattern (reference _patterns.py:473-485, replacement
     :364-398, block detection :51-56,102-118), priority 100;
-  * RMSNormPattern (reference _patterns.py:508-529), priority 50.
+  * RMSNormPattern (reference _patterns.py:508-529), priority 50;
+  * FusedSwiGLUPattern (reference :545-609), priority 45, packed `w_gate_up`;
+  * SiluGateMulPattern (reference :532-542, replacement :180-215), priority 40.
 """
 from __future__ import annotations
 
@@ -152,7 +154,92 @@ class FusedResidualRMSNormPattern(Pattern):
         return _FusedResidualRMSNormBlockReplacement(module, _find_block_attrs(module))
 
 
+# (gate, down, up) projection names of a SwiGLU MLP (reference _patterns.py:46-49)
+_SWIGLU_ALIASES = [
+    ("w1", "w2", "w3"),
+    ("gate_proj", "down_proj", "up_proj"),
+]
+
+
+def _find_swiglu_attrs(module: nn.Module):
+    if getattr(module, "_skip_autokernel", False):
+        return None
+    for alias in _SWIGLU_ALIASES:
+        if all(hasattr(module, a) for a in alias) and isinstance(getattr(module, alias[0]), nn.Linear):
+            return alias
+    return None
+
+
+class _SiluGateMulReplacement(nn.Module):
+    """down(silu(gate(x)) * up(x)) with the activation product in one kernel
+    (`torch.ops.autokernel.silu_gate_mul`, autograd-registered) for every dtype.
+    Projections keep their attribute names (state dict unchanged)."""
+
+    def __init__(self, original: nn.Module, alias):
+        super().__init__()
+        self._alias = tuple(alias)
+        for a in alias:
+            setattr(self, a, getattr(original, a))
+        import kernels.hip._torch_ops  # noqa: F401
+        self._op = torch.ops.autokernel.silu_gate_mul
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        gate_p, down_p, up_p = (getattr(self, a) for a in self._alias)
+        gate, up = gate_p(x), up_p(x)
+        if not gate.is_cuda:
+            raise RuntimeError("autokernel SiLU-gate replacement needs CUDA tensors")
+        if up.dtype != gate.dtype:
+            dt = torch.promote_types(gate.dtype, up.dtype)
+            gate, up = gate.to(dt), up.to(dt)
+        return down_p(self._op(gate, up))
+
+
+class SiluGateMulPattern(Pattern):
+    def __init__(self):
+        super().__init__("silu_gate_mul", priority=40, op_speedup=1.6)
+
+    def matches(self, name: str, module: nn.Module, model: nn.Module) -> bool:
+        return not isinstance(module, _SiluGateMulReplacement) and _find_swiglu_attrs(module) is not None
+
+    def apply(self, name: str, module: nn.Module, model: nn.Module) -> nn.Module:
+        return _SiluGateMulReplacement(module, _find_swiglu_attrs(module))
+
+
+class _FusedSwiGLUReplacement(nn.Module):
+    """w_down(silu(gate) * up) with gate, up = w_gate_up(x).chunk(2, -1): the
+    packed projection output goes to `torch.ops.autokernel.silu_gate_mul_packed`
+    as is (no chunk copies) and its gradient comes back as one packed tensor."""
+
+    def __init__(self, original: nn.Module):
+        super().__init__()
+        self.w_gate_up = original.w_gate_up
+        self.w_down = original.w_down
+        import kernels.hip._torch_ops  # noqa: F401
+        self._op = torch.ops.autokernel.silu_gate_mul_packed
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        gu = self.w_gate_up(x)
+        if not gu.is_cuda:
+            raise RuntimeError("autokernel fused SwiGLU replacement needs CUDA tensors")
+        return self.w_down(self._op(gu.contiguous()))
+
+
+class FusedSwiGLUPattern(Pattern):
+    def __init__(self):
+        super().__init__("fused_silu_gate_mul", priority=45, op_speedup=1.6)
+
+    def matches(self, name: str, module: nn.Module, model: nn.Module) -> bool:
+        return (not isinstance(module, _FusedSwiGLUReplacement) and isinstance(getattr(module, "w_gate_up", None),
+                                                                              nn.Linear)
+                and hasattr(module, "w_down") and not getattr(module, "_skip_autokernel", False))
+
+    def apply(self, name: str, module: nn.Module, model: nn.Module) -> nn.Module:
+        return _FusedSwiGLUReplacement(module)
+
+
 ALL_PATTERNS: List[Pattern] = [
     FusedResidualRMSNormPattern(),
     RMSNormPattern(),
+    FusedSwiGLUPattern(),
+    SiluGateMulPattern(),
 ]

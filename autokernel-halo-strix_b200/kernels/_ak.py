@@ -31,6 +31,8 @@ SIGNATURES = {
     "ak_rmsnorm_bwd_noalloc": [_vp, _vp, _i, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
     "ak_fused_res_rmsnorm_fwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
     "ak_fused_res_rmsnorm_bwd": [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
+    "ak_silu_gate_mul_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_silu_gate_mul_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_softmax_fwd": [_vp, _vp, _i64, _i64, _i, _vp],
     "ak_softmax_bwd": [_vp, _vp, _vp, _i64, _i64, _i, _vp],
     "ak_ce_rows_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _i, _vp],
@@ -205,6 +207,62 @@ def fused_res_rmsnorm_bwd(hidden: torch.Tensor, w: torch.Tensor, grad_hidden: Op
     call("ak_fused_res_rmsnorm_bwd", ptr(dx), ptr(dw), _DT[dw_dtype], ptr(ws), ws_bytes, ptr(gh), ptr(gn),
          ptr(hidden), ptr(w), M, N, float(eps), dtype_code(hidden), dtype_code(w), stream(dev))
     return dx, dw
+
+
+# ---------------------------------------------------------------------------
+# SiLU gate multiply (SwiGLU body)
+# ---------------------------------------------------------------------------
+def _rows(t: torch.Tensor, cols: int) -> torch.Tensor:
+    """(rows, cols) view with unit column stride (a copy only when no such view exists)."""
+    if t.stride(-1) == 1:
+        try:
+            v = t.view(-1, cols)
+            if v.stride(1) == 1:
+                return v
+        except RuntimeError:
+            pass
+    return t.contiguous().view(-1, cols)
+
+
+def silu_gate_mul_fwd(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up; gate / up may be strided row views (e.g. halves of one packed tensor)."""
+    dev = require_cuda(gate, up)
+    if gate.shape != up.shape or gate.dtype != up.dtype:
+        raise ValueError(f"silu_gate_mul: gate {tuple(gate.shape)}/{gate.dtype} vs up {tuple(up.shape)}/{up.dtype}")
+    cols = gate.shape[-1]
+    y = torch.empty(gate.shape, dtype=gate.dtype, device=dev)
+    if gate.numel() == 0:
+        return y
+    g2, u2 = _rows(gate, cols), _rows(up, cols)
+    call("ak_silu_gate_mul_fwd", ptr(y), ptr(g2), ptr(u2), g2.shape[0], cols, g2.stride(0), u2.stride(0),
+         dtype_code(gate), stream(dev))
+    return y
+
+
+def silu_gate_mul_bwd(gate: torch.Tensor, up: torch.Tensor, dy: torch.Tensor,
+                      packed_out: Optional[torch.Tensor] = None):
+    """Returns (d gate, d up).  With `packed_out` ((..., 2*cols), contiguous) both are
+    written into its two halves and returned as views of it."""
+    dev = require_cuda(gate, up, dy)
+    cols = gate.shape[-1]
+    if packed_out is not None:
+        if packed_out.shape[-1] != 2 * cols or not packed_out.is_contiguous():
+            raise ValueError("silu_gate_mul_bwd: packed_out must be contiguous (..., 2*cols)")
+        dg, du = packed_out[..., :cols], packed_out[..., cols:]
+    else:
+        dg, du = torch.empty(gate.shape, dtype=gate.dtype, device=dev), torch.empty(gate.shape, dtype=gate.dtype,
+                                                                                     device=dev)
+    if gate.numel() == 0:
+        return dg, du
+    g2, u2 = _rows(gate, cols), _rows(up, cols)
+    y2 = _rows(dy.to(gate.dtype), cols)
+    if y2.stride(0) != cols:
+        y2 = y2.contiguous()
+    dg2, du2 = dg.view(-1, cols) if packed_out is None else packed_out.view(-1, 2 * cols)[:, :cols], \
+        du.view(-1, cols) if packed_out is None else packed_out.view(-1, 2 * cols)[:, cols:]
+    call("ak_silu_gate_mul_bwd", ptr(dg2), ptr(du2), ptr(g2), ptr(u2), ptr(y2), g2.shape[0], cols, g2.stride(0),
+         u2.stride(0), dg2.stride(0), du2.stride(0), dtype_code(gate), stream(dev))
+    return dg, du
 
 
 # ---------------------------------------------------------------------------

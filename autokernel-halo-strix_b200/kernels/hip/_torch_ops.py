@@ -9,6 +9,7 @@ Mirrors kernels/hip/_torch_ops.py of the reference:
     (d dA, d dBx, dC, dD, dx));
   * `torch.ops.autokernel.fused_res_rmsnorm(x, residual, weight) ->
     (hidden, normed)` (reference :238-303);
+  * `torch.ops.autokernel.silu_gate_mul(gate, up) -> y` (reference :181-231);
   * `torch.ops.autokernel.causal_conv1d(x, weight, bias) -> y` (reference
     :883-975).
 Added here (no reference counterpart):
@@ -16,7 +17,8 @@ Added here (no reference counterpart):
     and no autocast cast, used by the module replacement;
   * `autokernel::softmax(x)` — differentiable row softmax;
   * `autokernel::fused_res_rmsnorm_eps(x, residual, weight, eps)` and
-    `autokernel::causal_conv1d_silu(x, weight, bias)`;
+    `autokernel::causal_conv1d_silu(x, weight, bias)`,
+    `autokernel::silu_gate_mul_packed(gate_up)`;
   * the backward passes as their own custom ops (`*_bwd`), so torch.compile
     sees opaque nodes in both directions instead of tracing into ctypes calls.
 
@@ -265,6 +267,87 @@ def _(x, residual, weight, eps):
 
 
 fused_res_rmsnorm_eps_op.register_autograd(_res_backward_eps, setup_context=_res_setup)
+
+
+# ---------------------------------------------------------------------------
+# SiLU gate multiply — reference _torch_ops.py:181-231:
+# `autokernel::silu_gate_mul(gate, up) -> silu(gate) * up`, grads (d gate, d up),
+# autocast cuda/fp16.  `silu_gate_mul_packed(gate_up)` (added) takes the packed
+# (..., 2H) projection output and returns one packed (..., 2H) gradient.
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::silu_gate_mul_bwd", mutates_args=())
+def silu_gate_mul_bwd_op(gate: torch.Tensor, up: torch.Tensor, grad: torch.Tensor) -> List[torch.Tensor]:
+    return list(_ak.silu_gate_mul_bwd(gate, up, grad))
+
+
+@silu_gate_mul_bwd_op.register_fake
+def _(gate, up, grad):
+    return [torch.empty_like(gate), torch.empty_like(up)]
+
+
+@torch.library.custom_op("autokernel::silu_gate_mul", mutates_args=())
+def silu_gate_mul_op(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    return _ak.silu_gate_mul_fwd(gate, up)
+
+
+@silu_gate_mul_op.register_fake
+def _(gate, up):
+    return gate.new_empty(gate.shape)
+
+
+def _sgm_setup(ctx, inputs, output):
+    ctx.save_for_backward(*inputs)
+
+
+def _sgm_backward(ctx, grad):
+    gate, up = ctx.saved_tensors
+    dg, du = silu_gate_mul_bwd_op(gate, up, grad.contiguous())
+    return dg, du
+
+
+silu_gate_mul_op.register_autograd(_sgm_backward, setup_context=_sgm_setup)
+try:
+    silu_gate_mul_op.register_autocast("cuda", torch.float16)
+except AttributeError:  # pragma: no cover - older torch
+    pass
+
+
+@torch.library.custom_op("autokernel::silu_gate_mul_packed_bwd", mutates_args=())
+def silu_gate_mul_packed_bwd_op(gate_up: torch.Tensor, grad: torch.Tensor) -> torch.Tensor:
+    H = gate_up.shape[-1] // 2
+    out = torch.empty(gate_up.shape, dtype=gate_up.dtype, device=gate_up.device)
+    _ak.silu_gate_mul_bwd(gate_up[..., :H], gate_up[..., H:], grad, packed_out=out)
+    return out
+
+
+@silu_gate_mul_packed_bwd_op.register_fake
+def _(gate_up, grad):
+    return torch.empty_like(gate_up)
+
+
+@torch.library.custom_op("autokernel::silu_gate_mul_packed", mutates_args=())
+def silu_gate_mul_packed_op(gate_up: torch.Tensor) -> torch.Tensor:
+    H = gate_up.shape[-1] // 2
+    return _ak.silu_gate_mul_fwd(gate_up[..., :H], gate_up[..., H:])
+
+
+@silu_gate_mul_packed_op.register_fake
+def _(gate_up):
+    return gate_up.new_empty((*gate_up.shape[:-1], gate_up.shape[-1] // 2))
+
+
+def _sgmp_setup(ctx, inputs, output):
+    ctx.save_for_backward(inputs[0])
+
+
+def _sgmp_backward(ctx, grad):
+    (gate_up,) = ctx.saved_tensors
+    return silu_gate_mul_packed_bwd_op(gate_up, grad.contiguous())
+
+
+silu_gate_mul_packed_op.register_autograd(_sgmp_backward, setup_context=_sgmp_setup)
 
 
 # ---------------------------------------------------------------------------

@@ -270,7 +270,7 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
 
 def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768):
     """Device-timed throughput of the other swapped ops at their BASELINE configs.
-    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "fused_res", "conv1d"} (None = all)."""
+    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "fused_res", "silu_gate", "conv1d"} (None = all)."""
     from kernels import _ak
     res = {}
     st = torch.cuda.current_stream(dev)
@@ -399,6 +399,18 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         timeit(lambda: _ak.fused_res_rmsnorm_bwd(hr_, wr_, ghr, gnr), 8 * E, "fused_res_rmsnorm_bwd_bf16_65536x768",
                steps, graph=True)
         del xr_, rr_, ghr, gnr, hr_
+        torch.cuda.empty_cache()
+
+    if want("silu_gate"):
+        # SiLU gate multiply bf16 [65536, 2048] (the hybrid's SwiGLU hidden width; 268 MB per tensor):
+        # fwd reads gate, up, writes y; bwd reads gate, up, dy, writes d gate, d up.
+        Ms, Hs = 65536, 2048
+        gs_, us_, dys = (torch.randn(Ms, Hs, device=dev).to(torch.bfloat16) for _ in range(3))
+        E = Ms * Hs
+        timeit(lambda: _ak.silu_gate_mul_fwd(gs_, us_), 6 * E, "silu_gate_mul_fwd_bf16_65536x2048", steps, graph=True)
+        timeit(lambda: _ak.silu_gate_mul_bwd(gs_, us_, dys), 10 * E, "silu_gate_mul_bwd_bf16_65536x2048", steps,
+               graph=True)
+        del gs_, us_, dys
         torch.cuda.empty_cache()
 
     if want("conv1d"):
@@ -570,7 +582,7 @@ def main():
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
-    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,fused_res,conv1d")
+    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,fused_res,silu_gate,conv1d")
     ap.add_argument("--ce-rows", type=int, default=32768, help="with --only-ops: rows of the linear+CE case")
     ap.add_argument("--batch", type=int, default=0, help="override the headline batch (small-case profiling)")
     args = ap.parse_args()

@@ -273,6 +273,26 @@ AK_API int ak_fused_res_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspa
                                     const void* w, int64_t M, int64_t N, float eps,
                                     int dt_x, int dt_w, void* stream);
 
+/* ---- SiLU gate multiply (SwiGLU body) -------------------------------------
+ * y = silu(gate) * up over rows x cols; gate / up rows start ld_gate / ld_up
+ * elements apart (cols for dense tensors, 2*cols for the halves of one packed
+ * gate_up projection); y is dense (ld = cols).  All dt.
+ * Replaces silu_gate_mul_hip (kernels/hip/silu_gate_mul.py:102-118) behind
+ * autokernel::silu_gate_mul (kernels/hip/_torch_ops.py:181-186). */
+AK_API int ak_silu_gate_mul_fwd(void* y, const void* gate, const void* up,
+                                int64_t rows, int64_t cols, int64_t ld_gate,
+                                int64_t ld_up, int dt, void* stream);
+
+/* d gate = dy * up * silu'(gate), d up = dy * silu(gate); dgate / dup rows
+ * ld_dgate / ld_dup apart (2*cols writes one packed d gate_up).  Replaces
+ * silu_gate_mul_backward_hip (kernels/hip/silu_gate_mul_backward.py:145-180)
+ * and the fp32 branch of _silu_gate_mul_backward (_torch_ops.py:199-218). */
+AK_API int ak_silu_gate_mul_bwd(void* dgate, void* dup, const void* gate,
+                                const void* up, const void* dy, int64_t rows,
+                                int64_t cols, int64_t ld_gate, int64_t ld_up,
+                                int64_t ld_dgate, int64_t ld_dup, int dt,
+                                void* stream);
+
 /* ---- Depthwise causal conv1d (+ optional SiLU) --------------------------
  * y[b,d,t] = act(bias[d] + sum_k w[d,k] x[b,d,t-K+1+k]), x = 0 before t = 0;
  * act = SiLU when silu != 0, identity otherwise.  x, y: (B, D, T) dt, T

@@ -265,3 +265,20 @@ def fused_res_rmsnorm_bwd(hidden, w, grad_hidden, grad_normed, eps: float = 1e-6
     if grad_hidden is not None:
         dx = dx + _c(grad_hidden, dt)
     return dx, dw
+
+
+# ---------------------------------------------------------------------------
+# SiLU gate multiply — kernels/hip/silu_gate_mul.py:102-118 (fp32 branch
+# F.silu(gate) * up); backward kernels/hip/_torch_ops.py:199-218 and
+# kernels/hip/silu_gate_mul_backward.py:160-168.
+# ---------------------------------------------------------------------------
+def silu_gate_mul(gate, up, dt=DEFAULT):
+    g, u = _c(gate, dt), _c(up, dt)
+    return g * torch.sigmoid(g) * u
+
+
+def silu_gate_mul_bwd(gate, up, dy, dt=DEFAULT):
+    """Returns (d gate, d up)."""
+    g, u, gy = _c(gate, dt), _c(up, dt), _c(dy, dt)
+    s = torch.sigmoid(g)
+    return gy * u * s * (1 + g * (1 - s)), gy * g * s

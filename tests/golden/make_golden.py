@@ -22,6 +22,9 @@ read-only is fine).  Every output stored here comes from the reference's code:
                    (+ autograd, plus grad_hidden for the hidden output),
                    _torch_ops._fused_res_rmsnorm_backward (:262-290) and
                    kernels/hip/fused_residual_rmsnorm_backward.kernel_fn (:265-281)
+  silu_gate.npz    kernels/hip/silu_gate_mul.kernel_fn (fp32 branch, :102-110),
+                   _torch_ops._silu_gate_mul_backward (:199-218),
+                   kernels/hip/silu_gate_mul_backward.kernel_fn (:160-168), autograd
   linear_ce.npz    F.linear + F.cross_entropy(ignore_index) fp32 + autograd, the
                    oracle of scripts/test_chunked_ce.py:13-39
 The fixtures are committed; the GPU box never needs the reference.
@@ -207,6 +210,22 @@ def main() -> None:
                         grad_normed=_np(gna), hidden=_np(hid), normed=_np(nrm), single=_np(single),
                         ref_fn=_np(ref_fn), dx_op=_np(gx), dres_op=_np(gr), dw_op=_np(gw), dx_kfn=_np(bx),
                         dres_kfn=_np(br), dw_kfn=_np(bw))
+
+    # ---------------- SiLU gate multiply (fp32 branches of the reference)
+    from kernels.hip import silu_gate_mul as rsg
+    from kernels.hip import silu_gate_mul_backward as rsgb
+    g = torch.Generator().manual_seed(7)
+    gs_ = 3 * torch.randn(64, 520, generator=g)
+    us_ = torch.randn(64, 520, generator=g)
+    dys = torch.randn(64, 520, generator=g)
+    ysg = rsg.kernel_fn(_on_cuda(gs_), _on_cuda(us_))
+    dg_op, du_op = rops._silu_gate_mul_backward(_Ctx((gs_, us_)), dys)
+    dg_k, du_k = rsgb.kernel_fn(_on_cuda(gs_), _on_cuda(us_), _on_cuda(dys))
+    ga, ua = gs_.clone().requires_grad_(True), us_.clone().requires_grad_(True)
+    (torch.nn.functional.silu(ga) * ua).backward(dys)
+    np.savez_compressed(HERE / "silu_gate.npz", gate=_np(gs_), up=_np(us_), dy=_np(dys), y=_np(ysg),
+                        dgate_op=_np(dg_op), dup_op=_np(du_op), dgate_kfn=_np(dg_k), dup_kfn=_np(du_k),
+                        dgate_autograd=_np(ga.grad), dup_autograd=_np(ua.grad))
 
     # ---------------- causal conv1d (reference op; T crosses the 256-step kernel chunk)
     g = torch.Generator().manual_seed(5)

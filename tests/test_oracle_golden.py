@@ -137,3 +137,14 @@ def test_reference_fused_res_fallback_dx_differs_by_missing_rstd():
     for k in ("dx_op", "dres_op", "dx_kfn", "dres_kfn"):
         assert_fp32_close(buggy, g[k], rtol=1e-5, what=k)
     assert (torch.from_numpy(g["dx_op"]).double() - torch.from_numpy(g["dx_autograd"]).double()).abs().max() > 1e-3
+
+
+def test_silu_gate_mul_golden():
+    g = golden("silu_gate")
+    gate, up, dy = (torch.from_numpy(g[k]) for k in ("gate", "up", "dy"))
+    assert_fp32_close(O.silu_gate_mul(gate, up), g["y"], what="y")
+    dg, du = O.silu_gate_mul_bwd(gate, up, dy)
+    for k in ("dgate_op", "dgate_kfn", "dgate_autograd"):
+        assert_fp32_close(dg, g[k], what=k)
+    for k in ("dup_op", "dup_kfn", "dup_autograd"):
+        assert_fp32_close(du, g[k], what=k)

@@ -3,8 +3,9 @@ import torch
 import torch.nn as nn
 
 import autokernel
-from autokernel._patterns import (FusedResidualRMSNormPattern, RMSNormPattern, _FusedResidualRMSNormBlockReplacement,
-                                  _RMSNormReplacement)
+from autokernel._patterns import (FusedResidualRMSNormPattern, FusedSwiGLUPattern, RMSNormPattern,
+                                  SiluGateMulPattern, _FusedResidualRMSNormBlockReplacement, _FusedSwiGLUReplacement,
+                                  _RMSNormReplacement, _SiluGateMulReplacement)
 
 
 class RMSNorm(nn.Module):
@@ -27,7 +28,7 @@ class Block(nn.Module):
 
 
 def test_list_patterns():
-    assert autokernel.list_patterns() == ["fused_residual_rmsnorm", "rmsnorm"]
+    assert autokernel.list_patterns() == ["fused_residual_rmsnorm", "rmsnorm", "fused_silu_gate_mul", "silu_gate_mul"]
 
 
 def test_optimize_replaces_rmsnorms_and_keeps_parameters(monkeypatch):
@@ -119,3 +120,28 @@ def test_fused_residual_block_pattern(monkeypatch):
     assert isinstance(m[0], TransformerBlock) and isinstance(m[0].attention_norm, RMSNorm)
     p = FusedResidualRMSNormPattern()
     assert p.matches("b", TransformerBlock(), None) and not p.matches("b", Block(), None)
+
+
+class SwiGLU(nn.Module):
+    def __init__(self, d=16, h=32):
+        super().__init__()
+        self.w1, self.w2, self.w3 = nn.Linear(d, h), nn.Linear(h, d), nn.Linear(d, h)
+
+
+class PackedSwiGLU(nn.Module):
+    def __init__(self, d=16, h=32):
+        super().__init__()
+        self.w_gate_up, self.w_down = nn.Linear(d, 2 * h), nn.Linear(h, d)
+
+
+def test_swiglu_patterns(monkeypatch):
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    m = nn.Sequential(SwiGLU(), PackedSwiGLU())
+    keys = set(m.state_dict())
+    autokernel.optimize(m, training=True)
+    assert isinstance(m[0], _SiluGateMulReplacement) and isinstance(m[1], _FusedSwiGLUReplacement)
+    assert set(m.state_dict()) == keys
+    rep = autokernel.report(m)["patterns"]
+    assert rep["silu_gate_mul"]["modules_replaced"] == 1 and rep["fused_silu_gate_mul"]["modules_replaced"] == 1
+    assert SiluGateMulPattern().matches("s", SwiGLU(), None) and not SiluGateMulPattern().matches("s", Block(), None)
+    assert FusedSwiGLUPattern().matches("s", PackedSwiGLU(), None)
