@@ -5,6 +5,8 @@
 (autokernel/_patterns.py:22-33).  The pattern set here is the hot-path one:
   * FusedResidualRMSNormPattern (reference _patterns.py:473-485, replacement
     :364-398, block detection :51-56,102-118), priority 100;
+  * FusedQKVPattern (reference _patterns.py:488-505, replacement :216-361),
+    priority 90: one QKV GEMM, RoPE + head-major transpose in one kernel;
   * RMSNormPattern (reference _patterns.py:508-529), priority 50;
   * FusedSwiGLUPattern (reference :545-609), priority 45, packed `w_gate_up`;
   * SiluGateMulPattern (reference :532-542, replacement :180-215), priority 40.
@@ -16,6 +18,7 @@ from typing import List
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 
 @dataclass
@@ -237,8 +240,124 @@ class FusedSwiGLUPattern(Pattern):
         return _FusedSwiGLUReplacement(module)
 
 
+# (q, k, v, o) projection names (reference _patterns.py:41-44)
+_QKV_ALIASES = [
+    ("wq", "wk", "wv", "wo"),
+    ("q_proj", "k_proj", "v_proj", "o_proj"),
+]
+
+
+def _find_qkv_attrs(module: nn.Module):
+    if getattr(module, "_skip_autokernel", False):
+        return None
+    for alias in _QKV_ALIASES:
+        if all(hasattr(module, a) for a in alias) and all(isinstance(getattr(module, a), nn.Linear)
+                                                          for a in alias):
+            return alias
+    return None
+
+
+def _find_complex_freqs(model: nn.Module):
+    """Complex `freqs_cis` buffer of the model, if any (reference _patterns.py:133-138)."""
+    if model is None:
+        return None
+    for bname, buf in model.named_buffers():
+        if "freqs_cis" in bname and buf.is_complex():
+            return buf
+    return None
+
+
+def _rope_theta(module: nn.Module):
+    for a in ("rope_theta", "theta"):
+        v = getattr(module, a, None)
+        if isinstance(v, (int, float)):
+            return float(v)
+    return None
+
+
+class _FusedQKVAttentionReplacement(nn.Module):
+    """Causal GQA attention with one QKV GEMM and the RoPE kernel.
+
+    forward(x, freqs_cis=None): qkv = x [Wq; Wk; Wv]^T in one GEMM (the
+    concatenation is taken from the original Parameters each call, so state
+    dict, optimizer state and gradients stay on them); q and k are rotated
+    straight out of the packed qkv rows by `torch.ops.autokernel.rotary_emb_fp32`
+    (strided read, dense head-major write: no transpose copies); then
+    scaled_dot_product_attention(is_causal=True, enable_gqa) and the output
+    projection.  RoPE tables: the complex `freqs_cis` argument or model buffer
+    (reference :216-361), else cos / sin of the module's `rope_theta`
+    (interleaved pairs, theta^(-2i/D)), cached per length and device.
+    """
+
+    def __init__(self, original: nn.Module, alias, freqs_cis=None):
+        super().__init__()
+        self._alias = tuple(alias)
+        for a in alias:
+            setattr(self, a, getattr(original, a))
+        q_proj = getattr(original, alias[0])
+        self.n_heads = int(getattr(original, "n_heads", getattr(original, "num_heads", 1)))
+        self.n_kv_heads = int(getattr(original, "n_kv_heads", getattr(original, "num_key_value_heads",
+                                                                       self.n_heads)))
+        self.head_dim = int(getattr(original, "head_dim", q_proj.out_features // self.n_heads))
+        self.theta = _rope_theta(original)
+        self._freqs = freqs_cis
+        self._tables = {}
+        import kernels.hip._torch_ops  # noqa: F401
+        self._rope = torch.ops.autokernel.rotary_emb_fp32
+
+    def _cos_sin(self, T: int, device, freqs_cis):
+        f = freqs_cis if freqs_cis is not None and torch.is_tensor(freqs_cis) and freqs_cis.is_complex() \
+            else self._freqs
+        if f is not None:
+            f = f[:T].to(device)
+            return f.real.float().contiguous(), f.imag.float().contiguous()
+        key = (T, str(device))
+        if key not in self._tables:
+            hd = self.head_dim
+            inv = 1.0 / (self.theta ** (torch.arange(0, hd, 2, device=device, dtype=torch.float32) / hd))
+            ang = torch.outer(torch.arange(T, device=device, dtype=torch.float32), inv)
+            self._tables[key] = (ang.cos(), ang.sin())
+        return self._tables[key]
+
+    def forward(self, x: torch.Tensor, freqs_cis=None, **kwargs) -> torch.Tensor:
+        wq, wk, wv, wo = (getattr(self, a) for a in self._alias)
+        if not x.is_cuda:
+            raise RuntimeError("autokernel fused QKV attention needs CUDA tensors")
+        B, T, _ = x.shape
+        H, KH, hd = self.n_heads, self.n_kv_heads, self.head_dim
+        w = torch.cat([wq.weight, wk.weight, wv.weight], dim=0)
+        b = None
+        if wq.bias is not None or wk.bias is not None or wv.bias is not None:
+            b = torch.cat([p.bias if p.bias is not None else p.weight.new_zeros(p.out_features) for p in (wq, wk, wv)])
+        qkv = F.linear(x, w, b)
+        qs, ks = H * hd, KH * hd
+        q = qkv[..., :qs].view(B, T, H, hd).transpose(1, 2)
+        k = qkv[..., qs:qs + ks].view(B, T, KH, hd).transpose(1, 2)
+        v = qkv[..., qs + ks:].view(B, T, KH, hd).transpose(1, 2)
+        cos, sin = self._cos_sin(T, x.device, freqs_cis)
+        q = self._rope(q, cos, sin).to(qkv.dtype)
+        k = self._rope(k, cos, sin).to(qkv.dtype)
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=(H != KH))
+        return wo(o.transpose(1, 2).reshape(B, T, H * hd))
+
+
+class FusedQKVPattern(Pattern):
+    def __init__(self):
+        super().__init__("fused_qkv", priority=90, op_speedup=1.3)
+
+    def matches(self, name: str, module: nn.Module, model: nn.Module) -> bool:
+        if isinstance(module, _FusedQKVAttentionReplacement) or _find_qkv_attrs(module) is None:
+            return False
+        # RoPE needs tables: a theta on the module or a complex freqs_cis buffer on the model
+        return _rope_theta(module) is not None or _find_complex_freqs(model) is not None
+
+    def apply(self, name: str, module: nn.Module, model: nn.Module) -> nn.Module:
+        return _FusedQKVAttentionReplacement(module, _find_qkv_attrs(module), _find_complex_freqs(model))
+
+
 ALL_PATTERNS: List[Pattern] = [
     FusedResidualRMSNormPattern(),
+    FusedQKVPattern(),
     RMSNormPattern(),
     FusedSwiGLUPattern(),
     SiluGateMulPattern(),

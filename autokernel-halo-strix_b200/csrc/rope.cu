@@ -1,0 +1,161 @@
+// Rotary position embedding (interleaved pairs) forward / backward, sm_100a.
+//
+// Semantics: reference.rotary_embedding_ref (reference.py:63-69) and
+// kernels/hip/rotary_embedding.py kernel_fn / kernel_fn_fp32 (:253-300):
+//   y[..., 2i]   = x[..., 2i] * cos[n, i] - x[..., 2i+1] * sin[n, i]
+//   y[..., 2i+1] = x[..., 2i] * sin[n, i] + x[..., 2i+1] * cos[n, i]
+// fp32 arithmetic with fp32 cos / sin tables of shape (N, D/2), one rounding.
+// The backward is the rotation by -theta on the same pairs (sign = -1):
+//   dx[2i] = g[2i] c + g[2i+1] s,   dx[2i+1] = -g[2i] s + g[2i+1] c.
+//
+// Layout: x is read through arbitrary (b, h, n) element strides with unit
+// stride along D, so q / k can be read straight out of a fused (B, N, W) QKV
+// projection; y is written dense (B, H, N, D).  The head-major transpose that
+// attention wants costs nothing extra.  One thread rotates one 16-byte vector
+// (8 elements of a 16-bit type, 4 of fp32).
+#include "ak_common.cuh"
+
+namespace ak {
+namespace {
+
+constexpr int kThreadsR = 256;
+
+constexpr int kPerThread = 1;  // 16-byte vectors per thread (occupancy beats per-thread depth here)
+
+// Vector path: grid.y walks the B*H (b, h) planes, grid.x the N*D/VEC vectors
+// of one plane (32-bit index math); tables are read as float4 when VEC/2 == 4.
+template <typename T, int VEC>
+__global__ void __launch_bounds__(kThreadsR, 8)
+rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
+            int64_t planes, int H, int N, int D, int64_t sb, int64_t sh, int64_t sn_, float sign, bool tab4) {
+  const int vpr = D / VEC;
+  const int per_plane = N * vpr;
+  const int half = D / 2;
+  for (int64_t p = blockIdx.y; p < planes; p += gridDim.y) {
+    const int64_t b = p / H;
+    const int h = (int)(p - b * H);
+    const T* xp = x + b * sb + h * sh;
+    T* yp = y + p * (int64_t)N * D;
+    float v[kPerThread][VEC];
+    int nn[kPerThread], jj[kPerThread];
+#pragma unroll
+    for (int u = 0; u < kPerThread; ++u) {
+      const int idx = (blockIdx.x * kPerThread + u) * kThreadsR + threadIdx.x;
+      nn[u] = idx / vpr;
+      jj[u] = (idx - nn[u] * vpr) * VEC;
+      if (idx < per_plane) load_frag<T, VEC>(v[u], xp + (int64_t)nn[u] * sn_ + jj[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < kPerThread; ++u) {
+      const int idx = (blockIdx.x * kPerThread + u) * kThreadsR + threadIdx.x;
+      if (idx >= per_plane) break;
+      const int n = nn[u], jb = jj[u];
+      float c[VEC / 2], s[VEC / 2];
+      const float* cr = cs + (int64_t)n * half + jb / 2;
+      const float* sr = sn + (int64_t)n * half + jb / 2;
+      if constexpr (VEC / 2 == 4) {
+        if (tab4) {
+          const float4 c4 = __ldg(reinterpret_cast<const float4*>(cr));
+          const float4 s4 = __ldg(reinterpret_cast<const float4*>(sr));
+          c[0] = c4.x; c[1] = c4.y; c[2] = c4.z; c[3] = c4.w;
+          s[0] = s4.x; s[1] = s4.y; s[2] = s4.z; s[3] = s4.w;
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) { c[k] = __ldg(cr + k); s[k] = __ldg(sr + k); }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < VEC / 2; ++k) { c[k] = __ldg(cr + k); s[k] = __ldg(sr + k); }
+      }
+      float o[VEC];
+#pragma unroll
+      for (int k = 0; k < VEC / 2; ++k) {
+        const float sk = sign * s[k];
+        o[2 * k] = v[u][2 * k] * c[k] - v[u][2 * k + 1] * sk;
+        o[2 * k + 1] = v[u][2 * k] * sk + v[u][2 * k + 1] * c[k];
+      }
+      store_frag<T, VEC>(yp + (int64_t)n * D + jb, o);
+    }
+  }
+}
+
+// Scalar path (one pair per thread) for D not a multiple of the vector width.
+template <typename T>
+__global__ void __launch_bounds__(kThreadsR)
+rope_pair_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict__ cs,
+                 const float* __restrict__ sn, int64_t rows, int H, int N, int D, int64_t sb, int64_t sh,
+                 int64_t sn_, float sign) {
+  const int half = D / 2;
+  const int64_t total = rows * half;
+  for (int64_t t = (int64_t)blockIdx.x * kThreadsR + threadIdx.x; t < total; t += (int64_t)gridDim.x * kThreadsR) {
+    const int64_t row = t / half;
+    const int i = (int)(t - row * half);
+    const int n = (int)(row % N);
+    const int64_t bh = row / N;
+    const int h = (int)(bh % H);
+    const int64_t b = bh / H;
+    const T* xr = x + b * sb + h * sh + (int64_t)n * sn_;
+    const float x0 = to_f<T>(xr[2 * i]), x1 = to_f<T>(xr[2 * i + 1]);
+    const float c = cs[(int64_t)n * half + i], s = sign * sn[(int64_t)n * half + i];
+    y[row * D + 2 * i] = from_f<T>(x0 * c - x1 * s);
+    y[row * D + 2 * i + 1] = from_f<T>(x0 * s + x1 * c);
+  }
+}
+
+int rope_impl(void* y, const void* x, const float* cos_t, const float* sin_t, int64_t B, int64_t H, int64_t N,
+              int64_t D, int64_t sb, int64_t sh, int64_t sn, float sign, int dt, cudaStream_t st, const char* who) {
+  AK_REQUIRE(B >= 0 && H > 0 && N > 0 && D > 0 && D % 2 == 0 && H < (1LL << 31) && N < (1LL << 31) &&
+                 D < (1LL << 31),
+             AK_ERR_SHAPE, "%s: bad shape B=%lld H=%lld N=%lld D=%lld (D must be even)", who, (long long)B,
+             (long long)H, (long long)N, (long long)D);
+  if (B == 0) return AK_OK;
+  AK_REQUIRE(y && x && cos_t && sin_t, AK_ERR_ARG, "%s: null pointer", who);
+  const int64_t rows = B * H * N;
+  const int es = elem_size(dt);
+  const int vecw = 16 / es;
+  const bool vec_ok = D % vecw == 0 && aligned16(x) && aligned16(y) && (sb * es) % 16 == 0 && (sh * es) % 16 == 0 &&
+                      (sn * es) % 16 == 0;
+  const bool tab4 = aligned16(cos_t) && aligned16(sin_t) && (D / 2) % 4 == 0;
+  AK_REQUIRE(!vec_ok || N * (D / vecw) < (1LL << 31), AK_ERR_SHAPE, "%s: N*D too large", who);
+  AK_DISPATCH_DTYPE(dt, T, {
+    constexpr int VEC = 16 / sizeof(T);
+    if (vec_ok) {
+      const int64_t per_plane = N * (D / VEC);
+      const unsigned gx = (unsigned)((per_plane + (int64_t)kThreadsR * kPerThread - 1) / ((int64_t)kThreadsR * kPerThread));
+      const int64_t planes = B * H;
+      const unsigned gy = (unsigned)(planes < 65535 ? planes : 65535);
+      rope_kernel<T, VEC><<<dim3(gx, gy), kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes, (int)H,
+                                                             (int)N, (int)D, sb, sh, sn, sign, tab4);
+    } else {
+      int64_t g = (rows * (D / 2) + kThreadsR - 1) / kThreadsR;
+      const int64_t cap = (int64_t)sm_count() * 32;
+      if (g > cap) g = cap;
+      if (g < 1) g = 1;
+      rope_pair_kernel<T><<<(unsigned)g, kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, rows, (int)H, (int)N,
+                                                            (int)D, sb, sh, sn, sign);
+    }
+  });
+  AK_CHECK_LAUNCH(who);
+  return AK_OK;
+}
+
+}  // namespace
+}  // namespace ak
+
+using namespace ak;
+
+extern "C" int ak_rope_fwd(void* y, const void* x, const float* cos_t, const float* sin_t, int64_t B, int64_t H,
+                           int64_t N, int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_n, int dt,
+                           void* stream) {
+  clear_error();
+  return rope_impl(y, x, cos_t, sin_t, B, H, N, D, stride_b, stride_h, stride_n, 1.f, dt, (cudaStream_t)stream,
+                   "ak_rope_fwd");
+}
+
+extern "C" int ak_rope_bwd(void* dx, const void* dy, const float* cos_t, const float* sin_t, int64_t B, int64_t H,
+                           int64_t N, int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_n, int dt,
+                           void* stream) {
+  clear_error();
+  return rope_impl(dx, dy, cos_t, sin_t, B, H, N, D, stride_b, stride_h, stride_n, -1.f, dt, (cudaStream_t)stream,
+                   "ak_rope_bwd");
+}

@@ -83,23 +83,24 @@ def apply_rope(x, cos, sin):
 class GQAAttention(nn.Module):
     def __init__(self, cfg: HybridConfig):
         super().__init__()
-        self.nh, self.nkv = cfg.n_heads, cfg.n_kv_heads
-        self.hd = cfg.d_model // cfg.n_heads
-        self.wq = nn.Linear(cfg.d_model, self.nh * self.hd, bias=False)
-        self.wk = nn.Linear(cfg.d_model, self.nkv * self.hd, bias=False)
-        self.wv = nn.Linear(cfg.d_model, self.nkv * self.hd, bias=False)
-        self.wo = nn.Linear(self.nh * self.hd, cfg.d_model, bias=False)
-        self.theta = cfg.rope_theta
+        self.n_heads, self.n_kv_heads = cfg.n_heads, cfg.n_kv_heads
+        self.head_dim = cfg.d_model // cfg.n_heads
+        self.wq = nn.Linear(cfg.d_model, self.n_heads * self.head_dim, bias=False)
+        self.wk = nn.Linear(cfg.d_model, self.n_kv_heads * self.head_dim, bias=False)
+        self.wv = nn.Linear(cfg.d_model, self.n_kv_heads * self.head_dim, bias=False)
+        self.wo = nn.Linear(self.n_heads * self.head_dim, cfg.d_model, bias=False)
+        self.rope_theta = cfg.rope_theta
 
     def forward(self, x):
         B, T, _ = x.shape
-        q = self.wq(x).view(B, T, self.nh, self.hd).transpose(1, 2)
-        k = self.wk(x).view(B, T, self.nkv, self.hd).transpose(1, 2)
-        v = self.wv(x).view(B, T, self.nkv, self.hd).transpose(1, 2)
-        cos, sin = rope_tables(T, self.hd, self.theta, x.device)
+        H, KH, hd = self.n_heads, self.n_kv_heads, self.head_dim
+        q = self.wq(x).view(B, T, H, hd).transpose(1, 2)
+        k = self.wk(x).view(B, T, KH, hd).transpose(1, 2)
+        v = self.wv(x).view(B, T, KH, hd).transpose(1, 2)
+        cos, sin = rope_tables(T, hd, self.rope_theta, x.device)
         q, k = apply_rope(q, cos, sin), apply_rope(k, cos, sin)
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
-        return self.wo(o.transpose(1, 2).reshape(B, T, self.nh * self.hd))
+        return self.wo(o.transpose(1, 2).reshape(B, T, H * hd))
 
 
 def _default_scan():

@@ -33,6 +33,8 @@ SIGNATURES = {
     "ak_fused_res_rmsnorm_bwd": [_vp, _vp, _i, _vp, _sz, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i, _i, _vp],
     "ak_silu_gate_mul_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_silu_gate_mul_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_rope_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_rope_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_softmax_fwd": [_vp, _vp, _i64, _i64, _i, _vp],
     "ak_softmax_bwd": [_vp, _vp, _vp, _i64, _i64, _i, _vp],
     "ak_ce_rows_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _i, _vp],
@@ -263,6 +265,43 @@ def silu_gate_mul_bwd(gate: torch.Tensor, up: torch.Tensor, dy: torch.Tensor,
     call("ak_silu_gate_mul_bwd", ptr(dg2), ptr(du2), ptr(g2), ptr(u2), ptr(y2), g2.shape[0], cols, g2.stride(0),
          u2.stride(0), dg2.stride(0), du2.stride(0), dtype_code(gate), stream(dev))
     return dg, du
+
+
+# ---------------------------------------------------------------------------
+# Rotary position embedding (interleaved pairs), x (B, H, N, D)
+# ---------------------------------------------------------------------------
+def _rope_tables(t: torch.Tensor, N: int, D: int) -> torch.Tensor:
+    """fp32 (N, D/2) table from any (..., N', D/2) broadcast form with N' >= N."""
+    if t.shape[-1] != D // 2:
+        raise ValueError(f"rotary: tables must have last dim D/2 = {D // 2} (interleaved pairs), got {t.shape[-1]}")
+    t2 = t.detach().float().reshape(-1, D // 2) if t.dim() != 2 else t.float()
+    if t2.shape[0] < N:
+        raise ValueError(f"rotary: table has {t2.shape[0]} positions < sequence length {N}")
+    return t2[:N].contiguous()
+
+
+def _rope(name: str, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    dev = require_cuda(x, cos, sin)
+    if x.dim() != 4:
+        raise ValueError(f"rotary: x must be (B, H, N, D), got {tuple(x.shape)}")
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    B, H, N, D = x.shape
+    c, s = _rope_tables(cos, N, D), _rope_tables(sin, N, D)
+    y = torch.empty((B, H, N, D), dtype=x.dtype, device=dev)
+    if x.numel():
+        call(name, ptr(y), ptr(x), ptr(c), ptr(s), B, H, N, D, x.stride(0), x.stride(1), x.stride(2), dtype_code(x),
+             stream(dev))
+    return y
+
+
+def rope_fwd(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotate interleaved pairs of x (B, H, N, D; any strides with unit D stride) -> dense (B, H, N, D)."""
+    return _rope("ak_rope_fwd", x, cos, sin)
+
+
+def rope_bwd(dy: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    return _rope("ak_rope_bwd", dy, cos, sin)
 
 
 # ---------------------------------------------------------------------------

@@ -10,6 +10,8 @@ Mirrors kernels/hip/_torch_ops.py of the reference:
   * `torch.ops.autokernel.fused_res_rmsnorm(x, residual, weight) ->
     (hidden, normed)` (reference :238-303);
   * `torch.ops.autokernel.silu_gate_mul(gate, up) -> y` (reference :181-231);
+  * `torch.ops.autokernel.rotary_emb_fp32(x, cos, sin) -> y` (reference
+    :112-169);
   * `torch.ops.autokernel.causal_conv1d(x, weight, bias) -> y` (reference
     :883-975).
 Added here (no reference counterpart):
@@ -348,6 +350,51 @@ def _sgmp_backward(ctx, grad):
 
 
 silu_gate_mul_packed_op.register_autograd(_sgmp_backward, setup_context=_sgmp_setup)
+
+
+# ---------------------------------------------------------------------------
+# Rotary embedding — reference _torch_ops.py:112-169:
+# `autokernel::rotary_emb_fp32(x (B, H, N, D), cos, sin) -> y`, interleaved
+# pairs, tables (N, D/2) fp32, autocast rule cuda/fp32.  The backward is the
+# exact gradient of that forward (rotation by -theta); the reference's backward
+# uses the rotate-half pairing instead.
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::rotary_emb_fp32_bwd", mutates_args=())
+def rotary_emb_fp32_bwd_op(grad: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    return _ak.rope_bwd(grad, cos, sin)
+
+
+@rotary_emb_fp32_bwd_op.register_fake
+def _(grad, cos, sin):
+    return grad.new_empty(grad.shape)
+
+
+@torch.library.custom_op("autokernel::rotary_emb_fp32", mutates_args=())
+def rotary_emb_fp32_op(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    return _ak.rope_fwd(x, cos, sin)
+
+
+@rotary_emb_fp32_op.register_fake
+def _(x, cos, sin):
+    return x.new_empty(x.shape)
+
+
+def _rope_setup(ctx, inputs, output):
+    ctx.save_for_backward(inputs[1], inputs[2])
+
+
+def _rope_backward(ctx, grad):
+    cos, sin = ctx.saved_tensors
+    return rotary_emb_fp32_bwd_op(grad, cos, sin), None, None
+
+
+rotary_emb_fp32_op.register_autograd(_rope_backward, setup_context=_rope_setup)
+try:
+    rotary_emb_fp32_op.register_autocast("cuda", torch.float32)
+except AttributeError:  # pragma: no cover - older torch
+    pass
 
 
 # ---------------------------------------------------------------------------

@@ -270,7 +270,7 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
 
 def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768):
     """Device-timed throughput of the other swapped ops at their BASELINE configs.
-    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "fused_res", "silu_gate", "conv1d"} (None = all)."""
+    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "fused_res", "silu_gate", "rope", "conv1d"} (None = all)."""
     from kernels import _ak
     res = {}
     st = torch.cuda.current_stream(dev)
@@ -411,6 +411,23 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         timeit(lambda: _ak.silu_gate_mul_bwd(gs_, us_, dys), 10 * E, "silu_gate_mul_bwd_bf16_65536x2048", steps,
                graph=True)
         del gs_, us_, dys
+        torch.cuda.empty_cache()
+
+    if want("rope"):
+        # RoPE bf16 q (64, 12, 2048, 64) read from a packed (64, 2048, 1536) QKV projection, written
+        # head-major (201 MB read + 201 MB written); bwd on a dense gradient of the same shape.
+        Bq, T, H, KH, hd = 64, 2048, 12, 4, 64
+        qkv = torch.randn(Bq, T, (H + 2 * KH) * hd, device=dev).to(torch.bfloat16)
+        qv = qkv[..., :H * hd].view(Bq, T, H, hd).transpose(1, 2)
+        inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
+        ang = torch.outer(torch.arange(T, device=dev, dtype=torch.float32), inv)
+        cq, sq = ang.cos(), ang.sin()
+        dyq = torch.randn(Bq, H, T, hd, device=dev).to(torch.bfloat16)
+        E = Bq * H * T * hd
+        timeit(lambda: _ak.rope_fwd(qv, cq, sq), 4 * E, "rope_fwd_bf16_q_64x12x2048x64_from_packed_qkv", steps,
+               graph=True)
+        timeit(lambda: _ak.rope_bwd(dyq, cq, sq), 4 * E, "rope_bwd_bf16_64x12x2048x64", steps, graph=True)
+        del qkv, qv, dyq
         torch.cuda.empty_cache()
 
     if want("conv1d"):
@@ -582,7 +599,7 @@ def main():
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
-    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,fused_res,silu_gate,conv1d")
+    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,fused_res,silu_gate,rope,conv1d")
     ap.add_argument("--ce-rows", type=int, default=32768, help="with --only-ops: rows of the linear+CE case")
     ap.add_argument("--batch", type=int, default=0, help="override the headline batch (small-case profiling)")
     args = ap.parse_args()

@@ -293,6 +293,30 @@ AK_API int ak_silu_gate_mul_bwd(void* dgate, void* dup, const void* gate,
                                 int64_t ld_dgate, int64_t ld_dup, int dt,
                                 void* stream);
 
+/* ---- Rotary position embedding (interleaved pairs) ------------------------
+ * y[b,h,n,2i]   = x[.,2i] cos[n,i] - x[.,2i+1] sin[n,i]
+ * y[b,h,n,2i+1] = x[.,2i] sin[n,i] + x[.,2i+1] cos[n,i]
+ * x: element (b, h, n, d) at x + b*stride_b + h*stride_h + n*stride_n + d
+ * (any strides with unit stride along D, e.g. q / k inside a fused QKV
+ * projection); y: dense (B, H, N, D); cos_t / sin_t: fp32 (N, D/2).  D even.
+ * Replaces rotary_embedding_hip / rotary_embedding_fp32_hip
+ * (kernels/hip/rotary_embedding.py:253-300) behind autokernel::rotary_emb_fp32
+ * (kernels/hip/_torch_ops.py:117-131). */
+AK_API int ak_rope_fwd(void* y, const void* x, const float* cos_t,
+                       const float* sin_t, int64_t B, int64_t H, int64_t N,
+                       int64_t D, int64_t stride_b, int64_t stride_h,
+                       int64_t stride_n, int dt, void* stream);
+
+/* Gradient of ak_rope_fwd: dx = rotation of dy by -theta on the same pairs
+ * (dy read through the given strides, dx dense).  Replaces
+ * rotary_embedding_backward_hip (kernels/hip/rotary_embedding_backward.py:126-170)
+ * and _rotary_backward (kernels/hip/_torch_ops.py:140-162), which assume the
+ * rotate-half pairing with full-width tables. */
+AK_API int ak_rope_bwd(void* dx, const void* dy, const float* cos_t,
+                       const float* sin_t, int64_t B, int64_t H, int64_t N,
+                       int64_t D, int64_t stride_b, int64_t stride_h,
+                       int64_t stride_n, int dt, void* stream);
+
 /* ---- Depthwise causal conv1d (+ optional SiLU) --------------------------
  * y[b,d,t] = act(bias[d] + sum_k w[d,k] x[b,d,t-K+1+k]), x = 0 before t = 0;
  * act = SiLU when silu != 0, identity otherwise.  x, y: (B, D, T) dt, T

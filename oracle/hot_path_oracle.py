@@ -282,3 +282,20 @@ def silu_gate_mul_bwd(gate, up, dy, dt=DEFAULT):
     g, u, gy = _c(gate, dt), _c(up, dt), _c(dy, dt)
     s = torch.sigmoid(g)
     return gy * u * s * (1 + g * (1 - s)), gy * g * s
+
+
+# ---------------------------------------------------------------------------
+# Rotary embedding, interleaved pairs — reference.rotary_embedding_ref
+# (reference.py:63-69) = kernels/hip/rotary_embedding.py:258-261,288-291;
+# backward = autograd of that forward (rotation by -theta).
+# ---------------------------------------------------------------------------
+def rope(x, cos, sin, dt=DEFAULT):
+    x, c, s = _c(x, dt), _c(cos, dt), _c(sin, dt)
+    x1, x2 = x[..., ::2], x[..., 1::2]
+    return torch.stack([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1).flatten(-2)
+
+
+def rope_bwd(dy, cos, sin, dt=DEFAULT):
+    g, c, s = _c(dy, dt), _c(cos, dt), _c(sin, dt)
+    g1, g2 = g[..., ::2], g[..., 1::2]
+    return torch.stack([g1 * c + g2 * s, -g1 * s + g2 * c], dim=-1).flatten(-2)

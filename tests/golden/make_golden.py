@@ -25,6 +25,10 @@ read-only is fine).  Every output stored here comes from the reference's code:
   silu_gate.npz    kernels/hip/silu_gate_mul.kernel_fn (fp32 branch, :102-110),
                    _torch_ops._silu_gate_mul_backward (:199-218),
                    kernels/hip/silu_gate_mul_backward.kernel_fn (:160-168), autograd
+  rope.npz         kernels/hip/rotary_embedding.kernel_fn_fp32 (fp32 branch, :280-291),
+                   reference.rotary_embedding_ref + autograd; whether
+                   _torch_ops._rotary_backward (:140-162) accepts the forward's (N, D/2)
+                   tables is recorded as `ref_bwd_raises`
   linear_ce.npz    F.linear + F.cross_entropy(ignore_index) fp32 + autograd, the
                    oracle of scripts/test_chunked_ce.py:13-39
 The fixtures are committed; the GPU box never needs the reference.
@@ -226,6 +230,27 @@ def main() -> None:
     np.savez_compressed(HERE / "silu_gate.npz", gate=_np(gs_), up=_np(us_), dy=_np(dys), y=_np(ysg),
                         dgate_op=_np(dg_op), dup_op=_np(du_op), dgate_kfn=_np(dg_k), dup_kfn=_np(du_k),
                         dgate_autograd=_np(ga.grad), dup_autograd=_np(ua.grad))
+
+    # ---------------- rotary embedding (interleaved pairs)
+    from kernels.hip import rotary_embedding as rre
+    g = torch.Generator().manual_seed(8)
+    Bq, Hq, Nq, Dq = 2, 3, 40, 64
+    xq = torch.randn(Bq, Hq, Nq, Dq, generator=g)
+    inv = 1.0 / (10000.0 ** (torch.arange(0, Dq, 2, dtype=torch.float32) / Dq))
+    ang = torch.outer(torch.arange(Nq, dtype=torch.float32), inv)
+    cq, sq = ang.cos(), ang.sin()
+    dyq = torch.randn(Bq, Hq, Nq, Dq, generator=g)
+    yq = rre.kernel_fn_fp32(_on_cuda(xq), cq, sq)
+    xr = xq.clone().requires_grad_(True)
+    reference.rotary_embedding_ref(xr, cq, sq).backward(dyq)
+    try:
+        rops._rotary_backward(_Ctx((cq, sq), x_dtype=torch.float32), dyq)
+        raises = False
+    except RuntimeError:
+        raises = True
+    np.savez_compressed(HERE / "rope.npz", x=_np(xq), cos=_np(cq), sin=_np(sq), dy=_np(dyq), y=_np(yq),
+                        y_ref=_np(reference.rotary_embedding_ref(xq, cq, sq)), dx_autograd=_np(xr.grad),
+                        ref_bwd_raises=np.bool_(raises))
 
     # ---------------- causal conv1d (reference op; T crosses the 256-step kernel chunk)
     g = torch.Generator().manual_seed(5)

@@ -148,3 +148,18 @@ def test_silu_gate_mul_golden():
         assert_fp32_close(dg, g[k], what=k)
     for k in ("dup_op", "dup_kfn", "dup_autograd"):
         assert_fp32_close(du, g[k], what=k)
+
+
+def test_rope_golden():
+    g = golden("rope")
+    x, c, s, dy = (torch.from_numpy(g[k]) for k in ("x", "cos", "sin", "dy"))
+    assert_fp32_close(O.rope(x, c, s), g["y"], what="y (kernel_fn_fp32)")
+    assert_fp32_close(O.rope(x, c, s), g["y_ref"], what="y (rotary_embedding_ref)")
+    assert_fp32_close(O.rope_bwd(dy, c, s), g["dx_autograd"], what="dx")
+
+
+def test_reference_rope_backward_rejects_its_own_tables():
+    """Pins a reference bug: _rotary_backward (kernels/hip/_torch_ops.py:140-162) uses the
+    rotate-half pairing with full-width tables, so with the forward's (N, D/2) tables it
+    raises instead of returning the gradient.  The oracle is the autograd of the forward."""
+    assert bool(golden("rope")["ref_bwd_raises"])

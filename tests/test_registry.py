@@ -28,7 +28,8 @@ class Block(nn.Module):
 
 
 def test_list_patterns():
-    assert autokernel.list_patterns() == ["fused_residual_rmsnorm", "rmsnorm", "fused_silu_gate_mul", "silu_gate_mul"]
+    assert autokernel.list_patterns() == ["fused_residual_rmsnorm", "fused_qkv", "rmsnorm", "fused_silu_gate_mul",
+                                          "silu_gate_mul"]
 
 
 def test_optimize_replaces_rmsnorms_and_keeps_parameters(monkeypatch):
