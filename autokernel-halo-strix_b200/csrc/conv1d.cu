@@ -244,6 +244,7 @@ __global__ void conv1d_dw_reduce(float* __restrict__ dw, float* __restrict__ dbi
 #pragma unroll
   for (int k = 0; k <= K; ++k) s[k] = 0.f;
   const int n = B * nch;
+#pragma unroll 4  // independent loads in flight; the adds stay in index order
   for (int j = lane; j < n; j += 32) {
     const int b = j / nch, c = j - b * nch;
     const float* p = part + (((int64_t)b * D + d) * nch + c) * (K + 1);

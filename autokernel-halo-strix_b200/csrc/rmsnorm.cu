@@ -270,6 +270,7 @@ rmsnorm_dw_reduce(TD* __restrict__ dw, const float* __restrict__ part, int G, in
   const int c = blockIdx.x * 32 + threadIdx.x;
   float acc = 0.f;
   if (c < N)
+#pragma unroll 8  // independent loads in flight; the adds stay in index order
     for (int g = threadIdx.y; g < G; g += 32) acc += part[(int64_t)g * N + c];
   s[threadIdx.y][threadIdx.x] = acc;
   __syncthreads();

@@ -21,6 +21,9 @@ namespace {
 
 constexpr int kW = 8;  // warps per CTA
 
+// All loads of a segment are unconditional (indices clamped into range, values
+// masked afterwards), so a warp issues its 4*SEG loads back to back instead of
+// one dependent round trip per guarded step; only the stores are guarded.
 template <int SEG>
 __global__ void __launch_bounds__(kW * 32)
 scan1_fwd_kernel(float* __restrict__ y, const float* __restrict__ dA, const float* __restrict__ dBx,
@@ -32,20 +35,24 @@ scan1_fwd_kernel(float* __restrict__ y, const float* __restrict__ dA, const floa
   const int64_t b = blockIdx.y;
   const bool cv = c < d;
   const float Dc = (cv && Dv) ? Dv[c] : 0.f;
-  const int64_t base = b * (int64_t)L * d + c;
+  const int64_t base = b * (int64_t)L * d + (cv ? c : d - 1);
   constexpr int CH = kW * SEG;
   float carry = 0.f;
   int par = 0;
   for (int t0 = 0; t0 < L; t0 += CH, par ^= 1) {
     const int tw = t0 + warp * SEG;
-    float a[SEG], bb[SEG];
+    float a[SEG], bb[SEG], cc[SEG], xx[SEG];
 #pragma unroll
     for (int i = 0; i < SEG; ++i) {
-      const int t = tw + i;
-      const bool ok = cv && t < L;
-      a[i] = ok ? __ldcs(dA + base + (int64_t)t * d) : 1.f;
-      bb[i] = ok ? __ldcs(dBx + base + (int64_t)t * d) : 0.f;
+      const int64_t off = base + (int64_t)min(tw + i, L - 1) * d;
+      a[i] = __ldcs(dA + off);
+      bb[i] = __ldcs(dBx + off);
+      cc[i] = __ldcs(Cm + off);
+      xx[i] = __ldcs(x + off);
     }
+#pragma unroll
+    for (int i = 0; i < SEG; ++i)
+      if (!(cv && tw + i < L)) { a[i] = 1.f; bb[i] = 0.f; }
     float P = 1.f, H = 0.f;
 #pragma unroll
     for (int i = 0; i < SEG; ++i) { H = fmaf(a[i], H, bb[i]); P *= a[i]; }
@@ -64,10 +71,8 @@ scan1_fwd_kernel(float* __restrict__ y, const float* __restrict__ dA, const floa
     for (int i = 0; i < SEG; ++i) {
       const int t = tw + i;
       h = fmaf(a[i], h, bb[i]);
-      if (cv && t < L) {
-        const int64_t off = base + (int64_t)t * d;
-        __stcs(y + off, fmaf(__ldcs(Cm + off), h, Dc * __ldcs(x + off)));
-      }
+      const float yv = fmaf(cc[i], h, Dc * xx[i]);
+      if (cv && t < L) __stcs(y + base + (int64_t)t * d, yv);
     }
   }
 }
@@ -82,23 +87,24 @@ scan1_carry_kernel(float* __restrict__ carries, const float* __restrict__ dA, co
   const int c = blockIdx.x * 32 + lane;
   const int64_t b = blockIdx.y;
   const bool cv = c < d;
-  const int64_t base = b * (int64_t)L * d + c;
+  const int64_t cbase = b * (int64_t)L * d + (cv ? c : d - 1);
   constexpr int CH = kW * SEG;
   float carry = 0.f;
   int par = 0, ci = 0;
   for (int t0 = 0; t0 < L; t0 += CH, par ^= 1, ++ci) {
     if (warp == 0 && cv) carries[(b * nchunk + ci) * d + c] = carry;
     const int tw = t0 + warp * SEG;
+    float av[SEG], bv[SEG];
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) {  // unconditional (clamped) loads, masked values
+      const int64_t off = cbase + (int64_t)min(tw + i, L - 1) * d;
+      av[i] = dA[off];
+      bv[i] = dBx[off];
+    }
     float P = 1.f, H = 0.f;
 #pragma unroll
-    for (int i = 0; i < SEG; ++i) {
-      const int t = tw + i;
-      if (cv && t < L) {
-        const float a = dA[base + (int64_t)t * d];
-        H = fmaf(a, H, dBx[base + (int64_t)t * d]);
-        P *= a;
-      }
-    }
+    for (int i = 0; i < SEG; ++i)
+      if (cv && tw + i < L) { H = fmaf(av[i], H, bv[i]); P *= av[i]; }
     sP[par][warp][lane] = P;
     sH[par][warp][lane] = H;
     __syncthreads();
@@ -123,27 +129,34 @@ scan1_bwd_kernel(float* __restrict__ gdA, float* __restrict__ gdBx, float* __res
   const bool cv = c < d;
   const float Dc = (cv && Dv) ? Dv[c] : 0.f;
   const int64_t base = b * (int64_t)L * d + c;
+  const int64_t cbase = b * (int64_t)L * d + (cv ? c : d - 1);  // clamped, for unconditional loads
   constexpr int CH = kW * SEG;
   float gcarry = 0.f, gdacc = 0.f;
   int par = 0;
   for (int ci = nchunk - 1; ci >= 0; --ci, par ^= 1) {
     const int t0 = ci * CH;
     const int tw = t0 + warp * SEG;
-    float a[SEG + 1], bb[SEG], rb[SEG], gyv[SEG];
+    float a[SEG + 1], bb[SEG], rb[SEG], gyv[SEG], xv[SEG];
+    // unconditional (clamped) loads first, then the masks: all 5*SEG+1 loads in flight
 #pragma unroll
-    for (int i = 0; i <= SEG; ++i) {
-      const int t = tw + i;
-      a[i] = (cv && t < L) ? dA[base + (int64_t)t * d] : (i < SEG ? 1.f : 0.f);
-    }
+    for (int i = 0; i <= SEG; ++i) a[i] = dA[cbase + (int64_t)min(tw + i, L - 1) * d];
 #pragma unroll
     for (int i = 0; i < SEG; ++i) {
-      const int t = tw + i;
-      const bool ok = cv && t < L;
-      const int64_t off = base + (int64_t)t * d;
-      bb[i] = ok ? dBx[off] : 0.f;
-      gyv[i] = ok ? gy[off] : 0.f;
-      rb[i] = ok ? gyv[i] * Cm[off] : 0.f;
-      if (ok) gdacc = fmaf(gyv[i], x[off], gdacc);
+      const int64_t off = cbase + (int64_t)min(tw + i, L - 1) * d;
+      bb[i] = dBx[off];
+      gyv[i] = gy[off];
+      rb[i] = Cm[off];
+      xv[i] = x[off];
+    }
+#pragma unroll
+    for (int i = 0; i <= SEG; ++i)
+      if (!(cv && tw + i < L)) a[i] = (i < SEG ? 1.f : 0.f);
+#pragma unroll
+    for (int i = 0; i < SEG; ++i) {
+      const bool ok = cv && tw + i < L;
+      if (!ok) { bb[i] = 0.f; gyv[i] = 0.f; xv[i] = 0.f; }
+      rb[i] = gyv[i] * rb[i];
+      gdacc = fmaf(gyv[i], xv[i], gdacc);
     }
     // forward aggregates (prod a, local h) and reverse aggregates (prod a', local g)
     float P = 1.f, H = 0.f;
@@ -197,11 +210,12 @@ __global__ void scan1_gd_reduce(float* __restrict__ gD, const float* __restrict_
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= d) return;
   float s = 0.f;
+#pragma unroll 8  // independent loads in flight; the adds stay in index order
   for (int b = 0; b < B; ++b) s += part[(int64_t)b * d + c];
   gD[c] = s;
 }
 
-constexpr int kSegF = 16, kSegB = 8;
+constexpr int kSegF = 8, kSegB = 8;
 inline int nchunk_bwd(int64_t L) { return (int)((L + kW * kSegB - 1) / (kW * kSegB)); }
 
 }  // namespace

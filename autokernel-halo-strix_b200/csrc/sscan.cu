@@ -581,6 +581,7 @@ __global__ void sscan_bwd_reduce(float* __restrict__ dA, float* __restrict__ dD,
   if (i >= (int64_t)dim * per) return;
   const int d = (int)(i / per), k = (int)(i - d * per);
   float s = 0.f;
+#pragma unroll 8  // independent loads in flight; the adds stay in index order
   for (int b = 0; b < batch; ++b) s += part[((int64_t)b * dim + d) * per + k];
   if (k < N) dA[(int64_t)d * N + k] = s;
   else if (k == N) { if (dD) dD[d] = s; }

@@ -268,7 +268,7 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
                       f"of the same sample"}
 
 
-def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768):
+def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768, scale=1):
     """Device-timed throughput of the other swapped ops at their BASELINE configs.
     `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "fused_res", "silu_gate", "rope", "conv1d"} (None = all)."""
     from kernels import _ak
@@ -326,7 +326,7 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
 
     if want("softmax"):
         # Softmax causal scores bf16 [96*2048, 2048] (config 3): 805 MB per tensor > L2.
-        rows, cols = 96 * 2048, 2048
+        rows, cols = 96 * 2048 // scale, 2048
         s = (torch.randn(rows, cols, device=dev) / 8).to(torch.bfloat16)
         r = torch.arange(rows, device=dev) % cols
         s.masked_fill_(torch.arange(cols, device=dev)[None, :] > r[:, None], float("-inf"))
@@ -389,7 +389,7 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         # Fused residual add + RMSNorm bf16 [65536, 768] (the hybrid's d_model; 100 MB per tensor):
         # fwd reads x, residual and writes hidden, normed; bwd reads hidden, grad_hidden,
         # grad_normed and writes dx.
-        Mr, Nr = 65536, 768
+        Mr, Nr = 65536 // scale, 768
         xr_, rr_, ghr, gnr = (torch.randn(Mr, Nr, device=dev).to(torch.bfloat16) for _ in range(4))
         wr_ = torch.randn(Nr, device=dev).to(torch.bfloat16)
         hr_, _ = _ak.fused_res_rmsnorm_fwd(xr_, rr_, wr_)
@@ -404,7 +404,7 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
     if want("silu_gate"):
         # SiLU gate multiply bf16 [65536, 2048] (the hybrid's SwiGLU hidden width; 268 MB per tensor):
         # fwd reads gate, up, writes y; bwd reads gate, up, dy, writes d gate, d up.
-        Ms, Hs = 65536, 2048
+        Ms, Hs = 65536 // scale, 2048
         gs_, us_, dys = (torch.randn(Ms, Hs, device=dev).to(torch.bfloat16) for _ in range(3))
         E = Ms * Hs
         timeit(lambda: _ak.silu_gate_mul_fwd(gs_, us_), 6 * E, "silu_gate_mul_fwd_bf16_65536x2048", steps, graph=True)
@@ -416,7 +416,7 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
     if want("rope"):
         # RoPE bf16 q (64, 12, 2048, 64) read from a packed (64, 2048, 1536) QKV projection, written
         # head-major (201 MB read + 201 MB written); bwd on a dense gradient of the same shape.
-        Bq, T, H, KH, hd = 64, 2048, 12, 4, 64
+        Bq, T, H, KH, hd = 64 // scale, 2048, 12, 4, 64
         qkv = torch.randn(Bq, T, (H + 2 * KH) * hd, device=dev).to(torch.bfloat16)
         qv = qkv[..., :H * hd].view(Bq, T, H, hd).transpose(1, 2)
         inv = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device=dev, dtype=torch.float32) / hd))
@@ -433,7 +433,7 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
     if want("conv1d"):
         # Depthwise causal conv1d + SiLU bf16 (16, 1536, 2048), K=4 (the Mamba block's
         # conv at the hybrid model's d_inner): 100 MB per tensor, x + y > L2.
-        Bsz, Dc, T = 16, 1536, 2048
+        Bsz, Dc, T = max(1, 16 // scale), 1536, 2048
         xc = torch.randn(Bsz, Dc, T, device=dev).to(torch.bfloat16)
         dyc = torch.randn(Bsz, Dc, T, device=dev).to(torch.bfloat16)
         wc, bc = torch.randn(Dc, 4, device=dev), torch.randn(Dc, device=dev)
@@ -444,6 +444,8 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
                steps, graph=True)
         del xc, dyc
         torch.cuda.empty_cache()
+    if scale != 1:
+        res["_ops_scale"] = scale
     return res
 
 
@@ -485,7 +487,7 @@ def run_ours(args, world, rank, local):
         if rank == 0:
             emit({"ops": time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak,
                                         which=set(args.ops.split(",")) if args.ops else None,
-                                        ce_rows=args.ce_rows)})
+                                        ce_rows=args.ce_rows, scale=args.ops_scale)})
         return
     cfg = dict(HEADLINE)
     if args.batch:
@@ -601,6 +603,9 @@ def main():
     ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
     ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,fused_res,silu_gate,rope,conv1d")
     ap.add_argument("--ce-rows", type=int, default=32768, help="with --only-ops: rows of the linear+CE case")
+    ap.add_argument("--ops-scale", type=int, default=1,
+                    help="with --only-ops: divide the leading dimension of the softmax, fused_res, silu_gate, rope "
+                         "and conv1d cases by this (small cases for ncu captures; names keep the full-size label)")
     ap.add_argument("--batch", type=int, default=0, help="override the headline batch (small-case profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
