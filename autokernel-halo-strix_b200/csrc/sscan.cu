@@ -218,13 +218,13 @@ __host__ __device__ inline size_t stage_bytes(int N) { return (size_t)2 * N * CH
 // independent dependency chains.
 template <int ITEMS, int K>
 __device__ __forceinline__ void fwd_states(int n0, int N, const float (&dlt)[ITEMS], const float (&du)[ITEMS],
-                                           float (&y)[ITEMS], float S, const float* Arow, const float* tile, int lane,
+                                           float (&y)[ITEMS], float S, float A_l, const float* tile, int lane,
                                            float* carry_row, float* save) {
   constexpr int CH = 32 * ITEMS;
   float a[K][ITEMS], h[K][ITEMS], P[K], H[K];
 #pragma unroll
   for (int k = 0; k < K; ++k) {
-    const float A2 = Arow[n0 + k] * kLog2e;
+    const float A2 = __shfl_sync(0xffffffffu, A_l, n0 + k) * kLog2e;  // lane n holds A[d, n]
     float Bv[ITEMS];
     load_tile<ITEMS>(Bv, tile + (n0 + k) * CH, lane);
 #pragma unroll
@@ -330,13 +330,13 @@ sscan_fwd_kernel(SsParams p) {
         y[i] = Dd * du[i];
         du[i] *= v;
       }
-      const float* Arow = p.A + (int64_t)d * N;
+      const float A_l = lane < N ? p.A[(int64_t)d * N + lane] : 0.f;  // lane n holds A[d, n]
       float* carry_row = scarry + cl * N;
       // lane 31 ends the chunk = one state stride: it saves the states for the backward
       float* save = (p.chunk_states != nullptr && lane == 31) ? p.chunk_states + (chan * p.nsaved + k) * N : nullptr;
       int n = 0;
-      for (; n + 2 <= N; n += 2) fwd_states<ITEMS, 2>(n, N, dlt, du, y, S, Arow, tile, lane, carry_row, save);
-      if (n < N) fwd_states<ITEMS, 1>(n, N, dlt, du, y, S, Arow, tile, lane, carry_row, save);
+      for (; n + 2 <= N; n += 2) fwd_states<ITEMS, 2>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
+      if (n < N) fwd_states<ITEMS, 1>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
       if (p.z != nullptr) {
         float zz[ITEMS];
         load_items<T, ITEMS>(zz, reinterpret_cast<const T*>(p.z) + chan * L, tl, L, p.vec_io);
@@ -437,12 +437,14 @@ sscan_bwd_kernel(SsParams p) {
 #pragma unroll
       for (int i = 0; i < ITEMS; ++i) { yacc[i] = Dd * uu[i]; ddl[i] = 0.f; duacc[i] = dy[i] * Dd; }
       const float Sr = S - dlt[0];  // sum of delta' over the lane's steps 1..ITEMS-1
-      const float* Arow = p.A + (int64_t)d * N;
-      const float* hc_row = (k > 0) ? p.chunk_states_in + (chan * p.nsaved + (k - 1)) * N : nullptr;
+      // lane n holds A[d, n] and the saved chunk-start state n: one load each per
+      // channel and chunk, broadcast by shuffle inside the state loop
+      const float A_l = lane < N ? p.A[(int64_t)d * N + lane] : 0.f;
+      const float hc_l = (k > 0 && lane < N) ? p.chunk_states_in[(chan * p.nsaved + (k - 1)) * N + lane] : 0.f;
       float dAl_keep = 0.f;  // lane n < N keeps state n's dA partial
 
       for (int n = 0; n < N; ++n) {
-        const float An = Arow[n];
+        const float An = __shfl_sync(0xffffffffu, A_l, n);
         const float A2 = An * kLog2e;
         float a[ITEMS], h[ITEMS], Bv[ITEMS], Cv[ITEMS];
         load_tile<ITEMS>(Bv, tile + n * CH, lane);
@@ -463,7 +465,7 @@ sscan_bwd_kernel(SsParams p) {
           const float Hp = __shfl_up_sync(0xffffffffu, H, off);
           if (lane >= off) { H = fmaf(P, Hp, H); P *= Pp; }
         }
-        const float hc = hc_row ? hc_row[n] : 0.f;
+        const float hc = __shfl_sync(0xffffffffu, hc_l, n);
         float Pe = __shfl_up_sync(0xffffffffu, P, 1);
         float He = __shfl_up_sync(0xffffffffu, H, 1);
         if (lane == 0) { Pe = 1.f; He = 0.f; }
