@@ -27,7 +27,9 @@ constexpr int kWarps = 8;  // rows in flight per CTA
 // ----------------------------------------------------------------------------
 // RES: fused residual add (hidden = x + res, rounded to T, stored to h_out when
 // non-null, then normalised).
-template <typename T, typename TW, int VEC, int NIT, bool RES = false>
+// FULL: N == NIT * 32 * VEC, so no lane's vector is out of range and the loads
+// carry no guard (issued back to back).
+template <typename T, typename TW, int VEC, int NIT, bool RES = false, bool FULL = false>
 __global__ void __launch_bounds__(kWarps * 32)
 rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __restrict__ x,
                  const TW* __restrict__ w, int64_t M, int N, float eps, const T* __restrict__ res = nullptr,
@@ -38,7 +40,7 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
 #pragma unroll
   for (int it = 0; it < NIT; ++it) {
     const int c = (it * 32 + lane) * VEC;
-    if (c < N) load_frag<TW, VEC>(wr[it], w + c);
+    if (FULL || c < N) load_frag<TW, VEC>(wr[it], w + c);
     else {
 #pragma unroll
       for (int k = 0; k < VEC; ++k) wr[it][k] = 0.f;
@@ -52,7 +54,7 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
-      if (c < N) {
+      if (FULL || c < N) {
         load_frag<T, VEC>(xv[it], xr + c);
         if constexpr (RES) {
           float rv[VEC];
@@ -75,7 +77,7 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
-      if (c < N) {
+      if (FULL || c < N) {
         float o[VEC];
 #pragma unroll
         for (int k = 0; k < VEC; ++k) o[k] = xv[it][k] * r * wr[it][k];
@@ -139,7 +141,7 @@ __device__ __forceinline__ int bwd_slot(int c) {
   return (it * VEC + k) * 32 + lane;
 }
 
-template <typename T, typename TW, int VEC, int NIT, bool RES = false>
+template <typename T, typename TW, int VEC, int NIT, bool RES = false, bool FULL = false>
 __global__ void __launch_bounds__(kWarps * 32, (NIT * VEC <= 24) ? 3 : 2)
 rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __restrict__ dy,
                  const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps,
@@ -165,7 +167,7 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
-      if (c < N) {
+      if (FULL || c < N) {
         load_frag<T, VEC>(xv[it], x + row * N + c);
         load_frag<T, VEC>(gv[it], dy + row * N + c);
       } else {
@@ -189,7 +191,7 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
-      if (c < N) {
+      if (FULL || c < N) {
         float o[VEC];
 #pragma unroll
         for (int k = 0; k < VEC; ++k) {
@@ -355,9 +357,15 @@ int fwd_impl(void* y, float* rstd, const void* x, const void* w, int64_t M, int 
     int64_t g = (M + kWarps - 1) / kWarps;
     const int64_t cap = (int64_t)sm_count() * 16;
     if (g > cap) g = cap;
-    AK_NIT_SWITCH(p.nit, NIT,
-                  rmsnorm_fwd_warp<T, TW, VEC, NIT, RES><<<(unsigned)g, kWarps * 32, 0, st>>>(
-                      (T*)y, rstd, (const T*)x, (const TW*)w, M, N, eps, (const T*)res, (T*)h_out));
+    if (N == p.nit * 32 * VEC) {
+      AK_NIT_SWITCH(p.nit, NIT,
+                    rmsnorm_fwd_warp<T, TW, VEC, NIT, RES, true><<<(unsigned)g, kWarps * 32, 0, st>>>(
+                        (T*)y, rstd, (const T*)x, (const TW*)w, M, N, eps, (const T*)res, (T*)h_out));
+    } else {
+      AK_NIT_SWITCH(p.nit, NIT,
+                    rmsnorm_fwd_warp<T, TW, VEC, NIT, RES><<<(unsigned)g, kWarps * 32, 0, st>>>(
+                        (T*)y, rstd, (const T*)x, (const TW*)w, M, N, eps, (const T*)res, (T*)h_out));
+    }
   } else {
     int64_t g = M;
     const int64_t cap = (int64_t)sm_count() * 8;
@@ -383,8 +391,9 @@ int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const voi
   int G = bwd_grid(M, N);
   if (M > 0) {
     if (p.warp_path) {
+      const bool full = N == p.nit * 32 * VEC;
       AK_NIT_SWITCH(p.nit, NIT, if constexpr (NIT * VEC <= 32) {
-        auto kern = rmsnorm_bwd_warp<T, TW, VEC, NIT, RES>;
+        auto kern = full ? rmsnorm_bwd_warp<T, TW, VEC, NIT, RES, true> : rmsnorm_bwd_warp<T, TW, VEC, NIT, RES>;
         const size_t smem = (size_t)(kWarps + 1) * NIT * VEC * 32 * sizeof(float);
         if (smem > 48 * 1024)
           AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),

@@ -18,7 +18,7 @@ namespace {
 
 constexpr int kWarps = 4;
 
-template <typename T, int VEC, int NIT>
+template <typename T, int VEC, int NIT, bool FULL = false>
 __global__ void __launch_bounds__(kWarps * 32)
 softmax_fwd_warp(T* __restrict__ y, const T* __restrict__ x, int64_t rows, int cols) {
   const int lane = threadIdx.x & 31;
@@ -30,7 +30,7 @@ softmax_fwd_warp(T* __restrict__ y, const T* __restrict__ x, int64_t rows, int c
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
-      if (c < cols) {
+      if (FULL || c < cols) {
         load_frag_stream<T, VEC>(v[it], xr + c);
       } else {
 #pragma unroll
@@ -54,7 +54,7 @@ softmax_fwd_warp(T* __restrict__ y, const T* __restrict__ x, int64_t rows, int c
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
-      if (c < cols) {
+      if (FULL || c < cols) {
         float o[VEC];
 #pragma unroll
         for (int k = 0; k < VEC; ++k) o[k] = v[it][k] * inv;
@@ -68,7 +68,9 @@ softmax_fwd_warp(T* __restrict__ y, const T* __restrict__ x, int64_t rows, int c
 // y and dy (L1/L2 hits, the row was just read) and writes dx.  Keeping no row
 // in registers leaves room for many resident warps, which is what a pure
 // streaming kernel needs to cover HBM latency.
-template <typename T, int VEC, int NIT>
+// FULL: cols == NIT * 32 * VEC, every lane's vectors are in range and the
+// loads carry no guard (issued back to back).
+template <typename T, int VEC, int NIT, bool FULL = false>
 __global__ void __launch_bounds__(kWarps * 32)
 softmax_bwd_warp(T* __restrict__ dx, const T* __restrict__ y, const T* __restrict__ dy,
                  int64_t rows, int cols) {
@@ -81,7 +83,7 @@ softmax_bwd_warp(T* __restrict__ dx, const T* __restrict__ y, const T* __restric
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
-      if (c < cols) {
+      if (FULL || c < cols) {
         float yv[VEC], gv[VEC];
         load_frag<T, VEC>(yv, yr + c);
         load_frag<T, VEC>(gv, gr + c);
@@ -93,7 +95,7 @@ softmax_bwd_warp(T* __restrict__ dx, const T* __restrict__ y, const T* __restric
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
-      if (c < cols) {
+      if (FULL || c < cols) {
         float yv[VEC], gv[VEC], o[VEC];
         load_frag<T, VEC>(yv, yr + c);
         load_frag<T, VEC>(gv, gr + c);
@@ -181,8 +183,13 @@ int fwd_impl(void* y, const void* x, int64_t rows, int cols, cudaStream_t st) {
   constexpr int VEC = 16 / sizeof(T);
   const int nit = (cols % VEC == 0 && aligned16(x) && aligned16(y)) ? pick_nit(cols, VEC) : 0;
   if (nit > 0) {
-    AK_SMX_NIT_SWITCH(nit, NIT, softmax_fwd_warp<T, VEC, NIT><<<warp_grid(rows), kWarps * 32, 0, st>>>(
-                                    (T*)y, (const T*)x, rows, cols));
+    if (cols == nit * 32 * VEC) {
+      AK_SMX_NIT_SWITCH(nit, NIT, softmax_fwd_warp<T, VEC, NIT, true><<<warp_grid(rows), kWarps * 32, 0, st>>>(
+                                      (T*)y, (const T*)x, rows, cols));
+    } else {
+      AK_SMX_NIT_SWITCH(nit, NIT, softmax_fwd_warp<T, VEC, NIT><<<warp_grid(rows), kWarps * 32, 0, st>>>(
+                                      (T*)y, (const T*)x, rows, cols));
+    }
   } else {
     const int64_t cap = (int64_t)sm_count() * 4;
     softmax_fwd_block<T><<<(unsigned)(rows < cap ? rows : cap), 512, 0, st>>>((T*)y, (const T*)x, rows, cols);
@@ -196,8 +203,13 @@ int bwd_impl(void* dx, const void* y, const void* dy, int64_t rows, int cols, cu
   constexpr int VEC = 16 / sizeof(T);
   int nit = (cols % VEC == 0 && aligned16(dx) && aligned16(y) && aligned16(dy)) ? pick_nit(cols, VEC) : 0;
   if (nit > 0) {
-    AK_SMX_NIT_SWITCH(nit, NIT, softmax_bwd_warp<T, VEC, NIT><<<warp_grid(rows), kWarps * 32, 0, st>>>(
-                                    (T*)dx, (const T*)y, (const T*)dy, rows, cols));
+    if (cols == nit * 32 * VEC) {
+      AK_SMX_NIT_SWITCH(nit, NIT, softmax_bwd_warp<T, VEC, NIT, true><<<warp_grid(rows), kWarps * 32, 0, st>>>(
+                                      (T*)dx, (const T*)y, (const T*)dy, rows, cols));
+    } else {
+      AK_SMX_NIT_SWITCH(nit, NIT, softmax_bwd_warp<T, VEC, NIT><<<warp_grid(rows), kWarps * 32, 0, st>>>(
+                                      (T*)dx, (const T*)y, (const T*)dy, rows, cols));
+    }
   } else {
     const int64_t cap = (int64_t)sm_count() * 4;
     softmax_bwd_block<T><<<(unsigned)(rows < cap ? rows : cap), 512, 0, st>>>((T*)dx, (const T*)y,
