@@ -270,7 +270,7 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
 
 def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768, scale=1):
     """Device-timed throughput of the other swapped ops at their BASELINE configs.
-    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "fused_res", "silu_gate", "rope", "conv1d"} (None = all)."""
+    `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "ce_rows", "fused_res", "silu_gate", "rope", "conv1d"} (None = all)."""
     from kernels import _ak
     res = {}
     st = torch.cuda.current_stream(dev)
@@ -383,6 +383,19 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         timeit(lambda: _ak.scan1_fwd(dA, dBx, C, Dv, xx), 20 * E, "scan1_fwd_fp32_8x2048x1536", steps)
         timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy), 36 * E, "scan1_bwd_fp32_8x2048x1536", steps)
         del dA, dBx, C, xx, gy
+        torch.cuda.empty_cache()
+
+    if want("ce_rows"):
+        # CE rows with fused gradient, bf16 logits [4096, 50304] (one chunk of the chunked linear+CE
+        # path; 412 MB): reads each row once for the statistics, once more (L2) for the gradient,
+        # writes the gradient.  Algorithmic bytes: logits read + gradient written.
+        Nc, Vc = 4096 // scale if scale > 1 else 4096, 50304
+        lg = (torch.randn(Nc, Vc, device=dev) * 2).to(torch.bfloat16)
+        tg = torch.randint(0, Vc, (Nc,), device=dev)
+        E = Nc * Vc
+        timeit(lambda: _ak.ce_rows_fwd(lg, tg, write_grad=True), 4 * E, "ce_rows_fwd_grad_bf16_4096x50304", steps,
+               graph=True)
+        del lg, tg
         torch.cuda.empty_cache()
 
     if want("fused_res"):
@@ -601,7 +614,7 @@ def main():
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
-    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,fused_res,silu_gate,rope,conv1d")
+    ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,ce_rows,fused_res,silu_gate,rope,conv1d")
     ap.add_argument("--ce-rows", type=int, default=32768, help="with --only-ops: rows of the linear+CE case")
     ap.add_argument("--ops-scale", type=int, default=1,
                     help="with --only-ops: divide the leading dimension of the softmax, fused_res, silu_gate, rope "
