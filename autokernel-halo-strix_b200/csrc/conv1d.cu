@@ -38,9 +38,11 @@ __device__ __forceinline__ float dsilu_f(float p) {
   return s * (1.f + p * (1.f - s));
 }
 
-template <typename T, int kIt>
+// FULL: every run is in range and 16-byte aligned (T a multiple of the chunk):
+// no branch around the vector loads / stores.
+template <typename T, int kIt, bool FULL = false>
 __device__ __forceinline__ void load_run(float (&v)[kIt], const T* row, int t, int T_, bool vec) {
-  if (vec && t + kIt <= T_) {
+  if (FULL || (vec && t + kIt <= T_)) {
     constexpr int VEC = 16 / sizeof(T);
 #pragma unroll
     for (int i = 0; i < kIt; i += VEC) {
@@ -55,9 +57,9 @@ __device__ __forceinline__ void load_run(float (&v)[kIt], const T* row, int t, i
   }
 }
 
-template <typename T, int kIt>
+template <typename T, int kIt, bool FULL = false>
 __device__ __forceinline__ void store_run(T* row, const float (&v)[kIt], int t, int T_, bool vec) {
-  if (vec && t + kIt <= T_) {
+  if (FULL || (vec && t + kIt <= T_)) {
     constexpr int VEC = 16 / sizeof(T);
 #pragma unroll
     for (int i = 0; i < kIt; i += VEC) {
@@ -107,7 +109,7 @@ __device__ __forceinline__ void left_halo(float (&halo)[kMaxK], const float (&xv
   }
 }
 
-template <typename T, int K>
+template <typename T, int K, bool FULL>
 __global__ void __launch_bounds__(kWarpsC * 32)
 conv1d_fwd_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict__ wt,
                   const float* __restrict__ bias, int64_t rows, int nch, int D, int T_, int silu, bool vec) {
@@ -122,7 +124,7 @@ conv1d_fwd_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __res
   const int t0 = c0 + lane * kIt;
   // issue every global load first: the run, and lane 0's halo
   float xv[kIt], edge[kMaxK];
-  load_run<T, kIt>(xv, xr, t0, T_, vec);
+  load_run<T, kIt, FULL>(xv, xr, t0, T_, vec);
 #pragma unroll
   for (int j = 0; j < K - 1; ++j) edge[j] = lane == 0 ? ld_or0<T>(xr, t0 - (K - 1) + j, T_) : 0.f;
   float w[kMaxK];
@@ -136,11 +138,11 @@ conv1d_fwd_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __res
 #pragma unroll
     for (int i = 0; i < kIt; ++i) pre[i] = silu_f(pre[i]);
   }
-  store_run<T, kIt>(y + r * T_, pre, t0, T_, vec);
+  store_run<T, kIt, FULL>(y + r * T_, pre, t0, T_, vec);
 }
 
 // Backward; part[row][chunk][K+1] = per-warp (dw[0..K-1], dbias) partials.
-template <typename T, int K>
+template <typename T, int K, bool FULL>
 __global__ void __launch_bounds__(kWarpsC * 32, 4)
 conv1d_bwd_kernel(T* __restrict__ dx, float* __restrict__ part, const T* __restrict__ x, const T* __restrict__ dy,
                   const float* __restrict__ wt, const float* __restrict__ bias, int64_t rows, int D, int T_, int silu,
@@ -159,8 +161,8 @@ conv1d_bwd_kernel(T* __restrict__ dx, float* __restrict__ part, const T* __restr
   // all global loads up front: runs of x and dy, lane 0's left halo of x, and
   // lane 31's right edge (x and dy at te .. te+K-2) for the next chunk's dpre
   float xv[kIt], g[kIt], edge[kMaxK], xr_e[kMaxK], gr_e[kMaxK];
-  load_run<T, kIt>(xv, xr, t0, T_, vec);
-  load_run<T, kIt>(g, gr, t0, T_, vec);
+  load_run<T, kIt, FULL>(xv, xr, t0, T_, vec);
+  load_run<T, kIt, FULL>(g, gr, t0, T_, vec);
 #pragma unroll
   for (int j = 0; j < K - 1; ++j) {
     edge[j] = lane == 0 ? ld_or0<T>(xr, t0 - (K - 1) + j, T_) : 0.f;
@@ -220,7 +222,7 @@ conv1d_bwd_kernel(T* __restrict__ dx, float* __restrict__ part, const T* __restr
     }
     o[i] = acc;
   }
-  store_run<T, kIt>(dx + r * T_, o, t0, T_, vec);
+  store_run<T, kIt, FULL>(dx + r * T_, o, t0, T_, vec);
 #pragma unroll
   for (int k = 0; k < K; ++k) dwacc[k] = warp_sum(dwacc[k]);
   dbacc = warp_sum(dbacc);
@@ -289,9 +291,14 @@ extern "C" int ak_causal_conv1d_fwd(void* y, const void* x, const float* weight,
   const int nch = (int)((T + chunk - 1) / chunk);
   const bool vec = aligned16(x) && aligned16(y) && ((T * elem_size(dt)) % 16 == 0);
   const unsigned grid = (unsigned)((rows * nch + kWarpsC - 1) / kWarpsC);
+  const bool full = vec && T % chunk == 0;
   AK_DISPATCH_DTYPE(dt, TT, {
-    AK_K_SWITCH(K, KC, conv1d_fwd_kernel<TT, KC><<<grid, kWarpsC * 32, 0, (cudaStream_t)stream>>>(
-                           (TT*)y, (const TT*)x, weight, bias, rows, nch, (int)D, (int)T, silu, vec));
+    if (full)
+      AK_K_SWITCH(K, KC, conv1d_fwd_kernel<TT, KC, true><<<grid, kWarpsC * 32, 0, (cudaStream_t)stream>>>(
+                             (TT*)y, (const TT*)x, weight, bias, rows, nch, (int)D, (int)T, silu, vec))
+    else
+      AK_K_SWITCH(K, KC, conv1d_fwd_kernel<TT, KC, false><<<grid, kWarpsC * 32, 0, (cudaStream_t)stream>>>(
+                             (TT*)y, (const TT*)x, weight, bias, rows, nch, (int)D, (int)T, silu, vec))
   });
   AK_CHECK_LAUNCH("ak_causal_conv1d_fwd");
   return AK_OK;
@@ -332,9 +339,16 @@ extern "C" int ak_causal_conv1d_bwd(void* dx, float* dweight, float* dbias, void
   const bool vec = aligned16(x) && aligned16(dx) && aligned16(dy) && ((T * elem_size(dt)) % 16 == 0);
   const unsigned grid = (unsigned)((rows * nch + kWarpsC - 1) / kWarpsC);
   float* part = (float*)workspace;
+  const bool full = vec && T % chunk == 0;
   AK_DISPATCH_DTYPE(dt, TT, {
-    AK_K_SWITCH(K, KC, conv1d_bwd_kernel<TT, KC><<<grid, kWarpsC * 32, 0, st>>>(
-                           (TT*)dx, part, (const TT*)x, (const TT*)dy, weight, bias, rows, (int)D, (int)T, silu, nch, vec));
+    if (full)
+      AK_K_SWITCH(K, KC, conv1d_bwd_kernel<TT, KC, true><<<grid, kWarpsC * 32, 0, st>>>(
+                             (TT*)dx, part, (const TT*)x, (const TT*)dy, weight, bias, rows, (int)D, (int)T, silu, nch,
+                             vec))
+    else
+      AK_K_SWITCH(K, KC, conv1d_bwd_kernel<TT, KC, false><<<grid, kWarpsC * 32, 0, st>>>(
+                             (TT*)dx, part, (const TT*)x, (const TT*)dy, weight, bias, rows, (int)D, (int)T, silu, nch,
+                             vec))
   });
   AK_CHECK_LAUNCH("ak_causal_conv1d_bwd");
   AK_K_SWITCH(K, KC, conv1d_dw_reduce<KC><<<(unsigned)((D + 7) / 8), 256, 0, st>>>(dweight, dbias, part, (int)B,

@@ -24,7 +24,8 @@ constexpr int kPerThread = 1;  // 16-byte vectors per thread (occupancy beats pe
 
 // Vector path: grid.y walks the B*H (b, h) planes, grid.x the N*D/VEC vectors
 // of one plane (32-bit index math); tables are read as float4 when VEC/2 == 4.
-template <typename T, int VEC>
+// FULL: the plane's vector count is a multiple of the CTA's, no range guard.
+template <typename T, int VEC, bool FULL>
 __global__ void __launch_bounds__(kThreadsR, 8)
 rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
             int64_t planes, int H, int N, int D, int64_t sb, int64_t sh, int64_t sn_, float sign, bool tab4) {
@@ -43,12 +44,12 @@ rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict_
       const int idx = (blockIdx.x * kPerThread + u) * kThreadsR + threadIdx.x;
       nn[u] = idx / vpr;
       jj[u] = (idx - nn[u] * vpr) * VEC;
-      if (idx < per_plane) load_frag<T, VEC>(v[u], xp + (int64_t)nn[u] * sn_ + jj[u]);
+      if (FULL || idx < per_plane) load_frag<T, VEC>(v[u], xp + (int64_t)nn[u] * sn_ + jj[u]);
     }
 #pragma unroll
     for (int u = 0; u < kPerThread; ++u) {
       const int idx = (blockIdx.x * kPerThread + u) * kThreadsR + threadIdx.x;
-      if (idx >= per_plane) break;
+      if (!FULL && idx >= per_plane) break;
       const int n = nn[u], jb = jj[u];
       float c[VEC / 2], s[VEC / 2];
       const float* cr = cs + (int64_t)n * half + jb / 2;
@@ -124,8 +125,12 @@ int rope_impl(void* y, const void* x, const float* cos_t, const float* sin_t, in
       const unsigned gx = (unsigned)((per_plane + (int64_t)kThreadsR * kPerThread - 1) / ((int64_t)kThreadsR * kPerThread));
       const int64_t planes = B * H;
       const unsigned gy = (unsigned)(planes < 65535 ? planes : 65535);
-      rope_kernel<T, VEC><<<dim3(gx, gy), kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes, (int)H,
-                                                             (int)N, (int)D, sb, sh, sn, sign, tab4);
+      if (per_plane % ((int64_t)kThreadsR * kPerThread) == 0)
+        rope_kernel<T, VEC, true><<<dim3(gx, gy), kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes,
+                                                                     (int)H, (int)N, (int)D, sb, sh, sn, sign, tab4);
+      else
+        rope_kernel<T, VEC, false><<<dim3(gx, gy), kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes,
+                                                                      (int)H, (int)N, (int)D, sb, sh, sn, sign, tab4);
     } else {
       int64_t g = (rows * (D / 2) + kThreadsR - 1) / kThreadsR;
       const int64_t cap = (int64_t)sm_count() * 32;
