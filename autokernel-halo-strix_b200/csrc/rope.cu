@@ -12,7 +12,7 @@
 // stride along D, so q / k can be read straight out of a fused (B, N, W) QKV
 // projection; y is written dense (B, H, N, D).  The head-major transpose that
 // attention wants costs nothing extra.  One thread rotates one 16-byte vector
-// (8 elements of a 16-bit type, 4 of fp32).
+// position (8 elements of a 16-bit type, 4 of fp32) in several (b, h) planes.
 #include "ak_common.cuh"
 
 namespace ak {
@@ -20,63 +20,58 @@ namespace {
 
 constexpr int kThreadsR = 256;
 
-constexpr int kPerThread = 1;  // 16-byte vectors per thread (occupancy beats per-thread depth here)
+constexpr int kPlanesPerCta = 8;  // (b, h) planes one thread walks with the same (n, vector)
 
-// Vector path: grid.y walks the B*H (b, h) planes, grid.x the N*D/VEC vectors
-// of one plane (32-bit index math); tables are read as float4 when VEC/2 == 4.
-// FULL: the plane's vector count is a multiple of the CTA's, no range guard.
+// Vector path: a thread owns one 16-byte vector position (n, j) of a (N, D)
+// plane, loads its cos / sin once and applies them to kPlanesPerCta planes
+// (grid.y): per plane only an address step, one load, the rotation and one
+// store.  grid.x covers the N*D/VEC vector positions.
 template <typename T, int VEC, bool FULL>
-__global__ void __launch_bounds__(kThreadsR, 8)
+__global__ void __launch_bounds__(kThreadsR, 6)
 rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
             int64_t planes, int H, int N, int D, int64_t sb, int64_t sh, int64_t sn_, float sign, bool tab4) {
   const int vpr = D / VEC;
   const int per_plane = N * vpr;
   const int half = D / 2;
-  for (int64_t p = blockIdx.y; p < planes; p += gridDim.y) {
-    const int64_t b = p / H;
-    const int h = (int)(p - b * H);
-    const T* xp = x + b * sb + h * sh;
-    T* yp = y + p * (int64_t)N * D;
-    float v[kPerThread][VEC];
-    int nn[kPerThread], jj[kPerThread];
+  const int idx = blockIdx.x * kThreadsR + threadIdx.x;
+  if (!FULL && idx >= per_plane) return;
+  const int n = idx / vpr;
+  const int jb = (idx - n * vpr) * VEC;
+  float c[VEC / 2], s[VEC / 2];
+  const float* cr = cs + (int64_t)n * half + jb / 2;
+  const float* sr = sn + (int64_t)n * half + jb / 2;
+  if constexpr (VEC / 2 == 4) {
+    if (tab4) {
+      const float4 c4 = __ldg(reinterpret_cast<const float4*>(cr));
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(sr));
+      c[0] = c4.x; c[1] = c4.y; c[2] = c4.z; c[3] = c4.w;
+      s[0] = s4.x; s[1] = s4.y; s[2] = s4.z; s[3] = s4.w;
+    } else {
 #pragma unroll
-    for (int u = 0; u < kPerThread; ++u) {
-      const int idx = (blockIdx.x * kPerThread + u) * kThreadsR + threadIdx.x;
-      nn[u] = idx / vpr;
-      jj[u] = (idx - nn[u] * vpr) * VEC;
-      if (FULL || idx < per_plane) load_frag<T, VEC>(v[u], xp + (int64_t)nn[u] * sn_ + jj[u]);
+      for (int k = 0; k < 4; ++k) { c[k] = __ldg(cr + k); s[k] = __ldg(sr + k); }
     }
+  } else {
 #pragma unroll
-    for (int u = 0; u < kPerThread; ++u) {
-      const int idx = (blockIdx.x * kPerThread + u) * kThreadsR + threadIdx.x;
-      if (!FULL && idx >= per_plane) break;
-      const int n = nn[u], jb = jj[u];
-      float c[VEC / 2], s[VEC / 2];
-      const float* cr = cs + (int64_t)n * half + jb / 2;
-      const float* sr = sn + (int64_t)n * half + jb / 2;
-      if constexpr (VEC / 2 == 4) {
-        if (tab4) {
-          const float4 c4 = __ldg(reinterpret_cast<const float4*>(cr));
-          const float4 s4 = __ldg(reinterpret_cast<const float4*>(sr));
-          c[0] = c4.x; c[1] = c4.y; c[2] = c4.z; c[3] = c4.w;
-          s[0] = s4.x; s[1] = s4.y; s[2] = s4.z; s[3] = s4.w;
-        } else {
+    for (int k = 0; k < VEC / 2; ++k) { c[k] = __ldg(cr + k); s[k] = __ldg(sr + k); }
+  }
 #pragma unroll
-          for (int k = 0; k < 4; ++k) { c[k] = __ldg(cr + k); s[k] = __ldg(sr + k); }
-        }
-      } else {
+  for (int k = 0; k < VEC / 2; ++k) s[k] *= sign;
+  const int64_t xo = (int64_t)n * sn_ + jb, yo = (int64_t)n * D + jb, ystep = (int64_t)N * D;
+  const int64_t p0 = (int64_t)blockIdx.y * kPlanesPerCta;
+  const int64_t p1 = p0 + kPlanesPerCta < planes ? p0 + kPlanesPerCta : planes;
+  int64_t b = p0 / H;
+  int h = (int)(p0 - b * H);
+#pragma unroll 2
+  for (int64_t p = p0; p < p1; ++p) {
+    float v[VEC], o[VEC];
+    load_frag<T, VEC>(v, x + b * sb + h * sh + xo);
 #pragma unroll
-        for (int k = 0; k < VEC / 2; ++k) { c[k] = __ldg(cr + k); s[k] = __ldg(sr + k); }
-      }
-      float o[VEC];
-#pragma unroll
-      for (int k = 0; k < VEC / 2; ++k) {
-        const float sk = sign * s[k];
-        o[2 * k] = v[u][2 * k] * c[k] - v[u][2 * k + 1] * sk;
-        o[2 * k + 1] = v[u][2 * k] * sk + v[u][2 * k + 1] * c[k];
-      }
-      store_frag<T, VEC>(yp + (int64_t)n * D + jb, o);
+    for (int k = 0; k < VEC / 2; ++k) {
+      o[2 * k] = v[2 * k] * c[k] - v[2 * k + 1] * s[k];
+      o[2 * k + 1] = v[2 * k] * s[k] + v[2 * k + 1] * c[k];
     }
+    store_frag<T, VEC>(y + p * ystep + yo, o);
+    if (++h == H) { h = 0; ++b; }
   }
 }
 
@@ -118,14 +113,16 @@ int rope_impl(void* y, const void* x, const float* cos_t, const float* sin_t, in
                       (sn * es) % 16 == 0;
   const bool tab4 = aligned16(cos_t) && aligned16(sin_t) && (D / 2) % 4 == 0;
   AK_REQUIRE(!vec_ok || N * (D / vecw) < (1LL << 31), AK_ERR_SHAPE, "%s: N*D too large", who);
+  AK_REQUIRE(!vec_ok || (B * H + kPlanesPerCta - 1) / kPlanesPerCta < 65536, AK_ERR_SHAPE,
+             "%s: more than %d (b, h) planes", who, 65535 * kPlanesPerCta);
   AK_DISPATCH_DTYPE(dt, T, {
     constexpr int VEC = 16 / sizeof(T);
     if (vec_ok) {
       const int64_t per_plane = N * (D / VEC);
-      const unsigned gx = (unsigned)((per_plane + (int64_t)kThreadsR * kPerThread - 1) / ((int64_t)kThreadsR * kPerThread));
+      const unsigned gx = (unsigned)((per_plane + kThreadsR - 1) / kThreadsR);
       const int64_t planes = B * H;
-      const unsigned gy = (unsigned)(planes < 65535 ? planes : 65535);
-      if (per_plane % ((int64_t)kThreadsR * kPerThread) == 0)
+      const unsigned gy = (unsigned)((planes + kPlanesPerCta - 1) / kPlanesPerCta);
+      if (per_plane % kThreadsR == 0)
         rope_kernel<T, VEC, true><<<dim3(gx, gy), kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes,
                                                                      (int)H, (int)N, (int)D, sb, sh, sn, sign, tab4);
       else
