@@ -323,6 +323,22 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
             res[k] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
                       "note": "L2 flushed (256 MB write) before each rep; flush time subtracted"}
         del x, dy, flush
+        # bf16 at the training shape [16384, 768] (16 x 1024 tokens per GPU): 25 MB per tensor, same flush
+        xb = torch.randn(16384, 768, generator=g).to(torch.bfloat16).to(dev)
+        wb = (1 + 0.02 * torch.randn(768, generator=g)).to(torch.bfloat16).to(dev)
+        dyb = torch.randn(16384, 768, generator=g).to(torch.bfloat16).to(dev)
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        Eb = 16384 * 768
+        fwb, bwb = 2 * Eb * 2 + 768 * 2, 3 * Eb * 2 + 2 * 768 * 2
+        timeit(lambda: (flush.zero_(), _ak.rmsnorm_fwd(xb, wb, 1e-6)), fwb, "rmsnorm_fwd_bf16_16384x768", steps * 4)
+        timeit(lambda: (flush.zero_(), _ak.rmsnorm_bwd(xb, wb, dyb, 1e-6)), bwb, "rmsnorm_bwd_bf16_16384x768",
+               steps * 4)
+        for k, nb in (("rmsnorm_fwd_bf16_16384x768", fwb), ("rmsnorm_bwd_bf16_16384x768", bwb)):
+            ms = max(res[k]["ms"] - fl, 1e-6)
+            gbs = nb / ms / 1e6
+            res[k] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
+                      "note": "L2 flushed (256 MB write) before each rep; flush time subtracted"}
+        del xb, dyb, flush
 
     if want("softmax"):
         # Softmax causal scores bf16 [96*2048, 2048] (config 3): 805 MB per tensor > L2.

@@ -1,0 +1,133 @@
+"""Our selective scan vs the reference's own mamba CUDA kernels (`selective_scan_cuda`, the
+vendored mamba_ssm 2.3.0 sources built for sm_100a by oracle/build_mamba_ref.py).
+
+* parity: forward (out, last_state) and every gradient on the same inputs, through the
+  reference's own call sequence (SelectiveScanFn, selective_scan_interface.py:23-83);
+* speed: both at the headline configuration (B=8, D=1536, L=2048, N=16, bf16), CUDA events on
+  the current stream; written to $AK_COMPARATOR_OUT (JSON) when that is set.
+
+Skipped when the comparator has not been built (it needs the reference checkout to build).
+"""
+import json
+import os
+
+import pytest
+import torch
+
+from conftest import assert_lowp_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _mod():
+    from oracle.build_mamba_ref import load_built
+    m = load_built()
+    if m is None:
+        pytest.skip("reference selective_scan_cuda not built (oracle/build_mamba_ref.py)")
+    return m
+
+
+def _inputs(Bsz, D, L, N, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    u = torch.randn(Bsz, D, L, generator=g).to(bf)
+    delta = (torch.randn(Bsz, D, L, generator=g) - 4.6).to(bf)
+    A = -torch.arange(1, N + 1, dtype=torch.float32).repeat(D, 1)
+    Bm = torch.randn(Bsz, N, L, generator=g).to(bf)
+    Cm = torch.randn(Bsz, N, L, generator=g).to(bf)
+    Dv = torch.rand(D, generator=g)
+    z = torch.randn(Bsz, D, L, generator=g).to(bf)
+    bias = torch.rand(D, generator=g) * 0.5 - 4.0
+    dout = torch.randn(Bsz, D, L, generator=g).to(bf)
+    return [t.to(DEV) for t in (u, delta, A, Bm, Cm, Dv, z, bias, dout)]
+
+
+def _theirs(mod, u, delta, A, Bm, Cm, Dv, z, bias, dout):
+    """The reference call sequence: fwd, then bwd with the saved x and out."""
+    B4, C4 = Bm.unsqueeze(1), Cm.unsqueeze(1)
+    out, x, out_z = mod.fwd(u, delta, A, B4, C4, Dv, z, bias, True)
+    last = x[:, :, -1, 1::2]
+    du, ddelta, dA, dB, dC, dD, dbias, dz = mod.bwd(u, delta, A, B4, C4, Dv, z, bias, dout, x, out, None, True,
+                                                   False)
+    return out_z, last, (du, ddelta, dA, dB.squeeze(1), dC.squeeze(1), dD, dz, dbias)
+
+
+def _ours(u, delta, A, Bm, Cm, Dv, z, bias, dout):
+    from kernels.mamba_scan import selective_scan_fn
+    ins = [t.detach().clone().requires_grad_(t.is_floating_point()) for t in (u, delta, A, Bm, Cm, Dv, z, bias)]
+    out, last = selective_scan_fn(*ins[:5], D=ins[5], z=ins[6], delta_bias=ins[7], delta_softplus=True,
+                                  return_last_state=True)
+    out.backward(dout)
+    g = [t.grad for t in ins]
+    return out, last, (g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7])
+
+
+def test_parity_with_reference_cuda_kernel():
+    mod = _mod()
+    args = _inputs(2, 64, 2048, 16, seed=1)
+    o1, l1, g1 = _theirs(mod, *args)
+    o2, l2, g2 = _ours(*args)
+    assert_lowp_close(o2, o1, what="out")
+    torch.testing.assert_close(l2, l1, rtol=1e-3, atol=1e-3)
+    names = ("du", "ddelta", "dA", "dB", "dC", "dD", "dz", "ddelta_bias")
+    for n, a, b in zip(names, g2, g1):
+        scale = b.float().abs().max().item()
+        err = (a.float() - b.float()).abs().max().item()
+        # bf16 outputs: the elementwise low-precision bound; fp32 reductions (dA, dB, dC, dD,
+        # ddelta_bias) differ in summation order: 1e-2 of the largest value
+        if a.dtype == torch.bfloat16:
+            assert_lowp_close(a, b, what=n)
+        else:
+            assert err <= 1e-2 * max(scale, 1e-30), f"{n}: max err {err:.3e} vs scale {scale:.3e}"
+
+
+def _time(fn, reps=10, warm=3):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def test_speed_against_reference_cuda_kernel():
+    from kernels import _ak
+    mod = _mod()
+    u, delta, A, Bm, Cm, Dv, z, bias, dout = _inputs(8, 1536, 2048, 16)
+    B4, C4 = Bm.unsqueeze(1), Cm.unsqueeze(1)
+    saved = {}
+
+    def ref_fwd():
+        saved["r"] = mod.fwd(u, delta, A, B4, C4, Dv, z, bias, True)
+
+    def ref_bwd():
+        out, x, _ = saved["r"]
+        mod.bwd(u, delta, A, B4, C4, Dv, z, bias, dout, x, out, None, True, False)
+
+    def our_fwd():
+        saved["o"] = _ak.selective_scan_fwd(u, delta, A, Bm, Cm, Dv, z, bias, True)
+
+    def our_bwd():
+        _out, _last, states = saved["o"]
+        _ak.selective_scan_bwd(dout, u, delta, A, Bm, Cm, Dv, z, bias, True, states)
+
+    rf = _time(ref_fwd)
+    rb = _time(ref_bwd)
+    of = _time(our_fwd)
+    ob = _time(our_bwd)
+    res = {"config": "B=8 D=1536 L=2048 N=16 bf16, z, delta_bias, softplus",
+           "reference_cuda": {"impl": "mamba_ssm 2.3.0 selective_scan_cuda built for sm_100a",
+                              "fwd_ms": round(rf, 4), "bwd_ms": round(rb, 4), "total_ms": round(rf + rb, 4)},
+           "ours": {"fwd_ms": round(of, 4), "bwd_ms": round(ob, 4), "total_ms": round(of + ob, 4)},
+           "speedup_total": round((rf + rb) / (of + ob), 3)}
+    print(json.dumps(res))
+    path = os.environ.get("AK_COMPARATOR_OUT")
+    if path:
+        with open(path, "w") as f:
+            json.dump(res, f, indent=1)
+    assert of > 0 and ob > 0
