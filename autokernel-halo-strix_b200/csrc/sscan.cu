@@ -32,8 +32,10 @@
 // g_t = dy_t C_t + a_{t+1} g_{t+1} is scanned right-to-left with the same
 // two-level scheme; the adjoint carry crosses chunks pre-multiplied by a at
 // the chunk's first step.  dB/dC (sums over the channels of a group) are
-// reduced in shared memory across the CTA's channels and flushed once per
-// chunk with vectorised fp32 global reductions; dA/dD/dbias are per-(batch,
+// reduced in shared memory across the CTA's channels: a warp takes a per-state
+// row lock and adds its values in place (plain read-modify-write; warps walk
+// the states in staggered order so the locks are rarely contended), and the
+// rows are flushed once per chunk with vectorised fp32 global reductions; dA/dD/dbias are per-(batch,
 // channel) partials reduced in a fixed order by a second kernel.
 #include "ak_common.cuh"
 
@@ -381,6 +383,7 @@ sscan_bwd_kernel(SsParams p) {
   float* sdA = sg + cpc * N;       // dA partials [cpc][N]
   float* sdD = sdA + cpc * N;      // dD partials [cpc]
   float* sdb = sdD + cpc;          // dbias partials [cpc]
+  int* slock = reinterpret_cast<int*>(sdb + cpc);  // one lock word per state row of sdB / sdC
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.y;
@@ -394,6 +397,7 @@ sscan_bwd_kernel(SsParams p) {
 
   for (int i = threadIdx.x; i < 2 * N * CH; i += blockDim.x) sdB[i] = 0.f;
   for (int i = threadIdx.x; i < 2 * cpc * N + 2 * cpc; i += blockDim.x) sg[i] = 0.f;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) slock[i] = 0;
   if (threadIdx.x == 0) {
     mbar_init(bar, 1);
     mbar_fence_init();
@@ -443,7 +447,11 @@ sscan_bwd_kernel(SsParams p) {
       const float hc_l = (k > 0 && lane < N) ? p.chunk_states_in[(chan * p.nsaved + (k - 1)) * N + lane] : 0.f;
       float dAl_keep = 0.f;  // lane n < N keeps state n's dA partial
 
-      for (int n = 0; n < N; ++n) {
+      // warps visit the states in staggered order (warp w starts at w*N/nw), so two warps are
+      // rarely on the same state row of sdB / sdC at once; the row lock below makes it exclusive
+      const int nstart = (warp * N) / p.nw;
+      for (int nn = 0; nn < N; ++nn) {
+        const int n = nn + nstart < N ? nn + nstart : nn + nstart - N;
         const float An = __shfl_sync(0xffffffffu, A_l, n);
         const float A2 = An * kLog2e;
         float a[ITEMS], h[ITEMS], Bv[ITEMS], Cv[ITEMS];
@@ -493,6 +501,7 @@ sscan_bwd_kernel(SsParams p) {
         const float gfirst0 = __shfl_sync(0xffffffffu, a[0] * fmaf(Q, gc, G), 0);
         float gg = (lane == 31) ? gc : fmaf(Qd, gc, Gd);
         float dAl = 0.f;
+        float gsv[ITEMS];  // the adjoint per step, for the dB contribution below
 #pragma unroll
         for (int i = ITEMS - 1; i >= 0; --i) {
           const float ra = (i == ITEMS - 1) ? ra_last : a[i + 1];
@@ -503,9 +512,34 @@ sscan_bwd_kernel(SsParams p) {
           const float gB = gg * Bv[i];
           ddl[i] = fmaf(ea, An, fmaf(gB, uu[i], ddl[i]));
           duacc[i] = fmaf(gB, dlt[i], duacc[i]);
-          const int si = n * CH + i * 32 + lane;  // [n][item][lane]: conflict-free
-          atomicAdd(&sdB[si], gg * dlt[i] * uu[i]);
-          atomicAdd(&sdC[si], dy[i] * h[i]);
+          gsv[i] = gg;
+        }
+        // row n of sdB / sdC under its lock: a short plain read-modify-write section
+        // (no per-element atomics)
+        {
+          bool owned = true;
+          if (lane == 0) {
+            uint32_t spins = 0;
+            while (atomicCAS(&slock[n], 0, 1) != 0) {
+              if (++spins > kMaxSpins) { atomicExch(&g_sscan_err, (int)AK_ERR_TIMEOUT); owned = false; break; }
+              if (spins > 16) __nanosleep(20);
+            }
+            __threadfence_block();
+          }
+          owned = __shfl_sync(0xffffffffu, owned, 0);
+          if (owned) {
+#pragma unroll
+            for (int i = 0; i < ITEMS; ++i) {
+              const int si = n * CH + i * 32 + lane;  // [n][item][lane]: conflict-free
+              sdB[si] += gsv[i] * dlt[i] * uu[i];
+              sdC[si] += dy[i] * h[i];
+            }
+          }
+          __syncwarp();
+          if (lane == 0 && owned) {
+            __threadfence_block();
+            atomicExch(&slock[n], 0);
+          }
         }
         dAl = warp_sum(dAl);
         if (lane == n) dAl_keep += dAl;
@@ -624,7 +658,8 @@ size_t fwd_smem(int N, int cpc) {
 
 template <typename T, int CH>
 size_t bwd_smem(int N, int cpc) {
-  return 128 + stage_bytes<T, CH>(N) + (size_t)4 * N * CH * 4 + (size_t)(2 * cpc * N + 2 * cpc) * 4;
+  return 128 + stage_bytes<T, CH>(N) + (size_t)4 * N * CH * 4 + (size_t)(2 * cpc * N + 2 * cpc) * 4 +
+         (size_t)N * 4;  // + row locks
 }
 
 }  // namespace
