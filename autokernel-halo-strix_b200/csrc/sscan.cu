@@ -360,6 +360,21 @@ sscan_fwd_kernel(SsParams p) {
 // ============================================================================
 // Backward
 // ============================================================================
+// CTA-scope lock word in shared memory: acquire = CAS 0 -> 1 with acquire
+// semantics (returns the old value), release = store 0 with release semantics.
+__device__ __forceinline__ int lock_try_acquire(int* w) {
+  int old;
+  asm volatile("atom.acquire.cta.shared::cta.cas.b32 %0, [%1], 0, 1;"
+               : "=r"(old)
+               : "r"((uint32_t)__cvta_generic_to_shared(w))
+               : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void lock_release(int* w) {
+  asm volatile("st.release.cta.shared::cta.b32 [%0], 0;" ::"r"((uint32_t)__cvta_generic_to_shared(w)) : "memory");
+}
+
 __device__ __forceinline__ void red_add_v4(float* addr, float4 v) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
                "f"(v.w)
@@ -520,13 +535,12 @@ sscan_bwd_kernel(SsParams p) {
           bool owned = true;
           if (lane == 0) {
             uint32_t spins = 0;
-            while (atomicCAS(&slock[n], 0, 1) != 0) {
+            while (lock_try_acquire(&slock[n]) != 0) {
               if (++spins > kMaxSpins) { atomicExch(&g_sscan_err, (int)AK_ERR_TIMEOUT); owned = false; break; }
               if (spins > 16) __nanosleep(20);
             }
-            __threadfence_block();
           }
-          owned = __shfl_sync(0xffffffffu, owned, 0);
+          owned = __shfl_sync(0xffffffffu, owned, 0);  // also orders the lanes after lane 0's acquire
           if (owned) {
 #pragma unroll
             for (int i = 0; i < ITEMS; ++i) {
@@ -535,11 +549,8 @@ sscan_bwd_kernel(SsParams p) {
               sdC[si] += dy[i] * h[i];
             }
           }
-          __syncwarp();
-          if (lane == 0 && owned) {
-            __threadfence_block();
-            atomicExch(&slock[n], 0);
-          }
+          __syncwarp();  // every lane's row update is ordered before lane 0's release
+          if (lane == 0 && owned) lock_release(&slock[n]);
         }
         dAl = warp_sum(dAl);
         if (lane == n) dAl_keep += dAl;
