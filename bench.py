@@ -41,7 +41,9 @@ FALLBACK_BF16_TFLOPS = 1590.0
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from ncu captures, scaled
 # to the full config where the capture was smaller (see profiles/).  None = not captured.
 NCU_TRAFFIC_BYTES = {
-    "sscan_bwd": None,
+    # B=4 capture (profiles/selective_scan_kernels_B4_*): 106,179,072 read + 42,633,984 written,
+    # x2 for B=8 (every input, output and B/C tile is per batch row, so traffic is linear in B)
+    "sscan_bwd": 2 * (106_179_072 + 42_633_984),
 }
 
 
