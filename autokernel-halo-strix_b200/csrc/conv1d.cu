@@ -232,6 +232,7 @@ conv1d_bwd_kernel(T* __restrict__ dx, float* __restrict__ part, const T* __restr
     for (int k = 0; k < K; ++k) pr[k] = dwacc[k];
     pr[K] = dbacc;
   }
+  pdl_trigger();
 }
 
 // One warp per channel d: lanes stride over the B * nch partial records in a
@@ -239,6 +240,7 @@ conv1d_bwd_kernel(T* __restrict__ dx, float* __restrict__ part, const T* __restr
 template <int K>
 __global__ void conv1d_dw_reduce(float* __restrict__ dw, float* __restrict__ dbias, const float* __restrict__ part,
                                  int B, int D, int nch) {
+  pdl_wait();  // the backward kernel's partial records are complete and visible
   const int lane = threadIdx.x & 31;
   const int d = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (d >= D) return;
@@ -351,8 +353,10 @@ extern "C" int ak_causal_conv1d_bwd(void* dx, float* dweight, float* dbias, void
                              vec))
   });
   AK_CHECK_LAUNCH("ak_causal_conv1d_bwd");
-  AK_K_SWITCH(K, KC, conv1d_dw_reduce<KC><<<(unsigned)((D + 7) / 8), 256, 0, st>>>(dweight, dbias, part, (int)B,
-                                                                                     (int)D, nch));
+  AK_K_SWITCH(K, KC,
+              AK_CUDA_TRY(launch_pdl(conv1d_dw_reduce<KC>, dim3((unsigned)((D + 7) / 8)), dim3(256), 0, st, dweight,
+                                     dbias, (const float*)part, (int)B, (int)D, nch),
+                          "ak_causal_conv1d_bwd(reduce)"));
   AK_CHECK_LAUNCH("ak_causal_conv1d_bwd(reduce)");
   return AK_OK;
 }

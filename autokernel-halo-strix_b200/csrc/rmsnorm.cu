@@ -220,6 +220,7 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
     for (int i = 0; i < kWarps; ++i) s += s_dw[i * kSlots + sl];
     dw_part[(int64_t)blockIdx.x * N + c] = s;
   }
+  pdl_trigger();
 }
 
 // Backward fallback (wide / unaligned rows): one CTA per row at a time, the
@@ -269,6 +270,7 @@ template <typename TD>
 __global__ void __launch_bounds__(1024)
 rmsnorm_dw_reduce(TD* __restrict__ dw, const float* __restrict__ part, int G, int N) {
   __shared__ float s[32][33];
+  pdl_wait();  // the backward kernel's partial rows are complete and visible
   const int c = blockIdx.x * 32 + threadIdx.x;
   float acc = 0.f;
   if (c < N)
@@ -411,7 +413,9 @@ int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const voi
   const int Gred = M > 0 ? G : 0;
   dim3 rb(32, 32);
   const unsigned rg = (unsigned)((N + 31) / 32);
-  AK_DISPATCH_DTYPE(dt_dw, TD, rmsnorm_dw_reduce<TD><<<rg, rb, 0, st>>>((TD*)dw, ws, Gred, N));
+  AK_DISPATCH_DTYPE(dt_dw, TD,
+                    AK_CUDA_TRY(launch_pdl(rmsnorm_dw_reduce<TD>, dim3(rg), rb, 0, st, (TD*)dw, (const float*)ws, Gred, N),
+                                "ak_rmsnorm_bwd(dw reduce)"));
   AK_CHECK_LAUNCH("ak_rmsnorm_bwd(dw reduce)");
   return AK_OK;
 }
@@ -563,7 +567,10 @@ int bwd_noalloc_impl(void* dx, void* dw, int dt_dw, float* ws, int G, const void
   }
   dim3 rb(32, 32);
   const unsigned rg = (unsigned)((N + 31) / 32);
-  AK_DISPATCH_DTYPE(dt_dw, TD, rmsnorm_dw_reduce<TD><<<rg, rb, 0, st>>>((TD*)dw, ws, M > 0 ? G : 0, N));
+  AK_DISPATCH_DTYPE(dt_dw, TD,
+                    AK_CUDA_TRY(launch_pdl(rmsnorm_dw_reduce<TD>, dim3(rg), rb, 0, st, (TD*)dw, (const float*)ws,
+                                           M > 0 ? G : 0, N),
+                                "ak_rmsnorm_bwd_noalloc(dw reduce)"));
   AK_CHECK_LAUNCH("ak_rmsnorm_bwd_noalloc(dw reduce)");
   return AK_OK;
 }

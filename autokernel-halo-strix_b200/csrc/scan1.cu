@@ -204,9 +204,11 @@ scan1_bwd_kernel(float* __restrict__ gdA, float* __restrict__ gdBx, float* __res
     for (int k = 0; k < kW; ++k) s += sD[k][lane];
     gdpart[b * d + c] = s;
   }
+  pdl_trigger();
 }
 
 __global__ void scan1_gd_reduce(float* __restrict__ gD, const float* __restrict__ part, int B, int d) {
+  pdl_wait();  // the backward kernel's per-(b, c) partials are complete and visible
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= d) return;
   float s = 0.f;
@@ -268,7 +270,9 @@ extern "C" int ak_scan1_bwd(float* gdA, float* gdBx, float* gC, float* gD, float
   scan1_bwd_kernel<kSegB><<<grid, kW * 32, 0, st>>>(gdA, gdBx, gC, gx, gdpart, carries, dA, dBx, C, D, x, gy,
                                                     (int)L, (int)d, nch);
   AK_CHECK_LAUNCH("ak_scan1_bwd");
-  scan1_gd_reduce<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(gD, gdpart, (int)B, (int)d);
+  AK_CUDA_TRY(launch_pdl(scan1_gd_reduce, dim3((unsigned)((d + 255) / 256)), dim3(256), 0, st, gD,
+                         (const float*)gdpart, (int)B, (int)d),
+              "ak_scan1_bwd(gD)");
   AK_CHECK_LAUNCH("ak_scan1_bwd(gD)");
   return AK_OK;
 }

@@ -618,11 +618,14 @@ sscan_bwd_kernel(SsParams p) {
     pr[N] = sdD[i];
     pr[N + 1] = sdb[i];
   }
+  pdl_trigger();
 }
 
 // dA[d,n], dD[d], dbias[d] = fixed-order sums over the batch of the partials.
 __global__ void sscan_bwd_reduce(float* __restrict__ dA, float* __restrict__ dD, float* __restrict__ dbias,
                                  const float* __restrict__ part, int batch, int dim, int N) {
+  pdl_wait();  // the backward kernel's partials (and dB / dC accumulators) are complete
+  pdl_trigger();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t per = N + 2;
   if (i >= (int64_t)dim * per) return;
@@ -635,10 +638,15 @@ __global__ void sscan_bwd_reduce(float* __restrict__ dA, float* __restrict__ dD,
   else { if (dbias) dbias[d] = s; }
 }
 
+// dB and dC fp32 accumulators -> the output dtype (one launch for both).
 template <typename T>
-__global__ void f32_to(T* __restrict__ dst, const float* __restrict__ src, int64_t n) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    dst[i] = from_f<T>(src[i]);
+__global__ void f32_to2(T* __restrict__ d0, const float* __restrict__ s0, T* __restrict__ d1,
+                        const float* __restrict__ s1, int64_t n) {
+  pdl_wait();  // after the reduce, which itself waited for the backward kernel
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    d0[i] = from_f<T>(s0[i]);
+    d1[i] = from_f<T>(s1[i]);
+  }
 }
 
 // Channels per CTA: the largest candidate dividing dim/groups.
@@ -795,14 +803,13 @@ extern "C" int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB
   });
   AK_CHECK_LAUNCH("ak_selective_scan_bwd");
   const int64_t nred = dim * (dstate + 2);
-  sscan_bwd_reduce<<<(unsigned)((nred + 255) / 256), 256, 0, st>>>(dA, dD, ddelta_bias, p.part, (int)batch,
-                                                                  (int)dim, (int)dstate);
-  AK_CHECK_LAUNCH("ak_selective_scan_bwd(reduce)");
+  AK_CUDA_TRY(launch_pdl(sscan_bwd_reduce, dim3((unsigned)((nred + 255) / 256)), dim3(256), 0, st, dA, dD,
+                         ddelta_bias, (const float*)p.part, (int)batch, (int)dim, (int)dstate),
+              "ak_selective_scan_bwd(reduce)");
   const unsigned cg = (unsigned)std::min<int64_t>((int64_t)(nbc + 255) / 256, (int64_t)sm_count() * 8);
-  AK_DISPATCH_DTYPE(dt, T, {
-    f32_to<T><<<cg, 256, 0, st>>>((T*)dB, p.dB_acc, (int64_t)nbc);
-    f32_to<T><<<cg, 256, 0, st>>>((T*)dC, p.dC_acc, (int64_t)nbc);
-  });
-  AK_CHECK_LAUNCH("ak_selective_scan_bwd(convert)");
+  AK_DISPATCH_DTYPE(dt, T,
+                    AK_CUDA_TRY(launch_pdl(f32_to2<T>, dim3(cg), dim3(256), 0, st, (T*)dB, (const float*)p.dB_acc,
+                                           (T*)dC, (const float*)p.dC_acc, (int64_t)nbc),
+                                "ak_selective_scan_bwd(convert)"));
   return AK_OK;
 }

@@ -570,7 +570,8 @@ def run_ours(args, world, rank, local):
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
                 "api": "kernels.mamba_scan.selective_scan_fn + autograd backward, pinned host inputs"},
-        "gpu_launches": 5 * args.steps,
+        # per timed step: sscan_fwd_kernel; sscan_bwd_kernel, sscan_bwd_reduce, f32_to2 (dB and dC)
+        "gpu_launches": 4 * args.steps,
         "clocks": clocks,
     }
     if ops is not None:
