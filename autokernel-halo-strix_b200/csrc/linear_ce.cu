@@ -409,8 +409,11 @@ lce_mean(float* __restrict__ loss, float* __restrict__ inv_valid, const float* _
          const int64_t* __restrict__ labels, int64_t M, int64_t ignore_index) {
   __shared__ float r0[32], r1[32];
   float a = 0.f, n = 0.f;
+#pragma unroll 4
   for (int64_t i = threadIdx.x; i < M; i += blockDim.x) {
-    if (labels[i] != ignore_index) { a += losses[i]; n += 1.f; }
+    const int64_t lb = labels[i];
+    const float li = losses[i];  // unconditional: both loads in flight together
+    if (lb != ignore_index) { a += li; n += 1.f; }
   }
   a = warp_sum(a);
   n = warp_sum(n);
@@ -442,28 +445,41 @@ __global__ void transpose16(T* __restrict__ out, const T* __restrict__ in, int64
 }
 
 // In place over 16-bit logits L[M][V]: L = (softmax(L) - onehot(label)) / n_valid,
-// zero rows for ignored labels.  V % 8 == 0, so each 8-element vector is in one row.
+// zero rows for ignored labels.  V % 8 == 0.  A CTA walks whole rows (the row's
+// lse and label stay in registers, no per-vector division); each thread loads
+// kGradBatch 16-byte vectors before using any of them.
+constexpr int kGradBatch = 4;
+
 template <typename T>
 __global__ void __launch_bounds__(256)
 lce_grad_inplace(T* __restrict__ L, const float* __restrict__ lse, const int64_t* __restrict__ labels,
                  const float* __restrict__ inv_valid, int64_t M, int64_t V, int64_t ignore_index) {
   const float sc0 = *inv_valid;
-  const int64_t nvec = M * V / 8;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t e = i * 8;
-    const int64_t row = e / V, col = e - row * V;
+  const int nv = (int)(V / 8);
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const int64_t lab = labels[row];
     const float sc = (lab == ignore_index) ? 0.f : sc0;
     const float l2 = lse[row] * kLog2e;
-    float f[8];
-    load_frag<T, 8>(f, L + e);
+    T* Lr = L + row * V;
+    for (int v0 = threadIdx.x; v0 < nv; v0 += kGradBatch * 256) {
+      float f[kGradBatch][8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float gv = ex2(fmaf(f[k], kLog2e, -l2)) * sc;
-      if (col + k == lab) gv -= sc;
-      f[k] = gv;
+      for (int u = 0; u < kGradBatch; ++u)
+        if (v0 + u * 256 < nv) load_frag<T, 8>(f[u], Lr + (int64_t)(v0 + u * 256) * 8);
+#pragma unroll
+      for (int u = 0; u < kGradBatch; ++u) {
+        const int v = v0 + u * 256;
+        if (v >= nv) break;
+        const int64_t col = (int64_t)v * 8;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          float gv = ex2(fmaf(f[u][k], kLog2e, -l2)) * sc;
+          if (col + k == lab) gv -= sc;
+          f[u][k] = gv;
+        }
+        store_frag<T, 8>(Lr + col, f[u]);
+      }
     }
-    store_frag<T, 8>(L + e, f);
   }
 }
 
@@ -702,7 +718,7 @@ extern "C" int ak_linear_ce_logits_grad(float* loss, float* lse, void* G, void* 
   lce_rows_reduce<<<(unsigned)((N * 32 + 255) / 256), 256, 0, st>>>(lse, losses, part, tlogit, labels, (int)N,
                                                                     2 * ntiles, ignore_index);
   lce_mean<<<1, 1024, 0, st>>>(loss, inv_valid, losses, labels, N, ignore_index);
-  const unsigned grid = (unsigned)std::min<int64_t>((N * V / 8 + 255) / 256, (int64_t)sm_count() * 16);
+  const unsigned grid = (unsigned)std::min<int64_t>(N, (int64_t)sm_count() * 8);
   if (bf16)
     lce_grad_inplace<__nv_bfloat16><<<grid, 256, 0, st>>>((__nv_bfloat16*)G, lse, labels, inv_valid, N, V,
                                                          ignore_index);
