@@ -11,7 +11,8 @@
 //
 // Work decomposition.  A CTA owns `cpc` channels of one batch row (all in one
 // B/C group) and walks L in chunks of 32 lanes x ITEMS steps: lane l owns the
-// ITEMS consecutive steps starting at l*ITEMS.  The chunk's B and C tiles
+// ITEMS consecutive steps starting at l*ITEMS (forward: 16 when the tiles fit in
+// shared memory, else 8; backward: 8).  The chunk's B and C tiles
 // (N x chunk, shared by every channel of the CTA) arrive by bulk async copy
 // (TMA engine, mbarrier-completed) as 16-bit values into a staging buffer and
 // are converted once per CTA into an fp32 tile laid out [n][quad][lane][4], so
@@ -47,6 +48,8 @@ namespace {
 constexpr int kStateStride = 256;  // timesteps between saved states
 constexpr int kItems = 8;          // steps per lane: chunk = 256 steps = kStateStride
 static_assert(32 * kItems == kStateStride, "chunk must equal the state stride");
+constexpr int kFwdItems = 16;      // forward steps per lane when shared memory allows (chunk 512)
+constexpr int kFwdInterleave = 1;  // states interleaved per pass at 16 steps per lane (registers)
 
 __device__ int g_sscan_err;  // AK_ERR_TIMEOUT if a bounded wait gave up
 
@@ -278,11 +281,15 @@ __device__ __forceinline__ void fwd_states(int n0, int N, const float (&dlt)[ITE
   }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(256, 3)  // 3 CTAs (24 warps) per SM
+// ITEMS steps per lane: 8 (chunk = one state stride) or 16 (chunk = two state
+// strides; lanes 15 and 31 save the states, the shuffle scan is amortised over
+// twice the steps).  KI states are interleaved per pass.
+template <typename T, int ITEMS, int KI>
+__global__ void __launch_bounds__(256, ITEMS == 8 ? 3 : 2)
 sscan_fwd_kernel(SsParams p) {
-  constexpr int ITEMS = kItems;
+  static_assert(ITEMS * 32 % kStateStride == 0, "chunk must be a whole number of state strides");
   constexpr int CH = 32 * ITEMS;
+  constexpr int kSavesPerChunk = CH / kStateStride;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
   const int N = p.N, L = p.L;
@@ -334,11 +341,15 @@ sscan_fwd_kernel(SsParams p) {
       }
       const float A_l = lane < N ? p.A[(int64_t)d * N + lane] : 0.f;  // lane n holds A[d, n]
       float* carry_row = scarry + cl * N;
-      // lane 31 ends the chunk = one state stride: it saves the states for the backward
-      float* save = (p.chunk_states != nullptr && lane == 31) ? p.chunk_states + (chan * p.nsaved + k) * N : nullptr;
+      // the lanes that end a state stride (lane 31, and lane 15 with 16 steps per lane) save
+      // the states for the backward
+      constexpr int kLanesPerStride = kStateStride / ITEMS;
+      const int si = k * kSavesPerChunk + (lane + 1) / kLanesPerStride - 1;
+      float* save = (p.chunk_states != nullptr && (lane + 1) % kLanesPerStride == 0 && si < p.nsaved)
+                        ? p.chunk_states + (chan * p.nsaved + si) * N : nullptr;
       int n = 0;
-      for (; n + 2 <= N; n += 2) fwd_states<ITEMS, 2>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
-      if (n < N) fwd_states<ITEMS, 1>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
+      for (; n + KI <= N; n += KI) fwd_states<ITEMS, KI>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
+      for (; n < N; ++n) fwd_states<ITEMS, 1>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
       if (p.z != nullptr) {
         float zz[ITEMS];
         load_items<T, ITEMS>(zz, reinterpret_cast<const T*>(p.z) + chan * L, tl, L, p.vec_io);
@@ -716,13 +727,15 @@ extern "C" int ak_selective_scan_fwd(void* out, float* last_state, float* chunk_
   p.bulk = (((seqlen * es) % 16) == 0 && aligned16(Bm) && aligned16(Cm)) ? 1 : 0;
   p.vec_io = (((seqlen * es) % 16) == 0 && aligned16(u) && aligned16(delta) && aligned16(out) &&
               (z == nullptr || aligned16(z))) ? 1 : 0;
-  constexpr int CH = 32 * kItems;
   const int cpc = p.nw * p.cpw;
   dim3 grid((unsigned)(dim / cpc), (unsigned)batch);
   AK_DISPATCH_DTYPE(dt, T, {
-    const size_t smem = fwd_smem<T, CH>(p.N, cpc);
+    // 16 steps per lane when the 512-step tiles fit in shared memory, else 8
+    const size_t smem16 = fwd_smem<T, 32 * kFwdItems>(p.N, cpc);
+    const bool wide = smem16 <= 227 * 1024;
+    const size_t smem = wide ? smem16 : fwd_smem<T, 32 * kItems>(p.N, cpc);
     AK_REQUIRE(smem <= 227 * 1024, AK_ERR_SHAPE, "selective_scan_fwd: dstate too large for shared memory");
-    auto kern = sscan_fwd_kernel<T>;
+    auto kern = wide ? sscan_fwd_kernel<T, kFwdItems, kFwdInterleave> : sscan_fwd_kernel<T, kItems, 2>;
     AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "selective_scan_fwd: smem attribute");
     kern<<<grid, p.nw * 32, smem, st>>>(p);
