@@ -310,6 +310,72 @@ def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
                       f"of the same sample"}
 
 
+def cpu_ops_sample():
+    """The reference's CPU path for the other rows (restated in `oracle/`, fp32 on the host cores),
+    each on a bounded sample of its BASELINE config; same units as the GPU `ops` lines (GB/s of
+    algorithmic bytes, TFLOP/s for linear+CE), forward + backward per sample."""
+    from oracle import hot_path_oracle as O
+    f32 = torch.float32
+    g = torch.Generator().manual_seed(11)
+    res = {}
+
+    def timed(fn, reps=2):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps
+
+    # RMSNorm fp32 [8192, 768] (full config): fwd + bwd, 125.8 MB algorithmic
+    x = torch.randn(8192, 768, generator=g)
+    w = 1 + 0.02 * torch.randn(768, generator=g)
+    dy = torch.randn(8192, 768, generator=g)
+    t = timed(lambda: (O.rmsnorm_fwd(x, w, dt=f32), O.rmsnorm_bwd(x, w, dy, dt=f32)))
+    res["rmsnorm_fwd_bwd_fp32_8192x768"] = {"GB/s": round(125_838_336 / t / 1e9, 3), "s": round(t, 4),
+                                            "sample": "full config"}
+    # softmax: 2048 of the 196608 rows x 2048 (fp32 math on bf16-valued data), fwd + bwd = 5 row passes
+    sx = (torch.randn(2048, 2048, generator=g) / 8).to(torch.bfloat16).float()
+    sdy = torch.randn(2048, 2048, generator=g)
+    t = timed(lambda: O.softmax_bwd(O.softmax_fwd(sx, dt=f32), sdy, dt=f32))
+    res["softmax_fwd_bwd_bf16_2048x2048_sample"] = {"GB/s": round(5 * 2048 * 2048 * 2 / t / 1e9, 3),
+                                                    "s": round(t, 4), "sample": "2048 of 196608 rows"}
+    # collapsed scan: 1 of 8 batch rows, (1, 2048, 1536) fp32, fwd + bwd = 56 B/elt
+    dA = torch.rand(1, 2048, 1536, generator=g) * 0.5 + 0.5
+    dBx, Cm, xs, gy = (torch.randn(1, 2048, 1536, generator=g) for _ in range(4))
+    Dv = torch.randn(1536, generator=g)
+    t = timed(lambda: O.scan1_bwd(dA, dBx, Cm, Dv, xs, gy, dt=f32), reps=1)
+    res["scan1_fwd_bwd_fp32_1x2048x1536_sample"] = {"GB/s": round(56 * 2048 * 1536 / t / 1e9, 3),
+                                                    "s": round(t, 4), "sample": "batch 1 of 8"}
+    # linear + CE: 512 of the 32768 rows, D 768, V 50304, fp32 GEMMs + CE + autograd (3 * 2NDV FLOP)
+    H = torch.randn(512, 768, generator=g)
+    Wt = torch.randn(50304, 768, generator=g) * 0.02
+    lab = torch.randint(0, 50257, (512,), generator=g)
+    t = timed(lambda: O.linear_ce(H, Wt, lab, dt=f32), reps=1)
+    res["linear_ce_fp32_512x768x50304_sample"] = {"TFLOP/s": round(6 * 512 * 768 * 50304 / t / 1e12, 4),
+                                                  "s": round(t, 4), "sample": "512 of 32768 rows"}
+    # SiLU-gate, fused residual RMSNorm, RoPE, causal conv1d: 1/16 samples of their GPU cases
+    gt, up, gd = (torch.randn(4096, 2048, generator=g) for _ in range(3))
+    t = timed(lambda: (O.silu_gate_mul(gt, up, dt=f32), O.silu_gate_mul_bwd(gt, up, gd, dt=f32)))
+    res["silu_gate_fwd_bwd_4096x2048_sample"] = {"GB/s": round(8 * 4096 * 2048 * 2 / t / 1e9, 3),
+                                                 "s": round(t, 4), "sample": "4096 of 65536 rows"}
+    xr, rr, gh, gn = (torch.randn(4096, 768, generator=g) for _ in range(4))
+    t = timed(lambda: (O.fused_res_rmsnorm(xr, rr, w, dt=f32),
+                       O.fused_res_rmsnorm_bwd(xr + rr, w, gh, gn, dt=f32)))
+    res["fused_res_rmsnorm_fwd_bwd_4096x768_sample"] = {"GB/s": round(8 * 4096 * 768 * 2 / t / 1e9, 3),
+                                                        "s": round(t, 4), "sample": "4096 of 65536 rows"}
+    q = torch.randn(4, 12, 2048, 64, generator=g)
+    ang = torch.outer(torch.arange(2048, dtype=f32), 1.0 / (10000.0 ** (torch.arange(0, 64, 2, dtype=f32) / 64)))
+    t = timed(lambda: (O.rope(q, ang.cos(), ang.sin(), dt=f32), O.rope_bwd(q, ang.cos(), ang.sin(), dt=f32)))
+    res["rope_fwd_bwd_4x12x2048x64_sample"] = {"GB/s": round(4 * q.numel() * 2 / t / 1e9, 3), "s": round(t, 4),
+                                               "sample": "batch 4 of 64"}
+    xc, dc = (torch.randn(1, 1536, 2048, generator=g) for _ in range(2))
+    wc, bc = torch.randn(1536, 4, generator=g), torch.randn(1536, generator=g)
+    t = timed(lambda: O.causal_conv1d_grads(xc, wc, bc, dc, silu=True, dt=f32))
+    res["conv1d_silu_fwd_bwd_1x1536x2048_sample"] = {"GB/s": round(5 * xc.numel() * 2 / t / 1e9, 3),
+                                                     "s": round(t, 4), "sample": "batch 1 of 16"}
+    return {"cores": torch.get_num_threads(), "kind": "port", "ops": res}
+
+
 def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=32768, scale=1):
     """Device-timed throughput of the other swapped ops at their BASELINE configs.
     `which`: subset of {"rmsnorm", "softmax", "linear_ce", "scan1", "ce_rows", "fused_res", "silu_gate", "rope", "conv1d"} (None = all)."""
@@ -621,6 +687,8 @@ def run_ours(args, world, rank, local):
         line["train"] = train
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_sscan_sample()
+        if not args.no_ops:
+            line["cpu_baseline"]["ops"] = cpu_ops_sample()["ops"]
     emit(line)
 
 
