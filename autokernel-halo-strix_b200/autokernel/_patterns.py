@@ -184,7 +184,7 @@ class _SiluGateMulReplacement(nn.Module):
         for a in alias:
             setattr(self, a, getattr(original, a))
         import kernels.hip._torch_ops  # noqa: F401
-        self._op = torch.ops.autokernel.silu_gate_mul
+        self._op = torch.ops.autokernel.silu_gate_mul_nocast  # no fp16 autocast cast of bf16 activations
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         gate_p, down_p, up_p = (getattr(self, a) for a in self._alias)
@@ -303,7 +303,7 @@ class _FusedQKVAttentionReplacement(nn.Module):
         self._freqs = freqs_cis
         self._tables = {}
         import kernels.hip._torch_ops  # noqa: F401
-        self._rope = torch.ops.autokernel.rotary_emb_fp32
+        self._rope = torch.ops.autokernel.rotary_emb  # keeps the activation dtype (fp32 math inside)
 
     def _cos_sin(self, T: int, device, freqs_cis):
         f = freqs_cis if freqs_cis is not None and torch.is_tensor(freqs_cis) and freqs_cis.is_complex() \
@@ -335,8 +335,8 @@ class _FusedQKVAttentionReplacement(nn.Module):
         k = qkv[..., qs:qs + ks].view(B, T, KH, hd).transpose(1, 2)
         v = qkv[..., qs + ks:].view(B, T, KH, hd).transpose(1, 2)
         cos, sin = self._cos_sin(T, x.device, freqs_cis)
-        q = self._rope(q, cos, sin).to(qkv.dtype)
-        k = self._rope(k, cos, sin).to(qkv.dtype)
+        q = self._rope(q, cos, sin)
+        k = self._rope(k, cos, sin)
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=(H != KH))
         return wo(o.transpose(1, 2).reshape(B, T, H * hd))
 

@@ -128,7 +128,8 @@ class MambaBlock(nn.Module):
         self.D = nn.Parameter(torch.ones(self.d_inner))
         self.out_proj = nn.Linear(self.d_inner, d, bias=False)
         self._scan = scan_fn
-        # fused causal conv + SiLU kernel (torch.ops.autokernel.causal_conv1d_silu) when set
+        # kernel path (set by the trainer with use_kernels): fused causal conv + SiLU and the
+        # layout changes through the transpose kernel
         self.fused_conv = False
 
     def reset_dt(self, generator: Optional[torch.Generator] = None):
@@ -141,14 +142,12 @@ class MambaBlock(nn.Module):
             self.dt_proj.bias.copy_(dt + torch.log(-torch.expm1(-dt)))
 
     def forward(self, h):
+        if self.fused_conv:
+            return self._forward_kernels(h)
         B, T, _ = h.shape
         xz = self.in_proj(h).transpose(1, 2)                    # (B, 2*d_inner, T)
         x, z = xz.chunk(2, dim=1)
-        if self.fused_conv:
-            x = torch.ops.autokernel.causal_conv1d_silu(x.contiguous(), self.conv1d.weight.squeeze(1),
-                                                        self.conv1d.bias)
-        else:
-            x = F.silu(self.conv1d(x)[..., :T])
+        x = F.silu(self.conv1d(x)[..., :T])
         x_dbl = self.x_proj(x.transpose(1, 2))                  # (B, T, dt_rank + 2N)
         dt, Bm, Cm = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         dt = (dt @ self.dt_proj.weight.t().to(dt.dtype)).transpose(1, 2)   # (B, d_inner, T), bias in the scan
@@ -158,6 +157,23 @@ class MambaBlock(nn.Module):
                  Cm.transpose(1, 2).contiguous(), self.D.float(), z=z.contiguous(),
                  delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
         return self.out_proj(y.transpose(1, 2))
+
+    def _forward_kernels(self, h):
+        """Same computation with the layout changes done by the tiled transpose kernel
+        (torch.ops.autokernel.split_transpose / transpose_bt) and the fused conv + SiLU."""
+        ops = torch.ops.autokernel
+        di = self.d_inner
+        xz = self.in_proj(h)                                      # (B, T, 2*d_inner)
+        x, z = ops.split_transpose(xz, di)                        # (B, d_inner, T) each
+        x = ops.causal_conv1d_silu(x, self.conv1d.weight.squeeze(1), self.conv1d.bias)
+        x_dbl = self.x_proj(ops.transpose_bt(x))                  # (B, T, dt_rank + 2N)
+        dt, Bm, Cm = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
+        dt = ops.transpose_bt(dt @ self.dt_proj.weight.t().to(dt.dtype))   # (B, d_inner, T)
+        A = -torch.exp(self.A_log.float())
+        scan = self._scan or _default_scan()
+        y = scan(x, dt, A, ops.transpose_bt(Bm), ops.transpose_bt(Cm), self.D.float(), z=z,
+                 delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
+        return self.out_proj(ops.transpose_bt(y))
 
 
 class HybridLayer(nn.Module):

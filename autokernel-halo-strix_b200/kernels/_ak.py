@@ -35,6 +35,7 @@ SIGNATURES = {
     "ak_silu_gate_mul_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rope_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rope_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_transpose": [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_softmax_fwd": [_vp, _vp, _i64, _i64, _i, _vp],
     "ak_softmax_bwd": [_vp, _vp, _vp, _i64, _i64, _i, _vp],
     "ak_ce_rows_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _i, _vp],
@@ -302,6 +303,32 @@ def rope_fwd(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Ten
 
 def rope_bwd(dy: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     return _rope("ak_rope_bwd", dy, cos, sin)
+
+
+# ---------------------------------------------------------------------------
+# Batched last-two-dims transpose
+# ---------------------------------------------------------------------------
+def transpose_into(out: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """out[b, c, r] = x[b, r, c] for 3-D x (B, R, C) and out (B, C, R); both may be strided
+    views as long as their last dimension has unit stride."""
+    dev = require_cuda(x, out)
+    if x.dim() != 3 or out.shape != (x.shape[0], x.shape[2], x.shape[1]) or x.dtype != out.dtype:
+        raise ValueError(f"transpose: x {tuple(x.shape)} -> out {tuple(out.shape)}")
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    if out.stride(-1) != 1:
+        raise ValueError("transpose: out needs unit stride along its last dimension")
+    B, R, C = x.shape
+    if x.numel():
+        call("ak_transpose", ptr(out), ptr(x), B, R, C, x.stride(0), x.stride(1), out.stride(0), out.stride(1),
+             dtype_code(x), stream(dev))
+    return out
+
+
+def transpose_bt(x: torch.Tensor) -> torch.Tensor:
+    """Contiguous x.transpose(-1, -2) of a 3-D tensor (B, R, C) -> (B, C, R)."""
+    out = torch.empty((x.shape[0], x.shape[2], x.shape[1]), dtype=x.dtype, device=x.device)
+    return transpose_into(out, x)
 
 
 # ---------------------------------------------------------------------------

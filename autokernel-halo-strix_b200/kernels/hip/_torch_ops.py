@@ -316,6 +316,21 @@ except AttributeError:  # pragma: no cover - older torch
     pass
 
 
+# Same op without the fp16 autocast rule (added): the module replacements call this one,
+# so bf16 activations under bf16 autocast stay bf16 (no cast copies in and out).
+@torch.library.custom_op("autokernel::silu_gate_mul_nocast", mutates_args=())
+def silu_gate_mul_nocast_op(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    return _ak.silu_gate_mul_fwd(gate, up)
+
+
+@silu_gate_mul_nocast_op.register_fake
+def _(gate, up):
+    return gate.new_empty(gate.shape)
+
+
+silu_gate_mul_nocast_op.register_autograd(_sgm_backward, setup_context=_sgm_setup)
+
+
 @torch.library.custom_op("autokernel::silu_gate_mul_packed_bwd", mutates_args=())
 def silu_gate_mul_packed_bwd_op(gate_up: torch.Tensor, grad: torch.Tensor) -> torch.Tensor:
     H = gate_up.shape[-1] // 2
@@ -395,6 +410,86 @@ try:
     rotary_emb_fp32_op.register_autocast("cuda", torch.float32)
 except AttributeError:  # pragma: no cover - older torch
     pass
+
+
+# Same rotation without the fp32 autocast rule (added; the arithmetic is fp32 in the kernel
+# either way): the fused-QKV replacement keeps q / k in the activation dtype.
+@torch.library.custom_op("autokernel::rotary_emb", mutates_args=())
+def rotary_emb_op(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    return _ak.rope_fwd(x, cos, sin)
+
+
+@rotary_emb_op.register_fake
+def _(x, cos, sin):
+    return x.new_empty(x.shape)
+
+
+rotary_emb_op.register_autograd(_rope_backward, setup_context=_rope_setup)
+
+
+# ---------------------------------------------------------------------------
+# Layout changes of the Mamba block (added): (B, T, D) <-> (B, D, T) through the
+# tiled transpose kernel instead of `.transpose(1, 2).contiguous()`.
+#   transpose_bt(x (B, R, C)) -> (B, C, R) contiguous; its gradient is a transpose.
+#   split_transpose(xz (B, T, Dx + Dz), dx) -> (x (B, Dx, T), z (B, Dz, T)); its
+#   gradient is written straight into the two halves of one (B, T, Dx + Dz) tensor.
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::transpose_bt", mutates_args=())
+def transpose_bt_op(x: torch.Tensor) -> torch.Tensor:
+    return _ak.transpose_bt(x)
+
+
+@transpose_bt_op.register_fake
+def _(x):
+    return x.new_empty((x.shape[0], x.shape[2], x.shape[1]))
+
+
+transpose_bt_op.register_autograd(lambda ctx, g: transpose_bt_op(g.contiguous()),
+                                  setup_context=lambda ctx, inputs, output: None)
+
+
+@torch.library.custom_op("autokernel::split_transpose_bwd", mutates_args=())
+def split_transpose_bwd_op(gx: torch.Tensor, gz: torch.Tensor) -> torch.Tensor:
+    B, Dx, T = gx.shape
+    Dz = gz.shape[1]
+    out = torch.empty((B, T, Dx + Dz), dtype=gx.dtype, device=gx.device)
+    _ak.transpose_into(out[:, :, :Dx], gx.contiguous())
+    _ak.transpose_into(out[:, :, Dx:], gz.contiguous())
+    return out
+
+
+@split_transpose_bwd_op.register_fake
+def _(gx, gz):
+    return gx.new_empty((gx.shape[0], gx.shape[2], gx.shape[1] + gz.shape[1]))
+
+
+@torch.library.custom_op("autokernel::split_transpose", mutates_args=())
+def split_transpose_op(xz: torch.Tensor, dx: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    return _ak.transpose_bt(xz[:, :, :dx]), _ak.transpose_bt(xz[:, :, dx:])
+
+
+@split_transpose_op.register_fake
+def _(xz, dx):
+    B, T, Dt = xz.shape
+    return xz.new_empty((B, dx, T)), xz.new_empty((B, Dt - dx, T))
+
+
+def _split_transpose_backward(ctx, gx, gz):
+    if gx is None:
+        gx = torch.zeros(ctx.shapes[0], dtype=ctx.dtype, device=ctx.device)
+    if gz is None:
+        gz = torch.zeros(ctx.shapes[1], dtype=ctx.dtype, device=ctx.device)
+    return split_transpose_bwd_op(gx, gz), None
+
+
+def _split_transpose_setup(ctx, inputs, output):
+    ctx.shapes = (output[0].shape, output[1].shape)
+    ctx.dtype, ctx.device = output[0].dtype, output[0].device
+
+
+split_transpose_op.register_autograd(_split_transpose_backward, setup_context=_split_transpose_setup)
 
 
 # ---------------------------------------------------------------------------

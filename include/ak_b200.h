@@ -317,6 +317,18 @@ AK_API int ak_rope_bwd(void* dx, const void* dy, const float* cos_t,
                        int64_t D, int64_t stride_b, int64_t stride_h,
                        int64_t stride_n, int dt, void* stream);
 
+/* ---- Batched last-two-dims transpose ---------------------------------------
+ * out[b][c][r] = in[b][r][c] for b < batch, r < R, c < C; element (b, r, c) of
+ * `in` at in + b*in_bstride + r*in_ld + c, element (b, c, r) of `out` at
+ * out + b*out_bstride + c*out_ld + r (strides in elements, unit last stride).
+ * Replaces the `.transpose(1, 2).contiguous()` layout copies between the
+ * (B, T, D) projections and the (B, D, T) conv / scan operands of the Mamba
+ * block (external/mamba/mamba_ssm/modules/mamba_simple.py forward). */
+AK_API int ak_transpose(void* out, const void* in, int64_t batch, int64_t R,
+                        int64_t C, int64_t in_bstride, int64_t in_ld,
+                        int64_t out_bstride, int64_t out_ld, int dt,
+                        void* stream);
+
 /* ---- Depthwise causal conv1d (+ optional SiLU) --------------------------
  * y[b,d,t] = act(bias[d] + sum_k w[d,k] x[b,d,t-K+1+k]), x = 0 before t = 0;
  * act = SiLU when silu != 0, identity otherwise.  x, y: (B, D, T) dt, T
