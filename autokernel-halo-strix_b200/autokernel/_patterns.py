@@ -55,10 +55,17 @@ class _RMSNormReplacement(nn.Module):
         self.eps = float(getattr(original, "eps", 1e-6) or 1e-6)
         import kernels.hip._torch_ops  # noqa: F401  (registers the ops)
         self._op = torch.ops.autokernel.rmsnorm_eps
+        self._op_mixed = torch.ops.autokernel.rmsnorm_mixed
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not x.is_cuda:
             raise RuntimeError("autokernel RMSNorm replacement needs CUDA tensors")
+        if x.dtype == torch.float32 and torch.is_autocast_enabled("cuda"):
+            lo = torch.get_autocast_dtype("cuda")
+            if lo in (torch.bfloat16, torch.float16):
+                # fp32 residual stream under autocast: the output goes straight to a GEMM that
+                # would cast it to `lo`; write it in `lo` (same single rounding, no cast kernels)
+                return self._op_mixed(x, self.weight, self.eps, lo)
         return self._op(x, self.weight, self.eps)
 
 
@@ -132,14 +139,21 @@ class _FusedResidualRMSNormBlockReplacement(nn.Module):
             setattr(self, a, getattr(original, a))
         import kernels.hip._torch_ops  # noqa: F401  (registers the ops)
         self._op = torch.ops.autokernel.fused_res_rmsnorm_eps
+        self._op_mixed = torch.ops.autokernel.fused_res_rmsnorm_mixed
 
     def forward(self, x: torch.Tensor, *args, **kwargs) -> torch.Tensor:
         attn, attn_norm, ffn, ffn_norm = (getattr(self, a) for a in self._alias)
         a = attn(attn_norm(x), *args, **kwargs)
         if not a.is_cuda:
             raise RuntimeError("autokernel fused residual RMSNorm needs CUDA tensors")
-        dt = torch.promote_types(a.dtype, x.dtype)
         eps = float(getattr(ffn_norm, "eps", 1e-6) or 1e-6)
+        if (x.dtype == torch.float32 and a.dtype in (torch.bfloat16, torch.float16)
+                and torch.is_autocast_enabled("cuda")):
+            # fp32 residual stream, 16-bit mixer output: hidden stays fp32, normed comes out in the
+            # mixer's dtype for the FFN's autocast GEMM (no promotion or cast kernels)
+            hidden, normed = self._op_mixed(a, x, ffn_norm.weight, eps)
+            return hidden + ffn(normed)
+        dt = torch.promote_types(a.dtype, x.dtype)
         hidden, normed = self._op(a.to(dt), x.to(dt), ffn_norm.weight, eps)
         return hidden + ffn(normed)
 

@@ -29,9 +29,13 @@ constexpr int kWarps = 8;  // rows in flight per CTA
 // non-null, then normalised).
 // FULL: N == NIT * 32 * VEC, so no lane's vector is out of range and the loads
 // carry no guard (issued back to back).
-template <typename T, typename TW, int VEC, int NIT, bool RES = false, bool FULL = false>
+// TX / TY: types of x and y when they differ from the compute / residual type T
+// (mixed precision: an fp32 residual stream with 16-bit mixer outputs in and a
+// 16-bit normalised output for the next autocast GEMM, rounded once).
+template <typename T, typename TW, int VEC, int NIT, bool RES = false, bool FULL = false, typename TX = T,
+          typename TY = T>
 __global__ void __launch_bounds__(kWarps * 32)
-rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __restrict__ x,
+rmsnorm_fwd_warp(TY* __restrict__ y, float* __restrict__ rstd_out, const TX* __restrict__ x,
                  const TW* __restrict__ w, int64_t M, int N, float eps, const T* __restrict__ res = nullptr,
                  T* __restrict__ h_out = nullptr) {
   const int lane = threadIdx.x & 31;
@@ -48,14 +52,14 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
   }
   const float inv_n = 1.f / (float)N;
   for (int64_t row = (int64_t)blockIdx.x * kWarps + warp; row < M; row += (int64_t)gridDim.x * kWarps) {
-    const T* xr = x + row * N;
+    const TX* xr = x + row * N;
     float xv[NIT][VEC];
     float ss = 0.f;
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
       if (FULL || c < N) {
-        load_frag<T, VEC>(xv[it], xr + c);
+        load_frag<TX, VEC>(xv[it], xr + c);
         if constexpr (RES) {
           float rv[VEC];
           load_frag<T, VEC>(rv, res + row * N + c);
@@ -73,7 +77,7 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
     ss = warp_sum(ss);
     const float r = rsqrtf(ss * inv_n + eps);
     if (rstd_out != nullptr && lane == 0) rstd_out[row] = r;
-    T* yr = y + row * N;
+    TY* yr = y + row * N;
 #pragma unroll
     for (int it = 0; it < NIT; ++it) {
       const int c = (it * 32 + lane) * VEC;
@@ -81,7 +85,7 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
         float o[VEC];
 #pragma unroll
         for (int k = 0; k < VEC; ++k) o[k] = xv[it][k] * r * wr[it][k];
-        store_frag<T, VEC>(yr + c, o);
+        store_frag<TY, VEC>(yr + c, o);
       }
     }
   }
@@ -89,18 +93,18 @@ rmsnorm_fwd_warp(T* __restrict__ y, float* __restrict__ rstd_out, const T* __res
 
 // Forward fallback for rows that do not fit the register path (very wide or
 // unaligned rows): one CTA per row, scalar accesses, two passes (second from L2).
-template <typename T, typename TW, bool RES = false>
+template <typename T, typename TW, bool RES = false, typename TX = T, typename TY = T>
 __global__ void __launch_bounds__(256)
-rmsnorm_fwd_block(T* __restrict__ y, float* __restrict__ rstd_out, const T* __restrict__ x,
+rmsnorm_fwd_block(TY* __restrict__ y, float* __restrict__ rstd_out, const TX* __restrict__ x,
                   const TW* __restrict__ w, int64_t M, int N, float eps, const T* __restrict__ res = nullptr,
                   T* __restrict__ h_out = nullptr) {
   __shared__ float red[32];
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
-    const T* xr = x + row * N;
+    const TX* xr = x + row * N;
     const T* rr = RES ? res + row * N : nullptr;
     float ss = 0.f;
     for (int c = threadIdx.x; c < N; c += blockDim.x) {
-      float v = to_f<T>(xr[c]);
+      float v = to_f<TX>(xr[c]);
       if constexpr (RES) {
         const T h = from_f<T>(v + to_f<T>(rr[c]));
         if (h_out != nullptr) h_out[row * N + c] = h;
@@ -115,11 +119,11 @@ rmsnorm_fwd_block(T* __restrict__ y, float* __restrict__ rstd_out, const T* __re
     for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
     const float r = rsqrtf(tot / (float)N + eps);
     if (rstd_out != nullptr && threadIdx.x == 0) rstd_out[row] = r;
-    T* yr = y + row * N;
+    TY* yr = y + row * N;
     for (int c = threadIdx.x; c < N; c += blockDim.x) {
-      float v = to_f<T>(xr[c]);
+      float v = to_f<TX>(xr[c]);
       if constexpr (RES) v = to_f<T>(from_f<T>(v + to_f<T>(rr[c])));
-      yr[c] = from_f<T>(v * r * to_f<TW>(w[c]));
+      yr[c] = from_f<TY>(v * r * to_f<TW>(w[c]));
     }
     __syncthreads();
   }
@@ -141,11 +145,14 @@ __device__ __forceinline__ int bwd_slot(int c) {
   return (it * VEC + k) * 32 + lane;
 }
 
-template <typename T, typename TW, int VEC, int NIT, bool RES = false, bool FULL = false>
+// TG: type of dy when it differs from T (mixed precision: 16-bit gradient of a
+// 16-bit normalised output).  dx2 (nullable, type TG): a second copy of dx, the
+// gradient of a 16-bit fused-residual input.
+template <typename T, typename TW, int VEC, int NIT, bool RES = false, bool FULL = false, typename TG = T>
 __global__ void __launch_bounds__(kWarps * 32, (NIT * VEC <= 24) ? 3 : 2)
-rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __restrict__ dy,
+rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const TG* __restrict__ dy,
                  const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps,
-                 const T* __restrict__ gh = nullptr) {
+                 const T* __restrict__ gh = nullptr, TG* __restrict__ dx2 = nullptr) {
   constexpr int kSlots = NIT * VEC * 32;
   extern __shared__ float s_dw[];  // [kWarps][kSlots] accumulators, then [kSlots] weights
   float* s_w = s_dw + (size_t)kWarps * kSlots;
@@ -169,7 +176,7 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
       const int c = (it * 32 + lane) * VEC;
       if (FULL || c < N) {
         load_frag<T, VEC>(xv[it], x + row * N + c);
-        load_frag<T, VEC>(gv[it], dy + row * N + c);
+        load_frag<TG, VEC>(gv[it], dy + row * N + c);
       } else {
 #pragma unroll
         for (int k = 0; k < VEC; ++k) { xv[it][k] = 0.f; gv[it][k] = 0.f; }
@@ -208,6 +215,7 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
           }
         }
         store_frag<T, VEC>(dx + row * N + c, o);
+        if (dx2 != nullptr) store_frag<TG, VEC>(dx2 + row * N + c, o);
       }
     }
   }
@@ -225,20 +233,20 @@ rmsnorm_bwd_warp(T* __restrict__ dx, float* __restrict__ dw_part, const T* __res
 
 // Backward fallback (wide / unaligned rows): one CTA per row at a time, the
 // CTA owns partial row blockIdx.x of the workspace exclusively.
-template <typename T, typename TW, bool RES = false>
+template <typename T, typename TW, bool RES = false, typename TG = T>
 __global__ void __launch_bounds__(256)
-rmsnorm_bwd_block(T* __restrict__ dx, float* __restrict__ dw_part, const T* __restrict__ dy,
+rmsnorm_bwd_block(T* __restrict__ dx, float* __restrict__ dw_part, const TG* __restrict__ dy,
                   const T* __restrict__ x, const TW* __restrict__ w, int64_t M, int N, float eps,
-                  const T* __restrict__ gh = nullptr) {
+                  const T* __restrict__ gh = nullptr, TG* __restrict__ dx2 = nullptr) {
   __shared__ float red1[32], red2[32];
   float* part = dw_part + (int64_t)blockIdx.x * N;
   for (int c = threadIdx.x; c < N; c += blockDim.x) part[c] = 0.f;
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const T* xr = x + row * N;
-    const T* gr = dy + row * N;
+    const TG* gr = dy + row * N;
     float s1 = 0.f, s2 = 0.f;
     for (int c = threadIdx.x; c < N; c += blockDim.x) {
-      const float xv = to_f<T>(xr[c]), gv = to_f<T>(gr[c]);
+      const float xv = to_f<T>(xr[c]), gv = to_f<TG>(gr[c]);
       s1 = fmaf(xv, xv, s1);
       s2 = fmaf(gv * to_f<TW>(w[c]), xv, s2);
     }
@@ -251,12 +259,13 @@ rmsnorm_bwd_block(T* __restrict__ dx, float* __restrict__ dw_part, const T* __re
     const float r = rsqrtf(t1 / (float)N + eps);
     const float c3 = r * r * r * t2 / (float)N;
     for (int c = threadIdx.x; c < N; c += blockDim.x) {
-      const float xv = to_f<T>(xr[c]), gv = to_f<T>(gr[c]);
+      const float xv = to_f<T>(xr[c]), gv = to_f<TG>(gr[c]);
       float o = r * gv * to_f<TW>(w[c]) - xv * c3;
       if constexpr (RES) {
         if (gh != nullptr) o += to_f<T>(gh[row * N + c]);
       }
       dx[row * N + c] = from_f<T>(o);
+      if (dx2 != nullptr) dx2[row * N + c] = from_f<TG>(o);
       part[c] = fmaf(gv, xv * r, part[c]);
     }
     __syncthreads();
@@ -349,7 +358,8 @@ int bwd_grid(int64_t M, int N) {
   return (int)g;
 }
 
-template <typename T, typename TW, bool RES = false>
+// TX / TY: input / output types when they differ from T (mixed precision).
+template <typename T, typename TW, bool RES = false, typename TX = T, typename TY = T>
 int fwd_impl(void* y, float* rstd, const void* x, const void* w, int64_t M, int N, float eps,
              cudaStream_t st, const void* res = nullptr, void* h_out = nullptr) {
   RmsPlan p = plan<T, TW>(M, N, x, y, w);
@@ -361,29 +371,31 @@ int fwd_impl(void* y, float* rstd, const void* x, const void* w, int64_t M, int 
     if (g > cap) g = cap;
     if (N == p.nit * 32 * VEC) {
       AK_NIT_SWITCH(p.nit, NIT,
-                    rmsnorm_fwd_warp<T, TW, VEC, NIT, RES, true><<<(unsigned)g, kWarps * 32, 0, st>>>(
-                        (T*)y, rstd, (const T*)x, (const TW*)w, M, N, eps, (const T*)res, (T*)h_out));
+                    rmsnorm_fwd_warp<T, TW, VEC, NIT, RES, true, TX, TY><<<(unsigned)g, kWarps * 32, 0, st>>>(
+                        (TY*)y, rstd, (const TX*)x, (const TW*)w, M, N, eps, (const T*)res, (T*)h_out));
     } else {
       AK_NIT_SWITCH(p.nit, NIT,
-                    rmsnorm_fwd_warp<T, TW, VEC, NIT, RES><<<(unsigned)g, kWarps * 32, 0, st>>>(
-                        (T*)y, rstd, (const T*)x, (const TW*)w, M, N, eps, (const T*)res, (T*)h_out));
+                    rmsnorm_fwd_warp<T, TW, VEC, NIT, RES, false, TX, TY><<<(unsigned)g, kWarps * 32, 0, st>>>(
+                        (TY*)y, rstd, (const TX*)x, (const TW*)w, M, N, eps, (const T*)res, (T*)h_out));
     }
   } else {
     int64_t g = M;
     const int64_t cap = (int64_t)sm_count() * 8;
     if (g > cap) g = cap;
-    rmsnorm_fwd_block<T, TW, RES><<<(unsigned)g, 256, 0, st>>>((T*)y, rstd, (const T*)x, (const TW*)w, M, N,
-                                                               eps, (const T*)res, (T*)h_out);
+    rmsnorm_fwd_block<T, TW, RES, TX, TY><<<(unsigned)g, 256, 0, st>>>((TY*)y, rstd, (const TX*)x, (const TW*)w,
+                                                                       M, N, eps, (const T*)res, (T*)h_out);
   }
   AK_CHECK_LAUNCH("ak_rmsnorm_fwd");
   return AK_OK;
 }
 
-template <typename T, typename TW, bool RES = false>
+// TG: type of dy (and of the optional second output dx2) when it differs from T.
+template <typename T, typename TW, bool RES = false, typename TG = T>
 int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const void* x, const void* w,
-             int64_t M, int N, float eps, cudaStream_t st, const void* gh = nullptr) {
+             int64_t M, int N, float eps, cudaStream_t st, const void* gh = nullptr, void* dx2 = nullptr) {
   RmsPlan p = plan<T, TW>(M, N, x, dx, w);
   if (!aligned16(dy)) p.warp_path = false;
+  if (dx2 != nullptr && !aligned16(dx2)) p.warp_path = false;
   if (RES && gh != nullptr && !aligned16(gh)) p.warp_path = false;
   // x and dy live in registers (w and the dw accumulators in shared memory):
   // beyond 32 elements per lane the register path spills, so wider rows take
@@ -395,18 +407,19 @@ int bwd_impl(void* dx, void* dw, int dt_dw, float* ws, const void* dy, const voi
     if (p.warp_path) {
       const bool full = N == p.nit * 32 * VEC;
       AK_NIT_SWITCH(p.nit, NIT, if constexpr (NIT * VEC <= 32) {
-        auto kern = full ? rmsnorm_bwd_warp<T, TW, VEC, NIT, RES, true> : rmsnorm_bwd_warp<T, TW, VEC, NIT, RES>;
+        auto kern = full ? rmsnorm_bwd_warp<T, TW, VEC, NIT, RES, true, TG>
+                         : rmsnorm_bwd_warp<T, TW, VEC, NIT, RES, false, TG>;
         const size_t smem = (size_t)(kWarps + 1) * NIT * VEC * 32 * sizeof(float);
         if (smem > 48 * 1024)
           AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                       "ak_rmsnorm_bwd: smem attribute");
         G = resident_grid(kern, smem, G);
-        kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps,
-                                           (const T*)gh);
+        kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const TG*)dy, (const T*)x, (const TW*)w, M, N, eps,
+                                           (const T*)gh, (TG*)dx2);
       });
     } else {
-      rmsnorm_bwd_block<T, TW, RES><<<G, 256, 0, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N,
-                                                       eps, (const T*)gh);
+      rmsnorm_bwd_block<T, TW, RES, TG><<<G, 256, 0, st>>>((T*)dx, ws, (const TG*)dy, (const T*)x, (const TW*)w,
+                                                           M, N, eps, (const T*)gh, (TG*)dx2);
     }
     AK_CHECK_LAUNCH("ak_rmsnorm_bwd");
   }
@@ -502,6 +515,71 @@ extern "C" int ak_fused_res_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* wor
   return AK_OK;
 }
 
+// ---- Mixed precision (fp32 residual stream, 16-bit autocast activations) ----
+// Dispatch over the 16-bit edge type TL (bf16 / fp16) and the weight type with an
+// fp32 compute / residual type.
+#define AK_DISPATCH_MIXED(dt_lo, dt_w, ...)                                                              \
+  do {                                                                                                    \
+    if (dt_lo == AK_BF16 && dt_w == AK_F32) { using TL = __nv_bfloat16; using TW = float; __VA_ARGS__; }   \
+    else if (dt_lo == AK_F16 && dt_w == AK_F32) { using TL = __half; using TW = float; __VA_ARGS__; }      \
+    else if (dt_lo == AK_BF16 && dt_w == AK_BF16) { using TL = __nv_bfloat16; using TW = __nv_bfloat16; __VA_ARGS__; } \
+    else if (dt_lo == AK_F16 && dt_w == AK_F16) { using TL = __half; using TW = __half; __VA_ARGS__; }     \
+    else { set_error("rmsnorm mixed: unsupported dtypes lo=%d w=%d", dt_lo, dt_w); return AK_ERR_DTYPE; } \
+  } while (0)
+
+extern "C" int ak_rmsnorm_fwd_mixed(void* y, int dt_y, const void* x, int dt_x, const void* w, int dt_w, int64_t M,
+                                    int64_t N, float eps, void* stream) {
+  clear_error();
+  AK_REQUIRE(M >= 0 && N > 0 && N <= (1 << 24), AK_ERR_SHAPE, "ak_rmsnorm_fwd_mixed: bad shape");
+  if (M == 0) return AK_OK;
+  AK_REQUIRE(y && x && w, AK_ERR_ARG, "ak_rmsnorm_fwd_mixed: null pointer");
+  if (dt_y == dt_x) return ak_rmsnorm_fwd(y, nullptr, x, w, M, N, eps, dt_x, dt_w, stream);
+  AK_REQUIRE(dt_x == AK_F32, AK_ERR_DTYPE, "ak_rmsnorm_fwd_mixed: x must be fp32 when y differs");
+  AK_DISPATCH_MIXED(dt_y, dt_w,
+                    return fwd_impl<float, TW, false, float, TL>(y, nullptr, x, w, M, (int)N, eps,
+                                                                 (cudaStream_t)stream));
+  return AK_OK;
+}
+
+extern "C" int ak_fused_res_rmsnorm_fwd_mixed(void* hidden, void* normed, int dt_normed, const void* x, int dt_x,
+                                              const void* residual, int dt_res, const void* w, int dt_w, int64_t M,
+                                              int64_t N, float eps, void* stream) {
+  clear_error();
+  AK_REQUIRE(M >= 0 && N > 0 && N <= (1 << 24), AK_ERR_SHAPE, "ak_fused_res_rmsnorm_fwd_mixed: bad shape");
+  if (M == 0) return AK_OK;
+  AK_REQUIRE(normed && x && residual && w, AK_ERR_ARG, "ak_fused_res_rmsnorm_fwd_mixed: null pointer");
+  if (dt_x == dt_res && dt_normed == dt_res)
+    return ak_fused_res_rmsnorm_fwd(hidden, normed, x, residual, w, M, N, eps, dt_x, dt_w, stream);
+  AK_REQUIRE(dt_res == AK_F32 && dt_x == dt_normed, AK_ERR_DTYPE,
+             "ak_fused_res_rmsnorm_fwd_mixed: residual / hidden fp32, x and normed of one 16-bit type");
+  AK_DISPATCH_MIXED(dt_x, dt_w,
+                    return fwd_impl<float, TW, true, TL, TL>(normed, nullptr, x, w, M, (int)N, eps,
+                                                             (cudaStream_t)stream, residual, hidden));
+  return AK_OK;
+}
+
+extern "C" int ak_rmsnorm_bwd_mixed(void* dx, void* dx2, void* dw, int dt_dw, void* workspace, size_t ws_bytes,
+                                    const void* grad_hidden, const void* dy, int dt_dy, const void* x, int dt_x,
+                                    const void* w, int dt_w, int64_t M, int64_t N, float eps, void* stream) {
+  clear_error();
+  AK_REQUIRE(M >= 0 && N > 0 && N <= (1 << 24), AK_ERR_SHAPE, "ak_rmsnorm_bwd_mixed: bad shape");
+  AK_REQUIRE(dw && w, AK_ERR_ARG, "ak_rmsnorm_bwd_mixed: null pointer");
+  AK_REQUIRE(M == 0 || (dx && dy && x), AK_ERR_ARG, "ak_rmsnorm_bwd_mixed: null pointer");
+  const size_t need = (size_t)bwd_grid(M, (int)N) * (size_t)N * sizeof(float);
+  AK_REQUIRE(M == 0 || (workspace && ws_bytes >= need), AK_ERR_WORKSPACE,
+             "ak_rmsnorm_bwd_mixed: workspace %zu < %zu bytes", ws_bytes, need);
+  AK_REQUIRE(dt_x == AK_F32 && dt_dy != AK_F32, AK_ERR_DTYPE,
+             "ak_rmsnorm_bwd_mixed: x fp32 with a 16-bit dy (equal dtypes: ak_rmsnorm_bwd / ak_fused_res_rmsnorm_bwd)");
+  AK_DISPATCH_MIXED(dt_dy, dt_w, {
+    if (grad_hidden != nullptr)
+      return bwd_impl<float, TW, true, TL>(dx, dw, dt_dw, (float*)workspace, dy, x, w, M, (int)N, eps,
+                                           (cudaStream_t)stream, grad_hidden, dx2);
+    return bwd_impl<float, TW, false, TL>(dx, dw, dt_dw, (float*)workspace, dy, x, w, M, (int)N, eps,
+                                          (cudaStream_t)stream, nullptr, dx2);
+  });
+  return AK_OK;
+}
+
 // ============================================================================
 // RMSNorm backward that allocates nothing (no counterpart in the reference).
 //
@@ -558,7 +636,7 @@ int bwd_noalloc_impl(void* dx, void* dw, int dt_dw, float* ws, int G, const void
                       "ak_rmsnorm_bwd_noalloc: smem attribute");
         G = resident_grid(kern, smem, G);
         kern<<<G, kWarps * 32, smem, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps,
-                                           nullptr);
+                                           nullptr, nullptr);
       });
     } else {
       rmsnorm_bwd_block<T, TW><<<G, 256, 0, st>>>((T*)dx, ws, (const T*)dy, (const T*)x, (const TW*)w, M, N, eps);

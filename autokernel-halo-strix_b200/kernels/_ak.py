@@ -36,6 +36,9 @@ SIGNATURES = {
     "ak_rope_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rope_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_transpose": [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_rmsnorm_fwd_mixed": [_vp, _i, _vp, _i, _vp, _i, _i64, _i64, _f, _vp],
+    "ak_fused_res_rmsnorm_fwd_mixed": [_vp, _vp, _i, _vp, _i, _vp, _i, _vp, _i, _i64, _i64, _f, _vp],
+    "ak_rmsnorm_bwd_mixed": [_vp, _vp, _vp, _i, _vp, _sz, _vp, _vp, _i, _vp, _i, _vp, _i, _i64, _i64, _f, _vp],
     "ak_softmax_fwd": [_vp, _vp, _i64, _i64, _i, _vp],
     "ak_softmax_bwd": [_vp, _vp, _vp, _i64, _i64, _i, _vp],
     "ak_ce_rows_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _i64, _f, _f, _vp, _i, _vp],
@@ -210,6 +213,52 @@ def fused_res_rmsnorm_bwd(hidden: torch.Tensor, w: torch.Tensor, grad_hidden: Op
     call("ak_fused_res_rmsnorm_bwd", ptr(dx), ptr(dw), _DT[dw_dtype], ptr(ws), ws_bytes, ptr(gh), ptr(gn),
          ptr(hidden), ptr(w), M, N, float(eps), dtype_code(hidden), dtype_code(w), stream(dev))
     return dx, dw
+
+
+# ---------------------------------------------------------------------------
+# Mixed-precision RMSNorm: fp32 residual stream, 16-bit autocast activations
+# ---------------------------------------------------------------------------
+def rmsnorm_fwd_mixed(x: torch.Tensor, w: torch.Tensor, eps: float, out_dtype: torch.dtype) -> torch.Tensor:
+    """y = rmsnorm(x fp32) * w written in `out_dtype` (one rounding)."""
+    dev = require_cuda(x, w)
+    x, w = x.contiguous(), w.contiguous()
+    N = x.shape[-1]
+    M = x.numel() // N if N else 0
+    y = torch.empty(x.shape, dtype=out_dtype, device=dev)
+    call("ak_rmsnorm_fwd_mixed", ptr(y), _DT[out_dtype], ptr(x), dtype_code(x), ptr(w), dtype_code(w), M, N,
+         float(eps), stream(dev))
+    return y
+
+
+def fused_res_rmsnorm_fwd_mixed(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float):
+    """hidden (residual's dtype, fp32) = x (16-bit) + residual; normed (x's dtype) = rmsnorm(hidden) * w."""
+    dev = require_cuda(x, residual, w)
+    x, residual, w = x.contiguous(), residual.contiguous(), w.contiguous()
+    N = x.shape[-1]
+    M = x.numel() // N if N else 0
+    hidden = torch.empty(x.shape, dtype=residual.dtype, device=dev)
+    normed = torch.empty_like(x)
+    call("ak_fused_res_rmsnorm_fwd_mixed", ptr(hidden), ptr(normed), dtype_code(normed), ptr(x), dtype_code(x),
+         ptr(residual), dtype_code(residual), ptr(w), dtype_code(w), M, N, float(eps), stream(dev))
+    return hidden, normed
+
+
+def rmsnorm_bwd_mixed(x: torch.Tensor, w: torch.Tensor, dy: torch.Tensor, eps: float,
+                      grad_hidden: Optional[torch.Tensor] = None, want_lo: bool = False):
+    """x fp32, dy 16-bit.  Returns (dx fp32, dx in dy's dtype or None, dw fp32)."""
+    dev = require_cuda(x, w, dy, grad_hidden)
+    x, w, dy = x.contiguous(), w.contiguous(), dy.contiguous()
+    gh = grad_hidden.to(x.dtype).contiguous() if grad_hidden is not None else None
+    N = x.shape[-1]
+    M = x.numel() // N if N else 0
+    dx = torch.empty_like(x)
+    dx2 = torch.empty_like(dy) if want_lo else None
+    dw = torch.empty(N, dtype=torch.float32, device=dev)
+    ws_bytes = _size_query("ak_rmsnorm_bwd_workspace_size", M, N)
+    ws = workspace(ws_bytes, dev)
+    call("ak_rmsnorm_bwd_mixed", ptr(dx), ptr(dx2), ptr(dw), F32, ptr(ws), ws_bytes, ptr(gh), ptr(dy),
+         dtype_code(dy), ptr(x), dtype_code(x), ptr(w), dtype_code(w), M, N, float(eps), stream(dev))
+    return dx, dx2, dw
 
 
 # ---------------------------------------------------------------------------

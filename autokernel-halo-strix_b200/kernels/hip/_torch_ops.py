@@ -428,6 +428,93 @@ rotary_emb_op.register_autograd(_rope_backward, setup_context=_rope_setup)
 
 
 # ---------------------------------------------------------------------------
+# Mixed-precision RMSNorm (added): an fp32 residual stream under bf16/fp16
+# autocast.  The normalised output is written in the autocast dtype (the value
+# the next GEMM's autocast cast would produce, rounded once) and the 16-bit
+# gradient is consumed directly, so no cast kernels run in either direction.
+#   rmsnorm_mixed(x fp32, weight, eps, out_dtype) -> y (out_dtype)
+#   fused_res_rmsnorm_mixed(x 16-bit, residual fp32, weight, eps)
+#       -> (hidden fp32, normed 16-bit); grads (dx 16-bit, d residual fp32, dw)
+# ---------------------------------------------------------------------------
+
+
+@torch.library.custom_op("autokernel::rmsnorm_mixed_bwd", mutates_args=())
+def rmsnorm_mixed_bwd_op(x: torch.Tensor, weight: torch.Tensor, grad: torch.Tensor,
+                         eps: float) -> List[torch.Tensor]:
+    dx, _, dw = _ak.rmsnorm_bwd_mixed(x, weight, grad, eps)
+    return [dx, dw.to(weight.dtype)]
+
+
+@rmsnorm_mixed_bwd_op.register_fake
+def _(x, weight, grad, eps):
+    return [torch.empty_like(x), torch.empty_like(weight)]
+
+
+@torch.library.custom_op("autokernel::rmsnorm_mixed", mutates_args=())
+def rmsnorm_mixed_op(x: torch.Tensor, weight: torch.Tensor, eps: float, out_dtype: torch.dtype) -> torch.Tensor:
+    return _ak.rmsnorm_fwd_mixed(x, weight, eps, out_dtype)
+
+
+@rmsnorm_mixed_op.register_fake
+def _(x, weight, eps, out_dtype):
+    return x.new_empty(x.shape, dtype=out_dtype)
+
+
+def _rmsnorm_mixed_setup(ctx, inputs, output):
+    ctx.save_for_backward(inputs[0], inputs[1])
+    ctx.eps = inputs[2]
+
+
+def _rmsnorm_mixed_backward(ctx, grad):
+    x, w = ctx.saved_tensors
+    dx, dw = rmsnorm_mixed_bwd_op(x, w, grad.contiguous(), ctx.eps)
+    return dx, dw, None, None
+
+
+rmsnorm_mixed_op.register_autograd(_rmsnorm_mixed_backward, setup_context=_rmsnorm_mixed_setup)
+
+
+@torch.library.custom_op("autokernel::fused_res_rmsnorm_mixed_bwd", mutates_args=())
+def fused_res_rmsnorm_mixed_bwd_op(hidden: torch.Tensor, weight: torch.Tensor, grad_hidden: Optional[torch.Tensor],
+                                   grad_normed: torch.Tensor, eps: float) -> List[torch.Tensor]:
+    dres, dx, dw = _ak.rmsnorm_bwd_mixed(hidden, weight, grad_normed, eps, grad_hidden=grad_hidden, want_lo=True)
+    return [dx, dres, dw.to(weight.dtype)]
+
+
+@fused_res_rmsnorm_mixed_bwd_op.register_fake
+def _(hidden, weight, grad_hidden, grad_normed, eps):
+    return [torch.empty_like(grad_normed), torch.empty_like(hidden), torch.empty_like(weight)]
+
+
+@torch.library.custom_op("autokernel::fused_res_rmsnorm_mixed", mutates_args=())
+def fused_res_rmsnorm_mixed_op(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                               eps: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    return _ak.fused_res_rmsnorm_fwd_mixed(x, residual, weight, eps)
+
+
+@fused_res_rmsnorm_mixed_op.register_fake
+def _(x, residual, weight, eps):
+    return residual.new_empty(residual.shape), x.new_empty(x.shape)
+
+
+def _res_mixed_setup(ctx, inputs, output):
+    ctx.save_for_backward(output[0], inputs[2])
+    ctx.eps = inputs[3]
+    ctx.lo_dtype = inputs[0].dtype
+
+
+def _res_mixed_backward(ctx, grad_hidden, grad_normed):
+    hidden, weight = ctx.saved_tensors
+    if grad_normed is None:
+        grad_normed = torch.zeros(hidden.shape, dtype=ctx.lo_dtype, device=hidden.device)
+    dx, dres, dw = fused_res_rmsnorm_mixed_bwd_op(hidden, weight, grad_hidden, grad_normed.contiguous(), ctx.eps)
+    return dx, dres, dw, None
+
+
+fused_res_rmsnorm_mixed_op.register_autograd(_res_mixed_backward, setup_context=_res_mixed_setup)
+
+
+# ---------------------------------------------------------------------------
 # Layout changes of the Mamba block (added): (B, T, D) <-> (B, D, T) through the
 # tiled transpose kernel instead of `.transpose(1, 2).contiguous()`.
 #   transpose_bt(x (B, R, C)) -> (B, C, R) contiguous; its gradient is a transpose.

@@ -329,6 +329,32 @@ AK_API int ak_transpose(void* out, const void* in, int64_t batch, int64_t R,
                         int64_t out_bstride, int64_t out_ld, int dt,
                         void* stream);
 
+/* ---- Mixed-precision RMSNorm (fp32 residual stream, 16-bit activations) ----
+ * No reference counterpart: under bf16/fp16 autocast the reference computes the
+ * norm in fp32 and the next GEMM casts its output; these entries write the
+ * 16-bit output directly (the same single rounding) and take 16-bit gradients.
+ * Mixed combinations: compute / residual fp32, the 16-bit side bf16 or fp16,
+ * w fp32 or of the 16-bit type.  Equal dtypes route to the plain entries.
+ *
+ * ak_rmsnorm_fwd_mixed: y (dt_y) = rmsnorm(x fp32) * w.
+ * ak_fused_res_rmsnorm_fwd_mixed: hidden (fp32) = x (16-bit) + residual (fp32);
+ *   normed (16-bit, = dt_x) = rmsnorm(hidden) * w.
+ * ak_rmsnorm_bwd_mixed: x fp32 (the normalised input / hidden), dy 16-bit:
+ *   dx (fp32) = [grad_hidden fp32, nullable] + rmsnorm backward; dx2 (16-bit,
+ *   nullable) = dx rounded (the gradient of a 16-bit fused-residual input);
+ *   dw (dt_dw).  Workspace: ak_rmsnorm_bwd_workspace_size(M, N). */
+AK_API int ak_rmsnorm_fwd_mixed(void* y, int dt_y, const void* x, int dt_x,
+                                const void* w, int dt_w, int64_t M, int64_t N,
+                                float eps, void* stream);
+AK_API int ak_fused_res_rmsnorm_fwd_mixed(void* hidden, void* normed, int dt_normed,
+                                          const void* x, int dt_x, const void* residual,
+                                          int dt_res, const void* w, int dt_w,
+                                          int64_t M, int64_t N, float eps, void* stream);
+AK_API int ak_rmsnorm_bwd_mixed(void* dx, void* dx2, void* dw, int dt_dw, void* workspace,
+                                size_t ws_bytes, const void* grad_hidden, const void* dy,
+                                int dt_dy, const void* x, int dt_x, const void* w, int dt_w,
+                                int64_t M, int64_t N, float eps, void* stream);
+
 /* ---- Depthwise causal conv1d (+ optional SiLU) --------------------------
  * y[b,d,t] = act(bias[d] + sum_k w[d,k] x[b,d,t-K+1+k]), x = 0 before t = 0;
  * act = SiLU when silu != 0, identity otherwise.  x, y: (B, D, T) dt, T

@@ -145,3 +145,50 @@ def test_fused_residual_pattern_matches_eager(autocast):
     assert set(outs[1][2]) == set(outs[0][2])
     for n, g in outs[0][2].items():
         torch.testing.assert_close(outs[1][2][n].float(), g.float(), **tol, msg=n)
+
+
+@pytest.mark.parametrize("lo", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N", [(4096, 768), (37, 1000), (3, 64)])
+def test_mixed_precision_rmsnorm_equals_fp32_kernel_rounded(lo, M, N):
+    """fp32 residual stream, 16-bit edges: the mixed kernels do the fp32 kernels' arithmetic and
+    round once at the 16-bit outputs, so they match them exactly."""
+    from kernels import _ak
+    g = torch.Generator().manual_seed(M + N)
+    x = torch.randn(M, N, generator=g).to(DEV)
+    w = (1 + 0.1 * torch.randn(N, generator=g)).to(DEV)
+    a = torch.randn(M, N, generator=g).to(lo).to(DEV)
+    gn = torch.randn(M, N, generator=g).to(lo).to(DEV)
+    gh = torch.randn(M, N, generator=g).to(DEV)
+    # plain norm
+    y = _ak.rmsnorm_fwd_mixed(x, w, 1e-6, lo)
+    assert y.dtype == lo and torch.equal(y, _ak.rmsnorm_fwd(x, w, 1e-6).to(lo))
+    dx, _, dw = _ak.rmsnorm_bwd_mixed(x, w, gn, 1e-6)
+    rdx, rdw = _ak.rmsnorm_bwd(x, w, gn.float(), 1e-6)
+    assert torch.equal(dx, rdx) and torch.equal(dw, rdw)
+    # fused residual
+    h, n = _ak.fused_res_rmsnorm_fwd_mixed(a, x, w, 1e-6)
+    rh, rn = _ak.fused_res_rmsnorm_fwd(a.float(), x, w, 1e-6)
+    assert h.dtype == torch.float32 and n.dtype == lo
+    assert torch.equal(h, rh) and torch.equal(n, rn.to(lo))
+    dres, dlo, dw2 = _ak.rmsnorm_bwd_mixed(h, w, gn, 1e-6, grad_hidden=gh, want_lo=True)
+    rdx2, rdw2 = _ak.fused_res_rmsnorm_bwd(rh, w, gh, gn.float(), 1e-6)
+    assert torch.equal(dres, rdx2) and torch.equal(dlo, rdx2.to(lo)) and torch.equal(dw2, rdw2)
+
+
+def test_mixed_precision_ops_autograd():
+    import kernels.hip._torch_ops  # noqa: F401
+    x = torch.randn(256, 768, device=DEV, requires_grad=True)
+    a = torch.randn(256, 768, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    w = torch.ones(768, device=DEV, requires_grad=True)
+    h, n = torch.ops.autokernel.fused_res_rmsnorm_mixed(a, x, w, 1e-6)
+    y = torch.ops.autokernel.rmsnorm_mixed(h, w, 1e-6, torch.bfloat16)
+    (h.sum() + n.float().square().sum() + y.float().sum()).backward()
+    xr, ar, wr = (t.detach().clone().float().requires_grad_(True) for t in (x, a, w))
+    hr = ar + xr
+    def nrm(t):
+        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
+    (hr.sum() + nrm(hr).square().sum() + nrm(hr).sum()).backward()
+    torch.testing.assert_close(x.grad, xr.grad, atol=5e-2, rtol=2e-2)
+    torch.testing.assert_close(a.grad.float(), ar.grad, atol=5e-2, rtol=2e-2)
+    assert a.grad.dtype == torch.bfloat16 and x.grad.dtype == torch.float32
+    torch.testing.assert_close(w.grad, wr.grad, atol=5e-1, rtol=2e-2)
