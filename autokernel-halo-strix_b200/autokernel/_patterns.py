@@ -295,8 +295,9 @@ class _FusedQKVAttentionReplacement(nn.Module):
     forward(x, freqs_cis=None): qkv = x [Wq; Wk; Wv]^T in one GEMM (the
     concatenation is taken from the original Parameters each call, so state
     dict, optimizer state and gradients stay on them); q and k are rotated
-    straight out of the packed qkv rows by `torch.ops.autokernel.rotary_emb_fp32`
-    (strided read, dense head-major write: no transpose copies); then
+    straight out of the packed qkv rows, and v copied, by one strided RoPE pass
+    into a token-major buffer (`qkv_rope_split`: no transpose copies, and the
+    backward writes one packed d(qkv) with no slice fills or adds); then
     scaled_dot_product_attention(is_causal=True, enable_gqa) and the output
     projection.  RoPE tables: the complex `freqs_cis` argument or model buffer
     (reference :216-361), else cos / sin of the module's `rope_theta`
@@ -317,7 +318,8 @@ class _FusedQKVAttentionReplacement(nn.Module):
         self._freqs = freqs_cis
         self._tables = {}
         import kernels.hip._torch_ops  # noqa: F401
-        self._rope = torch.ops.autokernel.rotary_emb  # keeps the activation dtype (fp32 math inside)
+        from kernels.hip._torch_ops import qkv_rope_split
+        self._split = qkv_rope_split  # rotated q, k and v as views of one token-major buffer
 
     def _cos_sin(self, T: int, device, freqs_cis):
         f = freqs_cis if freqs_cis is not None and torch.is_tensor(freqs_cis) and freqs_cis.is_complex() \
@@ -344,13 +346,8 @@ class _FusedQKVAttentionReplacement(nn.Module):
         if wq.bias is not None or wk.bias is not None or wv.bias is not None:
             b = torch.cat([p.bias if p.bias is not None else p.weight.new_zeros(p.out_features) for p in (wq, wk, wv)])
         qkv = F.linear(x, w, b)
-        qs, ks = H * hd, KH * hd
-        q = qkv[..., :qs].view(B, T, H, hd).transpose(1, 2)
-        k = qkv[..., qs:qs + ks].view(B, T, KH, hd).transpose(1, 2)
-        v = qkv[..., qs + ks:].view(B, T, KH, hd).transpose(1, 2)
         cos, sin = self._cos_sin(T, x.device, freqs_cis)
-        q = self._rope(q, cos, sin)
-        k = self._rope(k, cos, sin)
+        q, k, v = self._split(qkv, cos, sin, H, KH)
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=(H != KH))
         return wo(o.transpose(1, 2).reshape(B, T, H * hd))
 

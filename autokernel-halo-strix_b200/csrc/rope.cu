@@ -8,11 +8,14 @@
 // The backward is the rotation by -theta on the same pairs (sign = -1):
 //   dx[2i] = g[2i] c + g[2i+1] s,   dx[2i+1] = -g[2i] s + g[2i+1] c.
 //
-// Layout: x is read through arbitrary (b, h, n) element strides with unit
-// stride along D, so q / k can be read straight out of a fused (B, N, W) QKV
-// projection; y is written dense (B, H, N, D).  The head-major transpose that
-// attention wants costs nothing extra.  One thread rotates one 16-byte vector
-// position (8 elements of a 16-bit type, 4 of fp32) in several (b, h) planes.
+// Layout: x is read and y written through arbitrary (b, h, n) element strides
+// with unit stride along D.  ak_rope_fwd / ak_rope_bwd write y dense
+// (B, H, N, D), so q / k are read straight out of a fused (B, N, W) QKV
+// projection and leave head-major; ak_rope_strided also takes y's strides, so
+// the gradients of q, k and v are written straight into their columns of one
+// packed (B, N, W) gradient (mode 0 copies without rotating, for v).  One
+// thread rotates one 16-byte vector position (8 elements of a 16-bit type, 4
+// of fp32) in several (b, h) planes.
 #include "ak_common.cuh"
 
 namespace ak {
@@ -26,10 +29,12 @@ constexpr int kPlanesPerCta = 8;  // (b, h) planes one thread walks with the sam
 // plane, loads its cos / sin once and applies them to kPlanesPerCta planes
 // (grid.y): per plane only an address step, one load, the rotation and one
 // store.  grid.x covers the N*D/VEC vector positions.
-template <typename T, int VEC, bool FULL>
+// ROT false: plain strided copy (no tables read).
+template <typename T, int VEC, bool FULL, bool ROT = true>
 __global__ void __launch_bounds__(kThreadsR, 6)
 rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
-            int64_t planes, int H, int N, int D, int64_t sb, int64_t sh, int64_t sn_, float sign, bool tab4) {
+            int64_t planes, int H, int N, int D, int64_t sb, int64_t sh, int64_t sn_, int64_t yb, int64_t yh,
+            int64_t yn, float sign, bool tab4) {
   const int vpr = D / VEC;
   const int per_plane = N * vpr;
   const int half = D / 2;
@@ -38,9 +43,12 @@ rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict_
   const int n = idx / vpr;
   const int jb = (idx - n * vpr) * VEC;
   float c[VEC / 2], s[VEC / 2];
-  const float* cr = cs + (int64_t)n * half + jb / 2;
-  const float* sr = sn + (int64_t)n * half + jb / 2;
-  if constexpr (VEC / 2 == 4) {
+  const float* cr = ROT ? cs + (int64_t)n * half + jb / 2 : nullptr;
+  const float* sr = ROT ? sn + (int64_t)n * half + jb / 2 : nullptr;
+  if constexpr (!ROT) {
+#pragma unroll
+    for (int k = 0; k < VEC / 2; ++k) { c[k] = 1.f; s[k] = 0.f; }
+  } else if constexpr (VEC / 2 == 4) {
     if (tab4) {
       const float4 c4 = __ldg(reinterpret_cast<const float4*>(cr));
       const float4 s4 = __ldg(reinterpret_cast<const float4*>(sr));
@@ -56,21 +64,25 @@ rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict_
   }
 #pragma unroll
   for (int k = 0; k < VEC / 2; ++k) s[k] *= sign;
-  const int64_t xo = (int64_t)n * sn_ + jb, yo = (int64_t)n * D + jb, ystep = (int64_t)N * D;
+  const int64_t xo = (int64_t)n * sn_ + jb, yo = (int64_t)n * yn + jb;
   const int64_t p0 = (int64_t)blockIdx.y * kPlanesPerCta;
   const int64_t p1 = p0 + kPlanesPerCta < planes ? p0 + kPlanesPerCta : planes;
   int64_t b = p0 / H;
   int h = (int)(p0 - b * H);
 #pragma unroll 2
   for (int64_t p = p0; p < p1; ++p) {
-    float v[VEC], o[VEC];
-    load_frag<T, VEC>(v, x + b * sb + h * sh + xo);
+    if constexpr (ROT) {
+      float v[VEC], o[VEC];
+      load_frag<T, VEC>(v, x + b * sb + h * sh + xo);
 #pragma unroll
-    for (int k = 0; k < VEC / 2; ++k) {
-      o[2 * k] = v[2 * k] * c[k] - v[2 * k + 1] * s[k];
-      o[2 * k + 1] = v[2 * k] * s[k] + v[2 * k + 1] * c[k];
+      for (int k = 0; k < VEC / 2; ++k) {
+        o[2 * k] = v[2 * k] * c[k] - v[2 * k + 1] * s[k];
+        o[2 * k + 1] = v[2 * k] * s[k] + v[2 * k + 1] * c[k];
+      }
+      store_frag<T, VEC>(y + b * yb + h * yh + yo, o);
+    } else {
+      *reinterpret_cast<int4*>(y + b * yb + h * yh + yo) = *reinterpret_cast<const int4*>(x + b * sb + h * sh + xo);
     }
-    store_frag<T, VEC>(y + p * ystep + yo, o);
     if (++h == H) { h = 0; ++b; }
   }
 }
@@ -80,7 +92,7 @@ template <typename T>
 __global__ void __launch_bounds__(kThreadsR)
 rope_pair_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict__ cs,
                  const float* __restrict__ sn, int64_t rows, int H, int N, int D, int64_t sb, int64_t sh,
-                 int64_t sn_, float sign) {
+                 int64_t sn_, int64_t yb, int64_t yh, int64_t yn, float sign, bool rot) {
   const int half = D / 2;
   const int64_t total = rows * half;
   for (int64_t t = (int64_t)blockIdx.x * kThreadsR + threadIdx.x; t < total; t += (int64_t)gridDim.x * kThreadsR) {
@@ -92,26 +104,30 @@ rope_pair_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __rest
     const int64_t b = bh / H;
     const T* xr = x + b * sb + h * sh + (int64_t)n * sn_;
     const float x0 = to_f<T>(xr[2 * i]), x1 = to_f<T>(xr[2 * i + 1]);
-    const float c = cs[(int64_t)n * half + i], s = sign * sn[(int64_t)n * half + i];
-    y[row * D + 2 * i] = from_f<T>(x0 * c - x1 * s);
-    y[row * D + 2 * i + 1] = from_f<T>(x0 * s + x1 * c);
+    const float c = rot ? cs[(int64_t)n * half + i] : 1.f, s = rot ? sign * sn[(int64_t)n * half + i] : 0.f;
+    T* yr = y + b * yb + h * yh + (int64_t)n * yn;
+    yr[2 * i] = from_f<T>(x0 * c - x1 * s);
+    yr[2 * i + 1] = from_f<T>(x0 * s + x1 * c);
   }
 }
 
+// sign: +1 rotate by theta, -1 by -theta, 0 copy.  y strides (yb, yh, yn); unit stride along D.
 int rope_impl(void* y, const void* x, const float* cos_t, const float* sin_t, int64_t B, int64_t H, int64_t N,
-              int64_t D, int64_t sb, int64_t sh, int64_t sn, float sign, int dt, cudaStream_t st, const char* who) {
+              int64_t D, int64_t sb, int64_t sh, int64_t sn, int64_t yb, int64_t yh, int64_t yn, float sign, int dt,
+              cudaStream_t st, const char* who) {
   AK_REQUIRE(B >= 0 && H > 0 && N > 0 && D > 0 && D % 2 == 0 && H < (1LL << 31) && N < (1LL << 31) &&
                  D < (1LL << 31),
              AK_ERR_SHAPE, "%s: bad shape B=%lld H=%lld N=%lld D=%lld (D must be even)", who, (long long)B,
              (long long)H, (long long)N, (long long)D);
   if (B == 0) return AK_OK;
-  AK_REQUIRE(y && x && cos_t && sin_t, AK_ERR_ARG, "%s: null pointer", who);
+  const bool rot = sign != 0.f;
+  AK_REQUIRE(y && x && (!rot || (cos_t && sin_t)), AK_ERR_ARG, "%s: null pointer", who);
   const int64_t rows = B * H * N;
   const int es = elem_size(dt);
   const int vecw = 16 / es;
   const bool vec_ok = D % vecw == 0 && aligned16(x) && aligned16(y) && (sb * es) % 16 == 0 && (sh * es) % 16 == 0 &&
-                      (sn * es) % 16 == 0;
-  const bool tab4 = aligned16(cos_t) && aligned16(sin_t) && (D / 2) % 4 == 0;
+                      (sn * es) % 16 == 0 && (yb * es) % 16 == 0 && (yh * es) % 16 == 0 && (yn * es) % 16 == 0;
+  const bool tab4 = rot && aligned16(cos_t) && aligned16(sin_t) && (D / 2) % 4 == 0;
   AK_REQUIRE(!vec_ok || N * (D / vecw) < (1LL << 31), AK_ERR_SHAPE, "%s: N*D too large", who);
   AK_REQUIRE(!vec_ok || (B * H + kPlanesPerCta - 1) / kPlanesPerCta < 65536, AK_ERR_SHAPE,
              "%s: more than %d (b, h) planes", who, 65535 * kPlanesPerCta);
@@ -122,19 +138,19 @@ int rope_impl(void* y, const void* x, const float* cos_t, const float* sin_t, in
       const unsigned gx = (unsigned)((per_plane + kThreadsR - 1) / kThreadsR);
       const int64_t planes = B * H;
       const unsigned gy = (unsigned)((planes + kPlanesPerCta - 1) / kPlanesPerCta);
-      if (per_plane % kThreadsR == 0)
-        rope_kernel<T, VEC, true><<<dim3(gx, gy), kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes,
-                                                                     (int)H, (int)N, (int)D, sb, sh, sn, sign, tab4);
-      else
-        rope_kernel<T, VEC, false><<<dim3(gx, gy), kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes,
-                                                                      (int)H, (int)N, (int)D, sb, sh, sn, sign, tab4);
+      const dim3 grid(gx, gy);
+      const bool full = per_plane % kThreadsR == 0;
+      auto kern = rot ? (full ? rope_kernel<T, VEC, true, true> : rope_kernel<T, VEC, false, true>)
+                      : (full ? rope_kernel<T, VEC, true, false> : rope_kernel<T, VEC, false, false>);
+      kern<<<grid, kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes, (int)H, (int)N, (int)D, sb, sh, sn,
+                                       yb, yh, yn, sign, tab4);
     } else {
       int64_t g = (rows * (D / 2) + kThreadsR - 1) / kThreadsR;
       const int64_t cap = (int64_t)sm_count() * 32;
       if (g > cap) g = cap;
       if (g < 1) g = 1;
       rope_pair_kernel<T><<<(unsigned)g, kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, rows, (int)H, (int)N,
-                                                            (int)D, sb, sh, sn, sign);
+                                                            (int)D, sb, sh, sn, yb, yh, yn, sign, rot);
     }
   });
   AK_CHECK_LAUNCH(who);
@@ -150,14 +166,24 @@ extern "C" int ak_rope_fwd(void* y, const void* x, const float* cos_t, const flo
                            int64_t N, int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_n, int dt,
                            void* stream) {
   clear_error();
-  return rope_impl(y, x, cos_t, sin_t, B, H, N, D, stride_b, stride_h, stride_n, 1.f, dt, (cudaStream_t)stream,
-                   "ak_rope_fwd");
+  return rope_impl(y, x, cos_t, sin_t, B, H, N, D, stride_b, stride_h, stride_n, H * N * D, N * D, D, 1.f, dt,
+                   (cudaStream_t)stream, "ak_rope_fwd");
 }
 
 extern "C" int ak_rope_bwd(void* dx, const void* dy, const float* cos_t, const float* sin_t, int64_t B, int64_t H,
                            int64_t N, int64_t D, int64_t stride_b, int64_t stride_h, int64_t stride_n, int dt,
                            void* stream) {
   clear_error();
-  return rope_impl(dx, dy, cos_t, sin_t, B, H, N, D, stride_b, stride_h, stride_n, -1.f, dt, (cudaStream_t)stream,
-                   "ak_rope_bwd");
+  return rope_impl(dx, dy, cos_t, sin_t, B, H, N, D, stride_b, stride_h, stride_n, H * N * D, N * D, D, -1.f, dt,
+                   (cudaStream_t)stream, "ak_rope_bwd");
+}
+
+extern "C" int ak_rope_strided(void* y, const void* x, const float* cos_t, const float* sin_t, int64_t B, int64_t H,
+                               int64_t N, int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_sn, int64_t y_sb,
+                               int64_t y_sh, int64_t y_sn, int mode, int dt, void* stream) {
+  clear_error();
+  AK_REQUIRE(mode == 1 || mode == -1 || mode == 0, AK_ERR_ARG, "ak_rope_strided: mode must be 1, -1 or 0, got %d",
+             mode);
+  return rope_impl(y, x, cos_t, sin_t, B, H, N, D, x_sb, x_sh, x_sn, y_sb, y_sh, y_sn, (float)mode, dt,
+                   (cudaStream_t)stream, "ak_rope_strided");
 }

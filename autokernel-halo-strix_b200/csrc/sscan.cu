@@ -91,9 +91,12 @@ __device__ __forceinline__ float softplus_t(float x) {
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + __expf(-x)); }
 
 // Load ITEMS consecutive elements starting at position t of a length-L row.
+// Vector width: 16 bytes, or the lane's whole run when that is shorter (then the run
+// start t * sizeof(T) is a multiple of ITEMS * sizeof(T), the access size).
 template <typename T, int ITEMS>
 __device__ __forceinline__ void load_items(float (&v)[ITEMS], const T* row, int t, int L, bool vec) {
-  constexpr int VEC = 16 / sizeof(T);
+  constexpr int VEC = ITEMS * sizeof(T) >= 16 ? 16 / sizeof(T) : ITEMS;
+  static_assert(ITEMS % VEC == 0, "ITEMS must be a multiple of the vector width");
   if (vec && t + ITEMS <= L) {
 #pragma unroll
     for (int i = 0; i < ITEMS; i += VEC) {
@@ -110,7 +113,8 @@ __device__ __forceinline__ void load_items(float (&v)[ITEMS], const T* row, int 
 
 template <typename T, int ITEMS>
 __device__ __forceinline__ void store_items(T* row, const float (&v)[ITEMS], int t, int L, bool vec) {
-  constexpr int VEC = 16 / sizeof(T);
+  constexpr int VEC = ITEMS * sizeof(T) >= 16 ? 16 / sizeof(T) : ITEMS;
+  static_assert(ITEMS % VEC == 0, "ITEMS must be a multiple of the vector width");
   if (vec && t + ITEMS <= L) {
 #pragma unroll
     for (int i = 0; i < ITEMS; i += VEC) {

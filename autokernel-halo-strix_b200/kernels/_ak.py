@@ -35,6 +35,7 @@ SIGNATURES = {
     "ak_silu_gate_mul_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rope_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rope_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_rope_strided": [_vp, _vp, _vp, _vp] + [_i64] * 10 + [_i, _i, _vp],
     "ak_transpose": [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rmsnorm_fwd_mixed": [_vp, _i, _vp, _i, _vp, _i, _i64, _i64, _f, _vp],
     "ak_fused_res_rmsnorm_fwd_mixed": [_vp, _vp, _i, _vp, _i, _vp, _i, _vp, _i, _i64, _i64, _f, _vp],
@@ -352,6 +353,29 @@ def rope_fwd(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Ten
 
 def rope_bwd(dy: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     return _rope("ak_rope_bwd", dy, cos, sin)
+
+
+def rope_into(y: torch.Tensor, x: torch.Tensor, cos, sin, mode: int) -> torch.Tensor:
+    """y <- rotation of x (mode 1), its inverse (mode -1) or a copy (mode 0); x and y are
+    (B, H, N, D) views with any strides and unit stride along D (e.g. head slices of packed
+    (B, N, W) projections or gradients).  cos / sin: (N, D/2) fp32, unused for mode 0."""
+    dev = require_cuda(x, y)
+    if x.dim() != 4 or y.shape != x.shape or y.dtype != x.dtype:
+        raise ValueError(f"rope_into: x {tuple(x.shape)} {x.dtype} -> y {tuple(y.shape)} {y.dtype}")
+    if y.stride(-1) != 1:
+        raise ValueError("rope_into: y needs unit stride along D")
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    B, H, N, D = x.shape
+    if mode not in (1, -1, 0):
+        raise ValueError(f"rope_into: mode must be 1, -1 or 0, got {mode}")
+    c = s = None
+    if mode != 0:
+        c, s = _rope_tables(cos, N, D), _rope_tables(sin, N, D)
+    if x.numel():
+        call("ak_rope_strided", ptr(y), ptr(x), ptr(c), ptr(s), B, H, N, D, x.stride(0), x.stride(1), x.stride(2), y.stride(0),
+             y.stride(1), y.stride(2), mode, dtype_code(x), stream(dev))
+    return y
 
 
 # ---------------------------------------------------------------------------

@@ -427,6 +427,56 @@ def _(x, cos, sin):
 rotary_emb_op.register_autograd(_rope_backward, setup_context=_rope_setup)
 
 
+# Packed QKV split with RoPE (added).  q, k and v come out as (B, heads, T, hd)
+# views of one token-major (B, T, W) buffer: q and k rotated (one launch over
+# the H + KH heads), v copied.  The backward writes RoPE^-1(dq), RoPE^-1(dk) and
+# dv straight into their columns of one packed d(qkv) (three strided launches),
+# where autograd of slice views would zero-fill a full-width gradient per slice
+# and add them up.
+def _head_view(t: torch.Tensor, off: int, nh: int, hd: int) -> torch.Tensor:
+    B, T, _ = t.shape
+    return t[..., off:off + nh * hd].view(B, T, nh, hd).transpose(1, 2)
+
+
+class _QKVRopeSplit(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, cos, sin, n_heads: int, n_kv_heads: int, head_dim: int):
+        B, T, W = qkv.shape
+        H, KH, hd = n_heads, n_kv_heads, head_dim
+        if W != (H + 2 * KH) * hd:
+            raise ValueError(f"qkv_rope_split: width {W} != (H + 2 KH) hd = {(H + 2 * KH) * hd}")
+        buf = torch.empty_like(qkv, memory_format=torch.contiguous_format)
+        _ak.rope_into(_head_view(buf, 0, H + KH, hd), _head_view(qkv, 0, H + KH, hd), cos, sin, 1)
+        _ak.rope_into(_head_view(buf, (H + KH) * hd, KH, hd), _head_view(qkv, (H + KH) * hd, KH, hd), None,
+                      None, 0)
+        ctx.save_for_backward(cos, sin)
+        ctx.dims = (H, KH, hd)
+        return (_head_view(buf, 0, H, hd), _head_view(buf, H * hd, KH, hd),
+                _head_view(buf, (H + KH) * hd, KH, hd))
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        cos, sin = ctx.saved_tensors
+        H, KH, hd = ctx.dims
+        g = next(t for t in (dq, dk, dv) if t is not None)
+        B, T = g.shape[0], g.shape[2]
+        dqkv = torch.empty((B, T, (H + 2 * KH) * hd), dtype=g.dtype, device=g.device)
+        for grad, off, nh, mode in ((dq, 0, H, -1), (dk, H * hd, KH, -1), (dv, (H + KH) * hd, KH, 0)):
+            dst = _head_view(dqkv, off, nh, hd)
+            if grad is None:
+                dst.zero_()
+            else:
+                _ak.rope_into(dst, grad.to(dqkv.dtype), cos, sin, mode)
+        return dqkv, None, None, None, None, None
+
+
+def qkv_rope_split(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, n_heads: int, n_kv_heads: int):
+    """(B, T, (H + 2 KH) hd) packed projection -> rotated q (B, H, T, hd), rotated k and v
+    (B, KH, T, hd), all views of one token-major buffer."""
+    hd = qkv.shape[-1] // (n_heads + 2 * n_kv_heads)
+    return _QKVRopeSplit.apply(qkv, cos, sin, n_heads, n_kv_heads, hd)
+
+
 # ---------------------------------------------------------------------------
 # Mixed-precision RMSNorm (added): an fp32 residual stream under bf16/fp16
 # autocast.  The normalised output is written in the autocast dtype (the value

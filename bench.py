@@ -425,12 +425,18 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         fl = res.pop("_flush")["ms"]
         timeit(lambda: (flush.zero_(), _ak.rmsnorm_fwd(x, w, 1e-6)), fw_b, "rmsnorm_fwd_fp32_8192x768", steps * 4)
         timeit(lambda: (flush.zero_(), _ak.rmsnorm_bwd(x, w, dy, 1e-6)), bw_b, "rmsnorm_bwd_fp32_8192x768", steps * 4)
+        # size ceiling: a plain torch copy of one such tensor (25 MB in, 25 MB out) under the same protocol
+        ycp = torch.empty_like(x)
+        timeit(lambda: (flush.zero_(), ycp.copy_(x)), 2 * E * 4, "_copy32", steps * 4)
+        cp32 = 2 * E * 4 / max(res.pop("_copy32")["ms"] - fl, 1e-6) / 1e6 / hbm_peak
         for k, nb in (("rmsnorm_fwd_fp32_8192x768", fw_b), ("rmsnorm_bwd_fp32_8192x768", bw_b)):
             ms = max(res[k]["ms"] - fl, 1e-6)
             gbs = nb / ms / 1e6
             res[k] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
-                      "note": "L2 flushed (256 MB write) before each rep; flush time subtracted"}
-        del x, dy, flush
+                      "copy_ceiling_frac": round(cp32, 3),
+                      "note": "L2 flushed (256 MB write) before each rep; flush time subtracted; "
+                              "copy_ceiling_frac = a plain 25 MB -> 25 MB copy under the same protocol"}
+        del x, dy, ycp, flush
         # bf16 at the training shape [16384, 768] (16 x 1024 tokens per GPU): 25 MB per tensor, same flush
         xb = torch.randn(16384, 768, generator=g).to(torch.bfloat16).to(dev)
         wb = (1 + 0.02 * torch.randn(768, generator=g)).to(torch.bfloat16).to(dev)
@@ -441,11 +447,17 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         timeit(lambda: (flush.zero_(), _ak.rmsnorm_fwd(xb, wb, 1e-6)), fwb, "rmsnorm_fwd_bf16_16384x768", steps * 4)
         timeit(lambda: (flush.zero_(), _ak.rmsnorm_bwd(xb, wb, dyb, 1e-6)), bwb, "rmsnorm_bwd_bf16_16384x768",
                steps * 4)
+        ycp = torch.empty_like(xb)
+        timeit(lambda: (flush.zero_(), ycp.copy_(xb)), 2 * Eb * 2, "_copy16", steps * 4)
+        cp16 = 2 * Eb * 2 / max(res.pop("_copy16")["ms"] - fl, 1e-6) / 1e6 / hbm_peak
+        del ycp
         for k, nb in (("rmsnorm_fwd_bf16_16384x768", fwb), ("rmsnorm_bwd_bf16_16384x768", bwb)):
             ms = max(res[k]["ms"] - fl, 1e-6)
             gbs = nb / ms / 1e6
             res[k] = {"ms": round(ms, 4), "GB/s": round(gbs, 1), "frac": round(gbs / hbm_peak, 3),
-                      "note": "L2 flushed (256 MB write) before each rep; flush time subtracted"}
+                      "copy_ceiling_frac": round(cp16, 3),
+                      "note": "L2 flushed (256 MB write) before each rep; flush time subtracted; "
+                              "copy_ceiling_frac = a plain 25 MB -> 25 MB copy under the same protocol"}
         del xb, dyb, flush
 
     if want("softmax"):

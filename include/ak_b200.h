@@ -317,6 +317,19 @@ AK_API int ak_rope_bwd(void* dx, const void* dy, const float* cos_t,
                        int64_t D, int64_t stride_b, int64_t stride_h,
                        int64_t stride_n, int dt, void* stream);
 
+/* Strided form of both: x element (b, h, n, d) at x + b*x_sb + h*x_sh + n*x_sn + d,
+ * y element at y + b*y_sb + h*y_sh + n*y_sn + d.  mode 1 = ak_rope_fwd's rotation,
+ * -1 = ak_rope_bwd's, 0 = plain copy (cos_t / sin_t may be NULL).  Used for the
+ * gradient of a fused QKV projection: dq and dk are rotated back and dv copied
+ * straight into their columns of one packed (B, N, W) gradient, the work the
+ * reference's autograd does with separate slice, fill and add kernels around
+ * autokernel::rotary_emb_fp32 (kernels/hip/_torch_ops.py:117-162). */
+AK_API int ak_rope_strided(void* y, const void* x, const float* cos_t,
+                           const float* sin_t, int64_t B, int64_t H, int64_t N,
+                           int64_t D, int64_t x_sb, int64_t x_sh, int64_t x_sn,
+                           int64_t y_sb, int64_t y_sh, int64_t y_sn, int mode,
+                           int dt, void* stream);
+
 /* ---- Batched last-two-dims transpose ---------------------------------------
  * out[b][c][r] = in[b][r][c] for b < batch, r < R, c < C; element (b, r, c) of
  * `in` at in + b*in_bstride + r*in_ld + c, element (b, c, r) of `out` at

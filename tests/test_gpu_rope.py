@@ -111,3 +111,53 @@ def test_fused_qkv_pattern_matches_eager(autocast):
     assert set(outs[1][2]) == set(outs[0][2])
     for n, g in outs[0][2].items():
         torch.testing.assert_close(outs[1][2][n].float(), g.float(), **tol, msg=n)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("D", [64, 6])  # vector path and the pair path
+def test_rope_strided_modes(dtype, D):
+    """ak_rope_strided: strided input and output, rotate / inverse / copy, bit-exact against
+    the dense kernels (same fp32 arithmetic) and untouched bytes outside the written slice."""
+    from kernels import _ak
+    B, H, N = 2, 3, 40
+    c, s = (t.to(DEV) for t in tables(N, D))
+    src = torch.randn(B, N, 5 * H * D, device=DEV).to(dtype)
+    x = src[..., H * D:2 * H * D].view(B, N, H, D).transpose(1, 2)
+    for mode, ref in ((1, _ak.rope_fwd(x, c, s)), (-1, _ak.rope_bwd(x, c, s)), (0, x.contiguous())):
+        dst = torch.full((B, N, 3 * H * D), 7.0, device=DEV).to(dtype)
+        y = dst[..., H * D:2 * H * D].view(B, N, H, D).transpose(1, 2)
+        _ak.rope_into(y, x, c, s, mode)
+        assert torch.equal(y, ref), mode
+        assert torch.all(dst[..., :H * D] == 7) and torch.all(dst[..., 2 * H * D:] == 7)
+    with pytest.raises(ValueError):
+        _ak.rope_into(y, x, c, s, 2)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_qkv_rope_split_matches_separate_ops(dtype):
+    """qkv_rope_split: forward equals rope of the q / k slices and the v slice; backward
+    equals the gradient of that composition (bit-exact: the same kernels and arithmetic), in one
+    packed d(qkv)."""
+    from kernels import _ak
+    from kernels.hip._torch_ops import qkv_rope_split
+    B, T, H, KH, hd = 2, 96, 12, 4, 64
+    c, s = (t.to(DEV) for t in tables(T, hd))
+    qkv = torch.randn(B, T, (H + 2 * KH) * hd, device=DEV).to(dtype).requires_grad_(True)
+    q, k, v = qkv_rope_split(qkv, c, s, H, KH)
+    assert q.shape == (B, H, T, hd) and k.shape == (B, KH, T, hd) and v.shape == (B, KH, T, hd)
+    qs, ks = H * hd, KH * hd
+    raw = qkv.detach()
+    assert torch.equal(q, _ak.rope_fwd(raw[..., :qs].view(B, T, H, hd).transpose(1, 2), c, s))
+    assert torch.equal(k, _ak.rope_fwd(raw[..., qs:qs + ks].view(B, T, KH, hd).transpose(1, 2), c, s))
+    assert torch.equal(v, raw[..., qs + ks:].view(B, T, KH, hd).transpose(1, 2))
+    gq, gk, gv = (torch.randn_like(t) for t in (q, k, v))
+    torch.autograd.backward((q, k, v), (gq, gk, gv))
+    want = torch.cat([_ak.rope_bwd(gq, c, s).transpose(1, 2).reshape(B, T, qs),
+                      _ak.rope_bwd(gk, c, s).transpose(1, 2).reshape(B, T, ks),
+                      gv.transpose(1, 2).reshape(B, T, ks)], dim=-1)
+    assert torch.equal(qkv.grad, want)
+    # only q used: the k and v columns of the gradient are zero
+    qkv.grad = None
+    q, k, v = qkv_rope_split(qkv, c, s, H, KH)
+    q.backward(gq)
+    assert torch.equal(qkv.grad[..., :qs], want[..., :qs]) and torch.all(qkv.grad[..., qs:] == 0)
