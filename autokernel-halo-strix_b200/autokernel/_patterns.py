@@ -14,7 +14,7 @@
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import List
+from typing import List, NamedTuple
 
 import torch
 import torch.nn as nn
@@ -38,6 +38,46 @@ class Pattern:
 _RMSNORM_CLASS_NAMES = {"RMSNorm", "LlamaRMSNorm", "MistralRMSNorm", "Qwen2RMSNorm", "T5LayerNorm"}
 
 
+class ResidualPair(NamedTuple):
+    """Residual stream value base + delta, not yet added.
+
+    Passed between chained pre-norm blocks (`chain_residual_blocks`): the next
+    consumer's RMSNorm adds and normalises in one fused pass
+    (`autokernel::fused_res_rmsnorm_mixed`), so the add never runs as its own
+    kernel and its backward needs no gradient-accumulation add either.
+    base: fp32 residual stream; delta: 16-bit block output (autocast).
+    """
+    base: torch.Tensor
+    delta: torch.Tensor
+
+    def materialize(self) -> torch.Tensor:
+        return self.base + self.delta
+
+
+def _pair_fusable(pair: ResidualPair) -> bool:
+    return (pair.base.dtype == torch.float32 and pair.delta.dtype in (torch.bfloat16, torch.float16)
+            and pair.base.is_cuda and torch.is_autocast_enabled("cuda"))
+
+
+def _norm_weight_eps(norm: nn.Module):
+    w = getattr(norm, "weight", None)
+    if not isinstance(w, torch.Tensor):
+        return None, None
+    return w, float(getattr(norm, "eps", 1e-6) or 1e-6)
+
+
+def _add_and_norm(pair: ResidualPair, norm: nn.Module):
+    """(x, norm(x)) for x = pair.base + pair.delta: one fused kernel when the pair is an fp32
+    stream plus a 16-bit delta under autocast and `norm` is an RMSNorm, else the add and the
+    module."""
+    w, eps = _norm_weight_eps(norm)
+    if w is not None and _pair_fusable(pair) and isinstance(norm, (_RMSNormReplacement,)):
+        import kernels.hip._torch_ops  # noqa: F401
+        return torch.ops.autokernel.fused_res_rmsnorm_mixed(pair.delta, pair.base, w, eps)
+    x = pair.materialize()
+    return x, norm(x)
+
+
 class _RMSNormReplacement(nn.Module):
     """Replacement for an RMSNorm module.
 
@@ -58,6 +98,8 @@ class _RMSNormReplacement(nn.Module):
         self._op_mixed = torch.ops.autokernel.rmsnorm_mixed
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if isinstance(x, ResidualPair):  # the end of a residual chain: add + norm in one pass
+            return _add_and_norm(x, self)[1]
         if not x.is_cuda:
             raise RuntimeError("autokernel RMSNorm replacement needs CUDA tensors")
         if x.dtype == torch.float32 and torch.is_autocast_enabled("cuda"):
@@ -141,9 +183,16 @@ class _FusedResidualRMSNormBlockReplacement(nn.Module):
         self._op = torch.ops.autokernel.fused_res_rmsnorm_eps
         self._op_mixed = torch.ops.autokernel.fused_res_rmsnorm_mixed
 
-    def forward(self, x: torch.Tensor, *args, **kwargs) -> torch.Tensor:
+    # set by chain_residual_blocks: return ResidualPair(hidden, ffn_out) instead of the sum
+    _emit_pair = False
+
+    def forward(self, x, *args, **kwargs):
         attn, attn_norm, ffn, ffn_norm = (getattr(self, a) for a in self._alias)
-        a = attn(attn_norm(x), *args, **kwargs)
+        if isinstance(x, ResidualPair):  # previous block's output, not yet added
+            x, h = _add_and_norm(x, attn_norm)
+            a = attn(h, *args, **kwargs)
+        else:
+            a = attn(attn_norm(x), *args, **kwargs)
         if not a.is_cuda:
             raise RuntimeError("autokernel fused residual RMSNorm needs CUDA tensors")
         eps = float(getattr(ffn_norm, "eps", 1e-6) or 1e-6)
@@ -152,10 +201,13 @@ class _FusedResidualRMSNormBlockReplacement(nn.Module):
             # fp32 residual stream, 16-bit mixer output: hidden stays fp32, normed comes out in the
             # mixer's dtype for the FFN's autocast GEMM (no promotion or cast kernels)
             hidden, normed = self._op_mixed(a, x, ffn_norm.weight, eps)
-            return hidden + ffn(normed)
-        dt = torch.promote_types(a.dtype, x.dtype)
-        hidden, normed = self._op(a.to(dt), x.to(dt), ffn_norm.weight, eps)
-        return hidden + ffn(normed)
+        else:
+            dt = torch.promote_types(a.dtype, x.dtype)
+            hidden, normed = self._op(a.to(dt), x.to(dt), ffn_norm.weight, eps)
+        f = ffn(normed)
+        if self._emit_pair:
+            return ResidualPair(hidden, f)
+        return hidden + f
 
 
 class FusedResidualRMSNormPattern(Pattern):
@@ -364,6 +416,28 @@ class FusedQKVPattern(Pattern):
 
     def apply(self, name: str, module: nn.Module, model: nn.Module) -> nn.Module:
         return _FusedQKVAttentionReplacement(module, _find_qkv_attrs(module), _find_complex_freqs(model))
+
+
+def chain_residual_blocks(model: nn.Module) -> int:
+    """Chain the residual stream through consecutive fused pre-norm blocks.
+
+    Opt-in (`autokernel.optimize(..., chain_residuals=True)`): in every
+    nn.ModuleList whose members are all fused residual blocks, each block but the
+    last returns `ResidualPair(hidden, ffn_out)` and the next block's first
+    RMSNorm adds and normalises it in one fused kernel.  This assumes the list is
+    run as `h = block(h)` in order (as pre-norm decoders do); code that reads the
+    intermediate hidden states must not use it.  The last block of a list returns a
+    plain tensor, so whatever follows the list sees what it saw before.
+    Returns the number of blocks that emit pairs.
+    """
+    n = 0
+    for mod in model.modules():
+        if isinstance(mod, nn.ModuleList) and len(mod) > 1 and all(
+                isinstance(b, _FusedResidualRMSNormBlockReplacement) for b in mod):
+            for b in list(mod)[:-1]:
+                b._emit_pair = True
+                n += 1
+    return n
 
 
 ALL_PATTERNS: List[Pattern] = [

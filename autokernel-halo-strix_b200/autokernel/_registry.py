@@ -16,7 +16,7 @@ from typing import Any, Dict, List, Optional, Set
 import torch
 import torch.nn as nn
 
-from autokernel._patterns import ALL_PATTERNS, Pattern
+from autokernel._patterns import ALL_PATTERNS, Pattern, chain_residual_blocks
 
 _STATE_ATTR = "_autokernel_state"
 
@@ -42,13 +42,20 @@ def _select_patterns(include: Optional[List[str]], exclude: Optional[List[str]])
 
 def optimize(model: nn.Module, dtype: torch.dtype = torch.float16, compile: bool = False,
              compile_mode: str = "default", include: Optional[List[str]] = None,
-             exclude: Optional[List[str]] = None, training: bool = False) -> nn.Module:
+             exclude: Optional[List[str]] = None, training: bool = False,
+             chain_residuals: bool = False) -> nn.Module:
     """Replace every matching module with its kernel-backed version (in place).
 
     As in the reference: when `training` is False the model is cast to `dtype`
     (complex buffers preserved) and put in eval mode; with `training=True` the
     parameters keep their dtype (mixed precision is left to autocast).  The
     model is moved to the current CUDA device if it is on the CPU.
+
+    chain_residuals (added, off by default): chain the residual stream through
+    consecutive fused pre-norm blocks of each nn.ModuleList
+    (`chain_residual_blocks`), so each residual add runs inside the next block's
+    fused add + RMSNorm kernel.  Only for models that run such a list as
+    `h = block(h)` and read no intermediate hidden state.
     """
     if not training:
         saved = {n: b.clone() for n, b in model.named_buffers() if b.is_complex()}
@@ -87,6 +94,11 @@ def optimize(model: nn.Module, dtype: torch.dtype = torch.float16, compile: bool
                 count += 1
         if count:
             applied[pattern.name] = count
+
+    if chain_residuals:
+        n = chain_residual_blocks(model)
+        if n:
+            applied["residual_chain"] = n
 
     if compile:
         try:

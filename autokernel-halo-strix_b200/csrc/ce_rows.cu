@@ -262,6 +262,18 @@ unsigned row_grid(int64_t B) {
   return (unsigned)(B < cap ? B : cap);
 }
 
+// x *= *scale, read on the device: every CTA returns after one scalar load when the scale
+// is 1 (an upstream gradient of exactly one, the usual loss.backward()), so the common
+// case moves no tensor bytes and needs no host read of the scalar.
+template <typename T>
+__global__ void __launch_bounds__(256) scale_by_device_scalar(T* __restrict__ x, int64_t n,
+                                                              const float* __restrict__ scale) {
+  const float s = __ldg(scale);
+  if (s == 1.f) return;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    x[i] = from_f<T>(to_f<T>(x[i]) * s);
+}
+
 }  // namespace
 }  // namespace ak
 
@@ -323,5 +335,16 @@ extern "C" int ak_ce_inv_valid(float* inv_out, const int64_t* targets, int64_t B
   AK_REQUIRE(inv_out && B >= 0 && (B == 0 || targets), AK_ERR_ARG, "ak_ce_inv_valid: bad args");
   ce_inv_valid_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(inv_out, targets, B, ignore_index);
   AK_CHECK_LAUNCH("ak_ce_inv_valid");
+  return AK_OK;
+}
+
+extern "C" int ak_scale_by_device_scalar(void* x, int64_t n, const float* scale, int dt, void* stream) {
+  clear_error();
+  AK_REQUIRE(n >= 0 && (n == 0 || (x && scale)), AK_ERR_ARG, "ak_scale_by_device_scalar: bad args");
+  if (n == 0) return AK_OK;
+  const int64_t g = std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
+  AK_DISPATCH_DTYPE(dt, T,
+                    scale_by_device_scalar<T><<<(unsigned)g, 256, 0, (cudaStream_t)stream>>>((T*)x, n, scale));
+  AK_CHECK_LAUNCH("ak_scale_by_device_scalar");
   return AK_OK;
 }

@@ -29,8 +29,9 @@ constexpr int kPlanesPerCta = 8;  // (b, h) planes one thread walks with the sam
 // plane, loads its cos / sin once and applies them to kPlanesPerCta planes
 // (grid.y): per plane only an address step, one load, the rotation and one
 // store.  grid.x covers the N*D/VEC vector positions.
-// ROT false: plain strided copy (no tables read).
-template <typename T, int VEC, bool FULL, bool ROT = true>
+// ROT false: plain strided copy (no tables read).  DENSE: y is dense (B, H, N, D) and its
+// address is one multiply-add per plane (the strided form keeps two more 64-bit strides live).
+template <typename T, int VEC, bool FULL, bool ROT = true, bool DENSE = false>
 __global__ void __launch_bounds__(kThreadsR, 6)
 rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict__ cs, const float* __restrict__ sn,
             int64_t planes, int H, int N, int D, int64_t sb, int64_t sh, int64_t sn_, int64_t yb, int64_t yh,
@@ -64,26 +65,38 @@ rope_kernel(T* __restrict__ y, const T* __restrict__ x, const float* __restrict_
   }
 #pragma unroll
   for (int k = 0; k < VEC / 2; ++k) s[k] *= sign;
-  const int64_t xo = (int64_t)n * sn_ + jb, yo = (int64_t)n * yn + jb;
+  const int64_t xo = (int64_t)n * sn_ + jb, yo = DENSE ? (int64_t)n * D + jb : (int64_t)n * yn + jb;
+  const int64_t ystep = (int64_t)N * D;
   const int64_t p0 = (int64_t)blockIdx.y * kPlanesPerCta;
   const int64_t p1 = p0 + kPlanesPerCta < planes ? p0 + kPlanesPerCta : planes;
   int64_t b = p0 / H;
   int h = (int)(p0 - b * H);
+  // running element pointers: + (head stride) per plane, re-based when the head index wraps
+  const T* xp = x + b * sb + h * sh + xo;
+  T* yp = y + (DENSE ? p0 * ystep : b * yb + h * yh) + yo;
 #pragma unroll 2
   for (int64_t p = p0; p < p1; ++p) {
     if constexpr (ROT) {
       float v[VEC], o[VEC];
-      load_frag<T, VEC>(v, x + b * sb + h * sh + xo);
+      load_frag<T, VEC>(v, xp);
 #pragma unroll
       for (int k = 0; k < VEC / 2; ++k) {
         o[2 * k] = v[2 * k] * c[k] - v[2 * k + 1] * s[k];
         o[2 * k + 1] = v[2 * k] * s[k] + v[2 * k + 1] * c[k];
       }
-      store_frag<T, VEC>(y + b * yb + h * yh + yo, o);
+      store_frag<T, VEC>(yp, o);
     } else {
-      *reinterpret_cast<int4*>(y + b * yb + h * yh + yo) = *reinterpret_cast<const int4*>(x + b * sb + h * sh + xo);
+      *reinterpret_cast<int4*>(yp) = *reinterpret_cast<const int4*>(xp);
     }
-    if (++h == H) { h = 0; ++b; }
+    if (++h == H) {
+      h = 0;
+      ++b;
+      xp = x + b * sb + xo;
+      yp = DENSE ? yp + ystep : y + b * yb + yo;
+    } else {
+      xp += sh;
+      yp += DENSE ? ystep : yh;
+    }
   }
 }
 
@@ -140,7 +153,9 @@ int rope_impl(void* y, const void* x, const float* cos_t, const float* sin_t, in
       const unsigned gy = (unsigned)((planes + kPlanesPerCta - 1) / kPlanesPerCta);
       const dim3 grid(gx, gy);
       const bool full = per_plane % kThreadsR == 0;
-      auto kern = rot ? (full ? rope_kernel<T, VEC, true, true> : rope_kernel<T, VEC, false, true>)
+      const bool dense = yn == D && yh == N * D && yb == H * N * D;
+      auto kern = rot ? (dense ? (full ? rope_kernel<T, VEC, true, true, true> : rope_kernel<T, VEC, false, true, true>)
+                               : (full ? rope_kernel<T, VEC, true, true> : rope_kernel<T, VEC, false, true>))
                       : (full ? rope_kernel<T, VEC, true, false> : rope_kernel<T, VEC, false, false>);
       kern<<<grid, kThreadsR, 0, st>>>((T*)y, (const T*)x, cos_t, sin_t, planes, (int)H, (int)N, (int)D, sb, sh, sn,
                                        yb, yh, yn, sign, tab4);

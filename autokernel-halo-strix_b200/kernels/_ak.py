@@ -36,6 +36,7 @@ SIGNATURES = {
     "ak_rope_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rope_bwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rope_strided": [_vp, _vp, _vp, _vp] + [_i64] * 10 + [_i, _i, _vp],
+    "ak_scale_by_device_scalar": [_vp, _i64, _vp, _i, _vp],
     "ak_transpose": [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i, _vp],
     "ak_rmsnorm_fwd_mixed": [_vp, _i, _vp, _i, _vp, _i, _i64, _i64, _f, _vp],
     "ak_fused_res_rmsnorm_fwd_mixed": [_vp, _vp, _i, _vp, _i, _vp, _i, _vp, _i, _i64, _i64, _f, _vp],
@@ -353,6 +354,18 @@ def rope_fwd(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Ten
 
 def rope_bwd(dy: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     return _rope("ak_rope_bwd", dy, cos, sin)
+
+
+def scale_by_device_scalar_(x: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """In place x *= scale (a one-element tensor read on the device; nothing is written when it
+    is exactly 1).  No host sync."""
+    dev = require_cuda(x, scale)
+    if not x.is_contiguous():
+        raise ValueError("scale_by_device_scalar_: x must be contiguous")
+    s = scale.reshape(1).to(torch.float32)
+    if x.numel():
+        call("ak_scale_by_device_scalar", ptr(x), x.numel(), ptr(s), dtype_code(x), stream(dev))
+    return x
 
 
 def rope_into(y: torch.Tensor, x: torch.Tensor, cos, sin, mode: int) -> torch.Tensor:

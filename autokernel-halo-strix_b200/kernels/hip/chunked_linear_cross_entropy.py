@@ -66,13 +66,34 @@ class _ChunkedLinearCrossEntropy(torch.autograd.Function):
     @staticmethod
     @custom_bwd(device_type="cuda")
     def backward(ctx, grad_output):
-        gh, gw = ctx.saved_tensors
-        one = grad_output.dim() == 0 and grad_output.item() == 1.0
-        if ctx.req[0]:
-            gh = gh if one else gh * grad_output.to(gh.dtype)
-        if ctx.req[1]:
-            gw = gw if one else gw * grad_output.to(gw.dtype)
-        return gh, gw, None, None, None, None, None, None
+        gh, gw = _take_saved(ctx)
+        return (_scaled(gh, grad_output) if ctx.req[0] else None), (_scaled(gw, grad_output) if ctx.req[1] else None), \
+            None, None, None, None, None, None
+
+
+def _take_saved(ctx):
+    """The gradients precomputed in the forward.  They are scaled in place, so a second
+    backward through the same graph (retain_graph=True) is refused instead of returning
+    twice-scaled values."""
+    if getattr(ctx, "consumed", False):
+        raise RuntimeError("fused linear + cross-entropy: backward through the same graph twice is not supported "
+                           "(the gradients are computed in the forward and consumed by the first backward)")
+    ctx.consumed = True
+    return ctx.saved_tensors
+
+
+def _scaled(g, grad_output):
+    """The saved gradient times the scalar upstream gradient.  The reference checks
+    `grad_output.item() == 1.0` on the host to skip the multiply
+    (chunked_linear_cross_entropy.py:159-169); here the scalar is read on the device by the
+    scaling kernel itself (nothing written when it is 1), so there is no host sync and the
+    backward can be captured in a CUDA graph.  The saved tensor is owned by this call (made in
+    the forward, used once), so it is scaled in place."""
+    if g is None:
+        return None
+    if grad_output.numel() != 1:
+        return g * grad_output.to(g.dtype)
+    return _ak.scale_by_device_scalar_(g, grad_output)
 
 
 class _FusedLinearCrossEntropy(torch.autograd.Function):
@@ -96,13 +117,9 @@ class _FusedLinearCrossEntropy(torch.autograd.Function):
     @staticmethod
     @custom_bwd(device_type="cuda")
     def backward(ctx, grad_output):
-        gh, gw = ctx.saved_tensors
-        one = grad_output.dim() == 0 and grad_output.item() == 1.0
-        if ctx.req[0] and not one:
-            gh = gh * grad_output.to(gh.dtype)
-        if ctx.req[1] and not one:
-            gw = gw * grad_output.to(gw.dtype)
-        return (gh if ctx.req[0] else None), (gw if ctx.req[1] else None), None, None
+        gh, gw = _take_saved(ctx)
+        return (_scaled(gh, grad_output) if ctx.req[0] else None), \
+            (_scaled(gw, grad_output) if ctx.req[1] else None), None, None
 
 
 class ChunkedLinearCrossEntropyLoss(nn.Module):

@@ -604,10 +604,11 @@ def time_train(dev, steps, warmup, world, rank, micro_batch=16, seq=1024):
     from halo_training.hybrid_lm import HybridConfig, count_params
     from halo_training.train_step import HybridTrainer, synthetic_batch
     cfg = HybridConfig()
-    tr = HybridTrainer(cfg, device=dev, use_kernels=True, ddp=world > 1, seed=0)
+    # the whole step (forward, backward with DDP's all-reduce, AdamW) replays as one CUDA graph
+    tr = HybridTrainer(cfg, device=dev, use_kernels=True, ddp=world > 1, seed=0, cuda_graph=True)
     idx, tgt = synthetic_batch(micro_batch, seq, cfg.vocab_size, seed=1000 + rank, device=dev)
     st = torch.cuda.current_stream(dev)
-    for _ in range(warmup):
+    for _ in range(max(warmup, tr.graph_warmup + 2)):  # eager warm-up, capture, one replay
         tr.step(idx, tgt)
     torch.cuda.synchronize(dev)
     barrier(world)
@@ -622,7 +623,8 @@ def time_train(dev, steps, warmup, world, rank, micro_batch=16, seq=1024):
            "params": count_params(tr.raw), "micro_batch_per_gpu": micro_batch, "seq_len": seq,
            "loss_last": round(float(loss.item()), 4), "steps": steps,
            "model": "hybrid 12L d768 (6 Mamba N16 + 6 GQA 12q/4kv), SwiGLU 2048, tied 50304 vocab",
-           "parallelism": f"ddp{world} (NCCL)" if world > 1 else "single GPU"}
+           "parallelism": f"ddp{world} (NCCL)" if world > 1 else "single GPU",
+           "cuda_graph": "whole step (forward, backward, all-reduce, AdamW) captured once, replayed per step"}
     del tr
     torch.cuda.empty_cache()
     return out

@@ -144,6 +144,15 @@ AK_API int ak_ce_rows_reduce(float* loss_out, float* n_valid_out, const float* l
 AK_API int ak_ce_inv_valid(float* inv_out, const int64_t* targets, int64_t B,
                     int64_t ignore_index, void* stream);
 
+/* x[i] *= scale[0] for i < n (x of dtype dt), with the scalar read on the device:
+ * nothing is written when it is 1.  Device-side replacement of the
+ * `grad_output.item() == 1.0` fast-path check before the gradient scaling in
+ * the backward of the chunked linear + CE
+ * (kernels/hip/chunked_linear_cross_entropy.py:152-169), so the backward needs
+ * no host sync and can be captured in a CUDA graph. */
+AK_API int ak_scale_by_device_scalar(void* x, int64_t n, const float* scale, int dt,
+                                     void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Fused linear + cross-entropy on the tensor cores (tcgen05 / TMEM / TMA)
  * ------------------------------------------------------------------------ */

@@ -140,3 +140,31 @@ def test_linear_ce_logits_grad(N, D, V):
     assert_lowp_close(G.float() * n, rg * n, what="G")
     rl, _, _ = O.linear_ce(H, W, lab)
     assert abs(loss.item() - rl.item()) <= 3e-3 * max(1.0, abs(rl.item()))
+
+
+@pytest.mark.parametrize("use_fused", [True, False])
+def test_linear_ce_upstream_grad_scaling_on_device(use_fused):
+    """The precomputed dH / dW are scaled by the upstream gradient on the device (no
+    grad_output.item()): exactly the unit-gradient result times the scale, unchanged for a unit
+    gradient, and a second backward through the same graph is refused."""
+    from kernels.hip.chunked_linear_cross_entropy import ChunkedLinearCrossEntropyLoss
+    g = torch.Generator().manual_seed(5)
+    H = torch.randn(300, 64, generator=g).to(torch.bfloat16).to(DEV)
+    W = (0.02 * torch.randn(1000, 64, generator=g)).to(torch.bfloat16).to(DEV)
+    lab = torch.randint(0, 1000, (300,), generator=g).to(DEV)
+    mod = ChunkedLinearCrossEntropyLoss(chunk_size=128)
+    mod.use_fused = use_fused
+    grads = []
+    for scale in (1.0, 2.5):
+        h, w = H.clone().requires_grad_(True), W.clone().requires_grad_(True)
+        loss = mod(h, w, lab)
+        loss.backward(torch.tensor(scale, device=DEV))
+        grads.append((h.grad.float(), w.grad.float()))
+    assert torch.equal(grads[1][0], (grads[0][0].to(torch.bfloat16) * 2.5).float()) or \
+        torch.allclose(grads[1][0], grads[0][0] * 2.5, rtol=1e-2, atol=1e-6)
+    torch.testing.assert_close(grads[1][1], grads[0][1] * 2.5, rtol=1e-2, atol=1e-6)
+    h, w = H.clone().requires_grad_(True), W.clone().requires_grad_(True)
+    loss = mod(h, w, lab)
+    loss.backward(retain_graph=True)
+    with pytest.raises(RuntimeError, match="twice"):
+        loss.backward()

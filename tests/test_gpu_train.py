@@ -62,3 +62,58 @@ def test_hybrid_124m_bf16_step_all_params_get_grads():
     for _ in range(3):
         l1 = tr.step(idx, tgt).item()
     assert l1 < l0
+
+
+def test_residual_chain_matches_unchained_bf16():
+    """chain_residuals=True (each residual add inside the next fused add + RMSNorm) against the
+    same optimized model without the chain, under bf16 autocast: the hidden stream is the same
+    fp32 add rounded once and the gradient accumulation the same fp32 sum, so outputs and
+    gradients agree to the last bit (a tight tolerance allows for reordering inside kernels)."""
+    import copy
+
+    import autokernel
+    from halo_training.hybrid_lm import HybridConfig, HybridLM
+    from autokernel._patterns import ResidualPair
+    torch.manual_seed(0)
+    cfg = HybridConfig(**TINY)
+    base = HybridLM(cfg).init_weights(seed=0).cuda()
+    for m in base.modules():
+        if hasattr(m, "fused_conv"):
+            m.fused_conv = True
+    plain = autokernel.optimize(copy.deepcopy(base), training=True)
+    chained = autokernel.optimize(copy.deepcopy(base), training=True, chain_residuals=True)
+    assert autokernel.report(chained)["patterns"]["residual_chain"]["modules_replaced"] == cfg.n_layers - 1
+    idx = torch.randint(0, cfg.vocab_size, (2, 256), device="cuda")
+    outs = []
+    for m in (plain, chained):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            h = m(idx)
+            if m is chained:  # intermediate blocks hand on pairs
+                with torch.no_grad():
+                    assert isinstance(m.layers[0](m.embed(idx)), ResidualPair)
+        assert torch.is_tensor(h)
+        h.float().square().mean().backward()
+        outs.append((h.detach(), {n: p.grad.detach().clone() for n, p in m.named_parameters()}))
+    torch.testing.assert_close(outs[1][0], outs[0][0], rtol=0, atol=0)
+    for n, g in outs[0][1].items():
+        torch.testing.assert_close(outs[1][1][n], g, rtol=1e-5, atol=1e-7, msg=n)
+
+
+def test_cuda_graph_step_matches_eager():
+    """HybridTrainer(cuda_graph=True): eager warm-up calls, then one captured step replayed per
+    call; one optimizer step per call, and the loss curve follows the eager trainer's (within
+    the run-to-run noise of the atomics-based reductions)."""
+    from halo_training.hybrid_lm import HybridConfig
+    from halo_training.train_step import HybridTrainer, synthetic_batch
+    cfg = HybridConfig(**TINY)
+    idx, tgt = synthetic_batch(4, 256, cfg.vocab_size, seed=7, device="cuda")
+    curves = []
+    for graph in (False, True):
+        tr = HybridTrainer(cfg, device=torch.device("cuda"), use_kernels=True, seed=0, cuda_graph=graph)
+        curves.append([tr.step(idx, tgt).item() for _ in range(tr.graph_warmup + 4)])
+        if graph:
+            assert tr._graph is not None
+            assert tr.opt.state[next(iter(tr.raw.parameters()))]["step"].item() == tr.graph_warmup + 4
+    for a, b in zip(*curves):
+        assert abs(a - b) < 2e-3 * max(1.0, abs(a)), (curves[0], curves[1])
+    assert curves[1][-1] < curves[1][0]
