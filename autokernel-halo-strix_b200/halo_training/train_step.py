@@ -61,9 +61,9 @@ class HybridTrainer:
             from torch.nn.parallel import DistributedDataParallel as DDP
             ids = [device.index] if device.type == "cuda" else None
             if self.cuda_graph:
-                # capture-safe DDP: built on a side stream, as CUDA-graph capture of its
-                # all-reduce hooks requires
-                s = torch.cuda.Stream(device)
+                # capture-safe DDP: built on the side stream that also runs the eager warm-up
+                # steps, as CUDA-graph capture of its all-reduce hooks requires
+                s = self._side_stream()
                 s.wait_stream(torch.cuda.current_stream(device))
                 with torch.cuda.stream(s):
                     model = DDP(model, device_ids=ids, gradient_as_bucket_view=True, bucket_cap_mb=bucket_cap_mb,
@@ -83,6 +83,11 @@ class HybridTrainer:
         self.loss_fn = loss_fn or (kernel_loss_fn() if use_kernels else eager_loss_fn)
         self.autocast = (device.type == "cuda") if autocast is None else autocast
 
+    def _side_stream(self) -> torch.cuda.Stream:
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(self.device)
+        return self._side
+
     def _eager_step(self, idx: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         # the autocast weight-cast cache cannot live across CUDA-graph replays
         with torch.autocast(self.device.type, dtype=torch.bfloat16, enabled=self.autocast,
@@ -98,7 +103,7 @@ class HybridTrainer:
         self._calls += 1
         if not self.cuda_graph or self._calls <= self.graph_warmup:
             if self.cuda_graph:  # warm-up on a side stream, as graph capture requires
-                s = torch.cuda.Stream(self.device)
+                s = self._side_stream()
                 s.wait_stream(torch.cuda.current_stream(self.device))
                 with torch.cuda.stream(s):
                     loss = self._eager_step(idx, targets)
@@ -113,7 +118,7 @@ class HybridTrainer:
             self.opt.zero_grad(set_to_none=True)  # the captured backward allocates and writes the grads
             self._graph = torch.cuda.CUDAGraph()
             # thread-local capture mode: the NCCL watchdog thread may query events meanwhile
-            with torch.cuda.graph(self._graph, capture_error_mode="thread_local"):
+            with torch.cuda.graph(self._graph, stream=self._side_stream(), capture_error_mode="thread_local"):
                 self._static_loss = self._eager_step(*self._static)
         else:
             self._static[0].copy_(idx, non_blocking=True)
