@@ -14,6 +14,7 @@ namespace ak {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kBatch = 4;  // independent 16-byte loads in flight per thread
 
 struct CeParams {
   float softcap, inv_softcap, ls, ls_uniform, target_coeff;
@@ -32,7 +33,48 @@ __device__ __forceinline__ void merge(float& m, float& s, float mb, float sb) {
   m = mn;
 }
 
-template <typename T>
+// Vector index holding the target column, or -1 (ignored row or target out of range).
+__device__ __forceinline__ int target_vec(int64_t tgt, bool ignored, int V, int vec) {
+  return (!ignored && tgt >= 0 && tgt < V) ? (int)(tgt / vec) : -1;
+}
+
+// o[k] -= d for the one element k == tk (unrolled select, no dynamic register index).
+template <int VEC>
+__device__ __forceinline__ void sub_at(float (&o)[VEC], int tk, float d) {
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) o[k] -= (k == tk) ? d : 0.f;
+}
+
+// Gradient of one vector: o = softmax * scale - u * scale (- t * scale at the target column),
+// times (1 - tanh^2) under softcap.  is_t: the vector holds the target column tk.
+template <bool CAP, int VEC>
+__device__ __forceinline__ void ce_grad_vec(const float (&e)[VEC], bool is_t, int tk, float off, float sc_p,
+                                            float sub, float tsub, const CeParams& p, float (&o)[VEC]) {
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) {
+    if constexpr (CAP) {
+      const float xc = cap(e[k], p);
+      float g = fmaf(ex2(fmaf(xc, kLog2e, off)), sc_p, -sub);
+      if (is_t && k == tk) g -= tsub;
+      const float t = xc * p.inv_softcap;
+      o[k] = g * (1.f - t * t);
+    } else {
+      o[k] = fmaf(ex2(fmaf(e[k], kLog2e, off)), sc_p, -sub);
+    }
+  }
+  if constexpr (!CAP) {
+    if (is_t) sub_at<VEC>(o, tk, tsub);
+  }
+}
+
+// One CTA per row.  Pass 1: online (max, sum of exp) with kBatch independent 16-byte loads per
+// thread in flight; pass 2 (fused mode): gradient from the row re-read (an L2 hit).
+// CAP: softcap active (tanh on every element and its derivative on the gradient); LS: label
+// smoothing (the row sum of x' for the loss).  Without CAP, an element costs one FFMA + ex2 + add
+// in pass 1 and FFMA + ex2 + FFMA in pass 2: log2(e), 1/S, the gradient scale and the uniform
+// smoothing term are folded into the two FFMA constants, and the target column is corrected once
+// per vector, not compared per element.
+template <typename T, bool CAP, bool LS>
 __global__ void __launch_bounds__(kThreads)
 ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, float* __restrict__ max_out,
                    float* __restrict__ sum_out, T* __restrict__ grad, const T* __restrict__ logits,
@@ -41,7 +83,6 @@ ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, floa
   constexpr int VEC = 16 / sizeof(T);
   __shared__ float s_m[kThreads / 32], s_s[kThreads / 32], s_x[kThreads / 32];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool use_ls = p.ls > 0.f;
   const float scale = scale_grad * (scale_dev ? *scale_dev : 1.f);
   for (int64_t b = blockIdx.x; b < B; b += gridDim.x) {
     const T* row = logits + b * V;
@@ -49,28 +90,55 @@ ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, floa
     const bool ignored = (tgt == p.ignore_index);
     float m = -INFINITY, s = 0.f, sx = 0.f;
     const int nvec = vec_ok ? V / VEC : 0;
-    for (int v = tid; v < nvec; v += kThreads) {
+    int v = tid;
+    for (; v + (kBatch - 1) * kThreads < nvec; v += kBatch * kThreads) {
+      float e[kBatch][VEC];
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q) load_frag<T, VEC>(e[q], row + (int64_t)(v + q * kThreads) * VEC);
+      float lm = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q)
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) {
+          if constexpr (CAP) e[q][k] = cap(e[q][k], p);
+          lm = fmaxf(lm, e[q][k]);
+          if constexpr (LS) sx += e[q][k];
+        }
+      const float mn = fmaxf(m, lm);
+      if (mn != -INFINITY) {
+        const float off = -mn * kLog2e;
+        float acc = s * ex2(fmaf(m, kLog2e, off));
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q)
+#pragma unroll
+          for (int k = 0; k < VEC; ++k) acc += ex2(fmaf(e[q][k], kLog2e, off));
+        s = acc;
+        m = mn;
+      }
+    }
+    for (; v < nvec; v += kThreads) {
       float e[VEC];
       load_frag<T, VEC>(e, row + (int64_t)v * VEC);
       float lm = -INFINITY;
 #pragma unroll
       for (int k = 0; k < VEC; ++k) {
-        e[k] = cap(e[k], p);
+        if constexpr (CAP) e[k] = cap(e[k], p);
         lm = fmaxf(lm, e[k]);
-        sx += e[k];
+        if constexpr (LS) sx += e[k];
       }
       const float mn = fmaxf(m, lm);
       if (mn != -INFINITY) {
-        float acc = s * ex2((m - mn) * kLog2e);
+        const float off = -mn * kLog2e;
+        float acc = s * ex2(fmaf(m, kLog2e, off));
 #pragma unroll
-        for (int k = 0; k < VEC; ++k) acc += ex2((e[k] - mn) * kLog2e);
+        for (int k = 0; k < VEC; ++k) acc += ex2(fmaf(e[k], kLog2e, off));
         s = acc;
         m = mn;
       }
     }
     for (int i = nvec * VEC + tid; i < V; i += kThreads) {
-      const float e = cap(to_f<T>(row[i]), p);
-      sx += e;
+      const float e = CAP ? cap(to_f<T>(row[i]), p) : to_f<T>(row[i]);
+      if constexpr (LS) sx += e;
       merge(m, s, e, 1.f);
     }
 #pragma unroll
@@ -79,7 +147,7 @@ ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, floa
       const float so = __shfl_xor_sync(0xffffffffu, s, o);
       merge(m, s, mo, so);
     }
-    sx = warp_sum(sx);
+    if constexpr (LS) sx = warp_sum(sx);
     if (lane == 0) { s_m[warp] = m; s_s[warp] = s; s_x[warp] = sx; }
     __syncthreads();
     float M = -INFINITY, S = 0.f, SX = 0.f;
@@ -96,16 +164,35 @@ ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, floa
         if (tgt < 0 || tgt >= V) {
           loss = NAN;
         } else {
-          const float xt = cap(to_f<T>(row[tgt]), p);
-          loss = use_ls ? lse - p.target_coeff * xt - p.ls * (SX / (float)V) : lse - xt;
+          const float xt = CAP ? cap(to_f<T>(row[tgt]), p) : to_f<T>(row[tgt]);
+          loss = LS ? lse - p.target_coeff * xt - p.ls * (SX / (float)V) : lse - xt;
         }
       }
       losses[b] = loss;
     }
     if (grad != nullptr) {
       T* grow = grad + b * V;
-      const float inv_s = 1.f / S;
-      for (int v = tid; v < nvec; v += kThreads) {
+      const float off = -M * kLog2e;
+      const float sc_p = scale / S;            // softmax * scale = ex2(x log2e + off) * sc_p
+      const float sub = p.ls_uniform * scale;  // uniform smoothing term, scaled
+      const float tsub = p.target_coeff * scale;
+      const int tv = target_vec(tgt, ignored, V, VEC);
+      const int tk = tv >= 0 ? (int)(tgt - (int64_t)tv * VEC) : -1;
+      int v = tid;
+      if (!ignored) {
+        for (; v + (kBatch - 1) * kThreads < nvec; v += kBatch * kThreads) {
+          float e[kBatch][VEC];
+#pragma unroll
+          for (int q = 0; q < kBatch; ++q) load_frag<T, VEC>(e[q], row + (int64_t)(v + q * kThreads) * VEC);
+#pragma unroll
+          for (int q = 0; q < kBatch; ++q) {
+            float o[VEC];
+            ce_grad_vec<CAP, VEC>(e[q], v + q * kThreads == tv, tk, off, sc_p, sub, tsub, p, o);
+            store_frag<T, VEC>(grow + (int64_t)(v + q * kThreads) * VEC, o);
+          }
+        }
+      }
+      for (; v < nvec; v += kThreads) {
         float o[VEC];
         if (ignored) {
 #pragma unroll
@@ -113,27 +200,17 @@ ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, floa
         } else {
           float e[VEC];
           load_frag<T, VEC>(e, row + (int64_t)v * VEC);
-#pragma unroll
-          for (int k = 0; k < VEC; ++k) {
-            const float xc = cap(e[k], p);
-            float g = ex2((xc - M) * kLog2e) * inv_s;
-            if ((int64_t)v * VEC + k == tgt) g -= p.target_coeff;
-            g -= p.ls_uniform;
-            if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
-            o[k] = g * scale;
-          }
+          ce_grad_vec<CAP, VEC>(e, v == tv, tk, off, sc_p, sub, tsub, p, o);
         }
         store_frag<T, VEC>(grow + (int64_t)v * VEC, o);
       }
       for (int i = nvec * VEC + tid; i < V; i += kThreads) {
         float g = 0.f;
         if (!ignored) {
-          const float xc = cap(to_f<T>(row[i]), p);
-          g = ex2((xc - M) * kLog2e) * inv_s;
-          if (i == tgt) g -= p.target_coeff;
-          g -= p.ls_uniform;
-          if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
-          g *= scale;
+          const float xc = CAP ? cap(to_f<T>(row[i]), p) : to_f<T>(row[i]);
+          g = fmaf(ex2(fmaf(xc, kLog2e, off)), sc_p, -sub);
+          if (i == tgt) g -= tsub;
+          if constexpr (CAP) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
         }
         grow[i] = from_f<T>(g);
       }
@@ -142,8 +219,10 @@ ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, floa
 }
 
 // Tiny-mode backward: recompute softmax from saved (row_max, row_sum), plus the
-// optional z-loss gradient z_coef * lse * softmax (kernels/ce_fused.py:672-689).
-template <typename T>
+// optional z-loss gradient z_coef * lse * softmax (kernels/ce_fused.py:672-689):
+//   g = (p - t[i==y] - u) * scale + z * lse * p,  times (1 - tanh^2) under softcap,
+// i.e. p * (scale + z lse) - (t[i==y] + u) * scale: one FFMA around the ex2 without softcap.
+template <typename T, bool CAP>
 __global__ void __launch_bounds__(kThreads)
 ce_rows_bwd_kernel(T* __restrict__ grad, const T* __restrict__ logits, const int64_t* __restrict__ targets,
                    const float* __restrict__ row_max, const float* __restrict__ row_sum, int64_t B, int V,
@@ -159,10 +238,29 @@ ce_rows_bwd_kernel(T* __restrict__ grad, const T* __restrict__ logits, const int
     const int64_t tgt = targets[b];
     const bool ignored = (tgt == p.ignore_index);
     const float M = row_max[b];
-    const float inv_s = 1.f / row_sum[b];
     const float lse = M + lg2(row_sum[b]) * kLn2;
+    const float off = -M * kLog2e;
+    const float sc_p = (scale + zc * lse) / row_sum[b];
+    const float sub = p.ls_uniform * scale;
+    const float tsub = p.target_coeff * scale;
+    const int tv = target_vec(tgt, ignored, V, VEC);
+    const int tk = tv >= 0 ? (int)(tgt - (int64_t)tv * VEC) : -1;
     const int nvec = vec_ok ? V / VEC : 0;
-    for (int v = tid; v < nvec; v += kThreads) {
+    int v = tid;
+    if (!ignored) {
+      for (; v + (kBatch - 1) * kThreads < nvec; v += kBatch * kThreads) {
+        float e[kBatch][VEC];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) load_frag<T, VEC>(e[q], row + (int64_t)(v + q * kThreads) * VEC);
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+          float o[VEC];
+          ce_grad_vec<CAP, VEC>(e[q], v + q * kThreads == tv, tk, off, sc_p, sub, tsub, p, o);
+          store_frag<T, VEC>(grow + (int64_t)(v + q * kThreads) * VEC, o);
+        }
+      }
+    }
+    for (; v < nvec; v += kThreads) {
       float o[VEC];
       if (ignored) {
 #pragma unroll
@@ -170,30 +268,17 @@ ce_rows_bwd_kernel(T* __restrict__ grad, const T* __restrict__ logits, const int
       } else {
         float e[VEC];
         load_frag<T, VEC>(e, row + (int64_t)v * VEC);
-#pragma unroll
-        for (int k = 0; k < VEC; ++k) {
-          const float xc = cap(e[k], p);
-          const float pr = ex2((xc - M) * kLog2e) * inv_s;
-          float g = pr;
-          if ((int64_t)v * VEC + k == tgt) g -= p.target_coeff;
-          g -= p.ls_uniform;
-          g = g * scale + zc * lse * pr;  // z-loss term also flows through the softcap
-          if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
-          o[k] = g;
-        }
+        ce_grad_vec<CAP, VEC>(e, v == tv, tk, off, sc_p, sub, tsub, p, o);
       }
       store_frag<T, VEC>(grow + (int64_t)v * VEC, o);
     }
     for (int i = nvec * VEC + tid; i < V; i += kThreads) {
       float g = 0.f;
       if (!ignored) {
-        const float xc = cap(to_f<T>(row[i]), p);
-        const float pr = ex2((xc - M) * kLog2e) * inv_s;
-        g = pr;
-        if (i == tgt) g -= p.target_coeff;
-        g -= p.ls_uniform;
-        g = g * scale + zc * lse * pr;
-        if (p.softcap > 0.f) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
+        const float xc = CAP ? cap(to_f<T>(row[i]), p) : to_f<T>(row[i]);
+        g = fmaf(ex2(fmaf(xc, kLog2e, off)), sc_p, -sub);
+        if (i == tgt) g -= tsub;
+        if constexpr (CAP) { const float t = xc * p.inv_softcap; g *= (1.f - t * t); }
       }
       grow[i] = from_f<T>(g);
     }
@@ -257,9 +342,17 @@ CeParams make_params(float softcap, int64_t ignore_index, float ls, int64_t V) {
   return p;
 }
 
-unsigned row_grid(int64_t B) {
-  const int64_t cap = (int64_t)sm_count() * 8;
-  return (unsigned)(B < cap ? B : cap);
+// CTAs for B rows: the CTAs resident at once (occupancy query), and the same number of rows for
+// every CTA, so the rows finish in one round with no partial last wave.
+template <typename K>
+unsigned row_grid(K kern, int64_t B) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
+  const int64_t cap = (int64_t)sm_count() * per_sm;
+  if (B <= cap) return (unsigned)B;
+  const int64_t per = (B + cap - 1) / cap;
+  return (unsigned)((B + per - 1) / per);
 }
 
 // x *= *scale, read on the device: every CTA returns after one scalar load when the scale
@@ -290,10 +383,14 @@ extern "C" int ak_ce_rows_fwd(float* losses, float* lse, float* row_max, float* 
   const CeParams p = make_params(softcap, ignore_index, label_smoothing, V);
   const int es = elem_size(dt);
   const bool vec_ok = aligned16(logits) && (grad == nullptr || aligned16(grad)) && ((V * es) % 16 == 0);
-  AK_DISPATCH_DTYPE(dt, T,
-                    ce_rows_fwd_kernel<T><<<row_grid(B), kThreads, 0, (cudaStream_t)stream>>>(
-                        losses, lse, row_max, row_sum, (T*)grad, (const T*)logits, targets, B, (int)V, p,
-                        scale_grad, scale_dev, vec_ok));
+  const bool capf = p.softcap > 0.f, lsf = p.ls > 0.f;
+  AK_DISPATCH_DTYPE(dt, T, {
+    auto kern = capf ? (lsf ? ce_rows_fwd_kernel<T, true, true> : ce_rows_fwd_kernel<T, true, false>)
+                     : (lsf ? ce_rows_fwd_kernel<T, false, true> : ce_rows_fwd_kernel<T, false, false>);
+    kern<<<row_grid(kern, B), kThreads, 0, (cudaStream_t)stream>>>(losses, lse, row_max, row_sum, (T*)grad,
+                                                             (const T*)logits, targets, B, (int)V, p, scale_grad,
+                                                             scale_dev, vec_ok);
+  });
   AK_CHECK_LAUNCH("ak_ce_rows_fwd");
   return AK_OK;
 }
@@ -309,10 +406,13 @@ extern "C" int ak_ce_rows_bwd(void* grad, const void* logits, const int64_t* tar
   const CeParams p = make_params(softcap, ignore_index, label_smoothing, V);
   const int es = elem_size(dt);
   const bool vec_ok = aligned16(logits) && aligned16(grad) && ((V * es) % 16 == 0);
-  AK_DISPATCH_DTYPE(dt, T,
-                    ce_rows_bwd_kernel<T><<<row_grid(B), kThreads, 0, (cudaStream_t)stream>>>(
-                        (T*)grad, (const T*)logits, targets, row_max, row_sum, B, (int)V, p, scale, scale_dev,
-                        z_coef, vec_ok));
+  const bool capf = p.softcap > 0.f;
+  AK_DISPATCH_DTYPE(dt, T, {
+    auto kern = capf ? ce_rows_bwd_kernel<T, true> : ce_rows_bwd_kernel<T, false>;
+    kern<<<row_grid(kern, B), kThreads, 0, (cudaStream_t)stream>>>((T*)grad, (const T*)logits, targets, row_max,
+                                                             row_sum, B, (int)V, p, scale, scale_dev, z_coef,
+                                                             vec_ok);
+  });
   AK_CHECK_LAUNCH("ak_ce_rows_bwd");
   return AK_OK;
 }
