@@ -26,9 +26,9 @@ constexpr int kW = 8;  // warps per CTA
 // one dependent round trip per guarded step; only the stores are guarded.
 template <int SEG>
 __global__ void __launch_bounds__(kW * 32)
-scan1_fwd_kernel(float* __restrict__ y, const float* __restrict__ dA, const float* __restrict__ dBx,
-                 const float* __restrict__ Cm, const float* __restrict__ Dv, const float* __restrict__ x,
-                 int L, int d) {
+scan1_fwd_kernel(float* __restrict__ y, float* __restrict__ carries, const float* __restrict__ dA,
+                 const float* __restrict__ dBx, const float* __restrict__ Cm, const float* __restrict__ Dv,
+                 const float* __restrict__ x, int L, int d, int nchunk) {
   __shared__ float sP[2][kW][32], sH[2][kW][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lane;
@@ -38,8 +38,10 @@ scan1_fwd_kernel(float* __restrict__ y, const float* __restrict__ dA, const floa
   const int64_t base = b * (int64_t)L * d + (cv ? c : d - 1);
   constexpr int CH = kW * SEG;
   float carry = 0.f;
-  int par = 0;
-  for (int t0 = 0; t0 < L; t0 += CH, par ^= 1) {
+  int par = 0, ci = 0;
+  for (int t0 = 0; t0 < L; t0 += CH, par ^= 1, ++ci) {
+    // chunk-start state h_{t0-1} for the backward (the carry pass's output, saved here)
+    if (carries != nullptr && warp == 0 && cv) carries[((int64_t)b * nchunk + ci) * d + c] = carry;
     const int tw = t0 + warp * SEG;
     float a[SEG], bb[SEG], cc[SEG], xx[SEG];
 #pragma unroll
@@ -218,6 +220,7 @@ __global__ void scan1_gd_reduce(float* __restrict__ gD, const float* __restrict_
 }
 
 constexpr int kSegF = 8, kSegB = 8;
+static_assert(kSegF == kSegB, "the forward saves the backward's chunk-start states: same chunking");
 inline int nchunk_bwd(int64_t L) { return (int)((L + kW * kSegB - 1) / (kW * kSegB)); }
 
 }  // namespace
@@ -225,16 +228,29 @@ inline int nchunk_bwd(int64_t L) { return (int)((L + kW * kSegB - 1) / (kW * kSe
 
 using namespace ak;
 
-extern "C" int ak_scan1_fwd(float* y, const float* dA, const float* dBx, const float* C, const float* D,
-                            const float* x, int64_t B, int64_t L, int64_t d, void* stream) {
+extern "C" int ak_scan1_fwd_ex(float* y, float* carries, const float* dA, const float* dBx, const float* C,
+                               const float* D, const float* x, int64_t B, int64_t L, int64_t d, void* stream) {
   clear_error();
   AK_REQUIRE(B >= 0 && L >= 0 && d >= 0 && B < 65536 && L < (1LL << 31) && d < (1LL << 31), AK_ERR_SHAPE,
              "ak_scan1_fwd: bad shape");
   if (B == 0 || L == 0 || d == 0) return AK_OK;
   AK_REQUIRE(y && dA && dBx && C && x, AK_ERR_ARG, "ak_scan1_fwd: null pointer");
   dim3 grid((unsigned)((d + 31) / 32), (unsigned)B);
-  scan1_fwd_kernel<kSegF><<<grid, kW * 32, 0, (cudaStream_t)stream>>>(y, dA, dBx, C, D, x, (int)L, (int)d);
+  scan1_fwd_kernel<kSegF><<<grid, kW * 32, 0, (cudaStream_t)stream>>>(y, carries, dA, dBx, C, D, x, (int)L, (int)d,
+                                                                      nchunk_bwd(L));
   AK_CHECK_LAUNCH("ak_scan1_fwd");
+  return AK_OK;
+}
+
+extern "C" int ak_scan1_fwd(float* y, const float* dA, const float* dBx, const float* C, const float* D,
+                            const float* x, int64_t B, int64_t L, int64_t d, void* stream) {
+  return ak_scan1_fwd_ex(y, nullptr, dA, dBx, C, D, x, B, L, d, stream);
+}
+
+extern "C" int ak_scan1_carries_size(int64_t B, int64_t L, int64_t d, size_t* bytes) {
+  clear_error();
+  AK_REQUIRE(bytes && B >= 0 && L >= 0 && d >= 0, AK_ERR_ARG, "ak_scan1_carries_size: bad args");
+  *bytes = (size_t)B * nchunk_bwd(L) * d * sizeof(float);
   return AK_OK;
 }
 
@@ -245,9 +261,10 @@ extern "C" int ak_scan1_bwd_workspace_size(int64_t B, int64_t L, int64_t d, size
   return AK_OK;
 }
 
-extern "C" int ak_scan1_bwd(float* gdA, float* gdBx, float* gC, float* gD, float* gx, void* workspace,
-                            size_t ws_bytes, const float* dA, const float* dBx, const float* C, const float* D,
-                            const float* x, const float* gy, int64_t B, int64_t L, int64_t d, void* stream) {
+extern "C" int ak_scan1_bwd_ex(float* gdA, float* gdBx, float* gC, float* gD, float* gx, void* workspace,
+                               size_t ws_bytes, const float* carries_in, const float* dA, const float* dBx,
+                               const float* C, const float* D, const float* x, const float* gy, int64_t B,
+                               int64_t L, int64_t d, void* stream) {
   clear_error();
   AK_REQUIRE(B >= 0 && L >= 0 && d >= 0 && B < 65536 && L < (1LL << 31) && d < (1LL << 31), AK_ERR_SHAPE,
              "ak_scan1_bwd: bad shape");
@@ -260,13 +277,18 @@ extern "C" int ak_scan1_bwd(float* gdA, float* gdBx, float* gC, float* gD, float
   }
   AK_REQUIRE(gdA && gdBx && gC && gx && dA && dBx && C && x && gy, AK_ERR_ARG, "ak_scan1_bwd: null pointer");
   const int nch = nchunk_bwd(L);
-  const size_t need = ((size_t)B * nch * d + (size_t)B * d) * sizeof(float);
+  const size_t ncarry = carries_in ? 0 : (size_t)B * nch * d;
+  const size_t need = (ncarry + (size_t)B * d) * sizeof(float);
   AK_REQUIRE(workspace && ws_bytes >= need, AK_ERR_WORKSPACE, "ak_scan1_bwd: workspace %zu < %zu", ws_bytes, need);
-  float* carries = (float*)workspace;
-  float* gdpart = carries + (size_t)B * nch * d;
+  float* gdpart = (float*)workspace + ncarry;
   dim3 grid((unsigned)((d + 31) / 32), (unsigned)B);
-  scan1_carry_kernel<kSegB><<<grid, kW * 32, 0, st>>>(carries, dA, dBx, (int)L, (int)d, nch);
-  AK_CHECK_LAUNCH("ak_scan1_bwd(carries)");
+  const float* carries = carries_in;
+  if (carries == nullptr) {  // no saved chunk-start states: re-derive them (reads dA, dBx once more)
+    float* cw = (float*)workspace;
+    scan1_carry_kernel<kSegB><<<grid, kW * 32, 0, st>>>(cw, dA, dBx, (int)L, (int)d, nch);
+    AK_CHECK_LAUNCH("ak_scan1_bwd(carries)");
+    carries = cw;
+  }
   scan1_bwd_kernel<kSegB><<<grid, kW * 32, 0, st>>>(gdA, gdBx, gC, gx, gdpart, carries, dA, dBx, C, D, x, gy,
                                                     (int)L, (int)d, nch);
   AK_CHECK_LAUNCH("ak_scan1_bwd");
@@ -275,4 +297,11 @@ extern "C" int ak_scan1_bwd(float* gdA, float* gdBx, float* gC, float* gD, float
               "ak_scan1_bwd(gD)");
   AK_CHECK_LAUNCH("ak_scan1_bwd(gD)");
   return AK_OK;
+}
+
+extern "C" int ak_scan1_bwd(float* gdA, float* gdBx, float* gC, float* gD, float* gx, void* workspace,
+                            size_t ws_bytes, const float* dA, const float* dBx, const float* C, const float* D,
+                            const float* x, const float* gy, int64_t B, int64_t L, int64_t d, void* stream) {
+  return ak_scan1_bwd_ex(gdA, gdBx, gC, gD, gx, workspace, ws_bytes, nullptr, dA, dBx, C, D, x, gy, B, L, d,
+                         stream);
 }

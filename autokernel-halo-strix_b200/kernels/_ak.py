@@ -54,6 +54,9 @@ SIGNATURES = {
     "ak_scan1_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ak_scan1_bwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_scan1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "ak_scan1_carries_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
+    "ak_scan1_fwd_ex": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "ak_scan1_bwd_ex": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ak_causal_conv1d_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _i, _vp],
     "ak_causal_conv1d_bwd_workspace_size": [_i64, _i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_causal_conv1d_bwd": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _i, _vp],
@@ -558,27 +561,40 @@ def _f32c(t: torch.Tensor) -> torch.Tensor:
     return t.contiguous()
 
 
-def scan1_fwd(dA, dBx, C, D, x) -> torch.Tensor:
+def scan1_fwd(dA, dBx, C, D, x, save_carries: bool = False):
+    """y (and, with save_carries, the chunk-start states the backward needs)."""
     dev = require_cuda(dA, dBx, C, D, x)
     dA, dBx, C, D, x = map(_f32c, (dA, dBx, C, D, x))
     if dA.dim() != 3:
         raise ValueError("dA must be 3D [batch, seq, d_inner]")
     B, L, d = dA.shape
     y = torch.empty_like(dA)
-    call("ak_scan1_fwd", ptr(y), ptr(dA), ptr(dBx), ptr(C), ptr(D), ptr(x), B, L, d, stream(dev))
-    return y
+    carries = None
+    if save_carries:
+        nbytes = _size_query("ak_scan1_carries_size", B, L, d)
+        carries = torch.empty(max(nbytes // 4, 1), dtype=torch.float32, device=dev)
+    call("ak_scan1_fwd_ex", ptr(y), ptr(carries), ptr(dA), ptr(dBx), ptr(C), ptr(D), ptr(x), B, L, d, stream(dev))
+    return (y, carries) if save_carries else y
 
 
-def scan1_bwd(dA, dBx, C, D, x, gy):
+def scan1_bwd(dA, dBx, C, D, x, gy, carries=None):
+    """(gdA, gdBx, gC, gD, gx); `carries` from scan1_fwd(save_carries=True) skips the pass that
+    re-derives the chunk-start states."""
     dev = require_cuda(dA, dBx, C, D, x, gy)
     dA, dBx, C, D, x, gy = map(_f32c, (dA, dBx, C, D, x, gy))
     B, L, d = dA.shape
     gdA, gdBx, gC, gx = (torch.empty_like(dA) for _ in range(4))
     gD = torch.empty(d, dtype=torch.float32, device=dev)
-    ws_bytes = _size_query("ak_scan1_bwd_workspace_size", B, L, d)
+    if carries is not None:
+        need = _size_query("ak_scan1_carries_size", B, L, d)
+        if carries.dtype != torch.float32 or not carries.is_contiguous() or carries.numel() * 4 < need:
+            raise ValueError("scan1_bwd: carries do not match this shape (use scan1_fwd(save_carries=True))")
+        ws_bytes = max(B * d * 4, 4)
+    else:
+        ws_bytes = _size_query("ak_scan1_bwd_workspace_size", B, L, d)
     ws = workspace(ws_bytes, dev)
-    call("ak_scan1_bwd", ptr(gdA), ptr(gdBx), ptr(gC), ptr(gD), ptr(gx), ptr(ws), ws_bytes, ptr(dA), ptr(dBx),
-         ptr(C), ptr(D), ptr(x), ptr(gy), B, L, d, stream(dev))
+    call("ak_scan1_bwd_ex", ptr(gdA), ptr(gdBx), ptr(gC), ptr(gD), ptr(gx), ptr(ws), ws_bytes, ptr(carries),
+         ptr(dA), ptr(dBx), ptr(C), ptr(D), ptr(x), ptr(gy), B, L, d, stream(dev))
     return gdA, gdBx, gC, gD, gx
 
 

@@ -176,29 +176,61 @@ def _(dA, dBx, C, D, x, grad_y):
             x.new_empty(x.shape)]
 
 
-@torch.library.custom_op("autokernel::selective_scan", mutates_args=())
-def selective_scan_op(dA: torch.Tensor, dBx: torch.Tensor, C: torch.Tensor, D: torch.Tensor,
-                      x: torch.Tensor) -> torch.Tensor:
-    return _ak.scan1_fwd(dA, dBx, C, D, x)
+# The forward also saves the 64-step chunk-start states, so the backward skips the pass that
+# re-derives them (two of its eleven tensor passes).  `autokernel::selective_scan` keeps the
+# reference's schema (one output) as a composite over `selective_scan_save`, which returns
+# (y, carries) and owns the autograd rule.
+@torch.library.custom_op("autokernel::selective_scan_bwd_carries", mutates_args=())
+def selective_scan_bwd_carries_op(dA: torch.Tensor, dBx: torch.Tensor, C: torch.Tensor, D: torch.Tensor,
+                                  x: torch.Tensor, grad_y: torch.Tensor, carries: torch.Tensor) -> List[torch.Tensor]:
+    return list(_ak.scan1_bwd(dA, dBx, C, D, x, grad_y.float(), carries=carries))
 
 
-@selective_scan_op.register_fake
+@selective_scan_bwd_carries_op.register_fake
+def _(dA, dBx, C, D, x, grad_y, carries):
+    return [dA.new_empty(dA.shape), dBx.new_empty(dBx.shape), C.new_empty(C.shape), D.new_empty(D.shape),
+            x.new_empty(x.shape)]
+
+
+_SCAN1_CHUNK = 64  # steps per saved chunk-start state (scan1.cu: kW * kSegB)
+
+
+@torch.library.custom_op("autokernel::selective_scan_save", mutates_args=())
+def selective_scan_save_op(dA: torch.Tensor, dBx: torch.Tensor, C: torch.Tensor, D: torch.Tensor,
+                           x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    return _ak.scan1_fwd(dA, dBx, C, D, x, save_carries=True)
+
+
+@selective_scan_save_op.register_fake
 def _(dA, dBx, C, D, x):
-    return dA.new_empty(dA.shape)
+    B, L, d = dA.shape
+    n = max(B * ((L + _SCAN1_CHUNK - 1) // _SCAN1_CHUNK) * d, 1)
+    return dA.new_empty(dA.shape), dA.new_empty((n,), dtype=torch.float32)
 
 
 def _selective_scan_setup(ctx, inputs, output):
     dA, dBx, C, D, x = inputs
-    ctx.save_for_backward(dA, dBx, C, D, x, output)
+    ctx.save_for_backward(dA, dBx, C, D, x, output[1])
 
 
-def _selective_scan_backward(ctx, grad_y):
-    dA, dBx, C, D, x, _y = ctx.saved_tensors
-    gdA, gdBx, gC, gD, gx = torch.ops.autokernel.selective_scan_bwd(dA, dBx, C, D, x, grad_y.contiguous())
+def _selective_scan_backward(ctx, grad_y, _grad_carries):
+    dA, dBx, C, D, x, carries = ctx.saved_tensors
+    gdA, gdBx, gC, gD, gx = torch.ops.autokernel.selective_scan_bwd_carries(dA, dBx, C, D, x, grad_y.contiguous(),
+                                                                          carries)
     return (gdA.to(dA.dtype), gdBx.to(dBx.dtype), gC.to(C.dtype), gD.to(D.dtype), gx.to(x.dtype))
 
 
-selective_scan_op.register_autograd(_selective_scan_backward, setup_context=_selective_scan_setup)
+selective_scan_save_op.register_autograd(_selective_scan_backward, setup_context=_selective_scan_setup)
+
+_scan_lib = torch.library.Library("autokernel", "FRAGMENT")
+_scan_lib.define("selective_scan(Tensor dA, Tensor dBx, Tensor C, Tensor D, Tensor x) -> Tensor")
+
+
+def _selective_scan_composite(dA, dBx, C, D, x):
+    return torch.ops.autokernel.selective_scan_save(dA, dBx, C, D, x)[0]
+
+
+_scan_lib.impl("selective_scan", _selective_scan_composite, "CompositeImplicitAutograd")
 
 
 # ---------------------------------------------------------------------------

@@ -516,9 +516,16 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         dBx, C, xx, gy = (torch.randn(Bsz, L, d, device=dev) for _ in range(4))
         Dv = torch.randn(d, device=dev)
         E = Bsz * L * d
-        timeit(lambda: _ak.scan1_fwd(dA, dBx, C, Dv, xx), 20 * E, "scan1_fwd_fp32_8x2048x1536", steps)
-        timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy), 36 * E, "scan1_bwd_fp32_8x2048x1536", steps)
-        del dA, dBx, C, xx, gy
+        # the product path (autokernel::selective_scan): the forward saves the 64-step chunk-start
+        # states (B * L/64 * d floats) and the backward reuses them
+        timeit(lambda: _ak.scan1_fwd(dA, dBx, C, Dv, xx, save_carries=True), 20 * E, "scan1_fwd_fp32_8x2048x1536",
+               steps)
+        _y, carries = _ak.scan1_fwd(dA, dBx, C, Dv, xx, save_carries=True)
+        timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy, carries=carries), 36 * E, "scan1_bwd_fp32_8x2048x1536",
+               steps)
+        # the reference-shaped C entry without saved states (re-derives them: +8 bytes per element)
+        timeit(lambda: _ak.scan1_bwd(dA, dBx, C, Dv, xx, gy), 36 * E, "scan1_bwd_nocarries_fp32_8x2048x1536", steps)
+        del dA, dBx, C, xx, gy, _y, carries
         torch.cuda.empty_cache()
 
     if want("ce_rows"):

@@ -211,6 +211,25 @@ AK_API int ak_scan1_bwd(float* gdA, float* gdBx, float* gC, float* gD, float* gx
                  const float* dBx, const float* C, const float* D, const float* x,
                  const float* gy, int64_t B, int64_t L, int64_t d, void* stream);
 
+/* Forward that also saves the backward's chunk-start states: carries (nullable)
+ * receives h at the start of every 64-step chunk, B * ceil(L/64) * d floats
+ * (ak_scan1_carries_size).  ak_scan1_fwd is this call with carries = NULL. */
+AK_API int ak_scan1_carries_size(int64_t B, int64_t L, int64_t d, size_t* bytes);
+AK_API int ak_scan1_fwd_ex(float* y, float* carries, const float* dA, const float* dBx,
+                           const float* C, const float* D, const float* x, int64_t B,
+                           int64_t L, int64_t d, void* stream);
+
+/* Backward given the carries saved by ak_scan1_fwd_ex (carries_in non-NULL): the
+ * pass that re-derives them from dA and dBx is skipped, and the workspace needs
+ * only B * d floats.  With carries_in = NULL it is ak_scan1_bwd.  The
+ * reference's sequential backward (kernels/hip/_torch_ops.py:335-389) keeps
+ * the forward states; this keeps one state per 64 steps. */
+AK_API int ak_scan1_bwd_ex(float* gdA, float* gdBx, float* gC, float* gD, float* gx,
+                           void* workspace, size_t ws_bytes, const float* carries_in,
+                           const float* dA, const float* dBx, const float* C,
+                           const float* D, const float* x, const float* gy, int64_t B,
+                           int64_t L, int64_t d, void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Mamba-style selective scan, layout (batch, dim, L), N states per channel
  * ------------------------------------------------------------------------ */

@@ -35,6 +35,32 @@ def test_scan1_shapes(B, L, d):
         assert_fp32_close(a, b, what=n)
 
 
+@pytest.mark.parametrize("B,L,d", [(2, 300, 40), (1, 1, 1), (3, 129, 33), (2, 2048, 1536)])
+def test_scan1_saved_carries_bit_exact(B, L, d):
+    """The forward's saved 64-step chunk-start states equal what the backward's own carry pass
+    derives, so the backward with saved carries is bit-identical to the one without; the
+    reference-shaped op `autokernel::selective_scan` takes the saving path."""
+    import kernels.hip._torch_ops  # noqa: F401
+    from kernels import _ak
+    g = torch.Generator().manual_seed(11 + L)
+    dA = (torch.rand(B, L, d, generator=g) * 0.5 + 0.5).to(DEV)
+    dBx, C, x, gy = (torch.randn(B, L, d, generator=g).to(DEV) for _ in range(4))
+    D = torch.randn(d, generator=g).to(DEV)
+    y0 = _ak.scan1_fwd(dA, dBx, C, D, x)
+    y1, carries = _ak.scan1_fwd(dA, dBx, C, D, x, save_carries=True)
+    assert torch.equal(y0, y1)
+    for a, b in zip(_ak.scan1_bwd(dA, dBx, C, D, x, gy), _ak.scan1_bwd(dA, dBx, C, D, x, gy, carries=carries)):
+        assert torch.equal(a, b)
+    ins = [t.clone().requires_grad_(True) for t in (dA, dBx, C, D, x)]
+    y = torch.ops.autokernel.selective_scan(*ins)
+    assert torch.equal(y, y0) and y.grad_fn is not None
+    y.backward(gy)
+    for t, r in zip(ins, _ak.scan1_bwd(dA, dBx, C, D, x, gy)):
+        assert torch.equal(t.grad, r)
+    with pytest.raises(ValueError):
+        _ak.scan1_bwd(dA, dBx, C, D, x, gy, carries=carries[:carries.numel() - 1])
+
+
 def _sscan_inputs(b, dim, L, N, groups, dtype, seed, with_z=True, with_D=True, with_bias=True):
     g = torch.Generator().manual_seed(seed)
     u = torch.randn(b, dim, L, generator=g).to(dtype)
