@@ -605,6 +605,24 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
     return res
 
 
+def profile_train_step(dev, micro_batch=16, seq=1024):
+    """One 124M training step (the CUDA-graph step the bench times) bracketed by
+    cudaProfilerStart / Stop after the eager warm-up, capture and one replay."""
+    from halo_training.hybrid_lm import HybridConfig
+    from halo_training.train_step import HybridTrainer, synthetic_batch
+    torch.cuda.set_device(dev)
+    cfg = HybridConfig()
+    tr = HybridTrainer(cfg, device=dev, use_kernels=True, seed=0, cuda_graph=True)
+    idx, tgt = synthetic_batch(micro_batch, seq, cfg.vocab_size, seed=1000, device=dev)
+    for _ in range(tr.graph_warmup + 2):
+        tr.step(idx, tgt)
+    torch.cuda.synchronize(dev)
+    torch.cuda.cudart().cudaProfilerStart()
+    tr.step(idx, tgt)
+    torch.cuda.synchronize(dev)
+    torch.cuda.cudart().cudaProfilerStop()
+
+
 def time_train(dev, steps, warmup, world, rank, micro_batch=16, seq=1024):
     """124M hybrid training step: kernels swapped in through the
     reference-facing API, bf16 autocast, AdamW, DDP over NCCL when world > 1."""
@@ -769,10 +787,16 @@ def main():
                     help="with --only-ops: divide the leading dimension of the softmax, fused_res, silu_gate, rope "
                          "and conv1d cases by this (small cases for ncu captures; names keep the full-size label)")
     ap.add_argument("--batch", type=int, default=0, help="override the headline batch (small-case profiling)")
+    ap.add_argument("--profile-train", action="store_true",
+                    help="profiling mode: warm the 124M training step up, then run exactly one step between "
+                         "cudaProfilerStart / Stop (for ncu --profile-from-start off); prints no JSON")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = setup_dist()
+    if args.profile_train:
+        profile_train_step(torch.device("cuda", local))
+        return
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
