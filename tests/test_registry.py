@@ -146,3 +146,47 @@ def test_swiglu_patterns(monkeypatch):
     assert rep["silu_gate_mul"]["modules_replaced"] == 1 and rep["fused_silu_gate_mul"]["modules_replaced"] == 1
     assert SiluGateMulPattern().matches("s", SwiGLU(), None) and not SiluGateMulPattern().matches("s", Block(), None)
     assert FusedSwiGLUPattern().matches("s", PackedSwiGLU(), None)
+
+
+def test_residual_chain_marking(monkeypatch):
+    """chain_residuals=True marks every fused block of an all-fused ModuleList but the last to
+    hand on ResidualPair(hidden, ffn_out); lists with another module, or a single block, are
+    left alone; off by default."""
+    from autokernel._patterns import ResidualPair, chain_residual_blocks
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+
+    class Net(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.layers = nn.ModuleList(TransformerBlock() for _ in range(4))
+            self.mixed = nn.ModuleList([TransformerBlock(), nn.Linear(16, 16)])
+            self.single = nn.ModuleList([TransformerBlock()])
+
+    m = autokernel.optimize(Net(), training=True)
+    assert not any(getattr(b, "_emit_pair", False) for b in m.modules())
+    m2 = autokernel.optimize(Net(), training=True, chain_residuals=True)
+    flags = [b._emit_pair for b in m2.layers]
+    assert flags == [True, True, True, False]
+    assert not m2.mixed[0]._emit_pair and not m2.single[0]._emit_pair
+    assert autokernel.report(m2)["patterns"]["residual_chain"]["modules_replaced"] == 3
+    assert chain_residual_blocks(nn.Sequential(nn.Linear(2, 2))) == 0
+    p = ResidualPair(torch.ones(2), torch.full((2,), 2.0))
+    assert torch.equal(p.materialize(), torch.full((2,), 3.0))
+
+
+def test_trainer_cuda_graph_flag_ignored_on_cpu():
+    """HybridTrainer(cuda_graph=True) on a CPU device runs the plain eager step."""
+    from halo_training.hybrid_lm import HybridConfig
+    from halo_training.train_step import HybridTrainer, eager_loss_fn, synthetic_batch
+    cfg = HybridConfig(vocab_size=64, d_model=32, n_layers=2, n_heads=2, n_kv_heads=1, ffn_hidden=64, d_state=4)
+    from oracle import hot_path_oracle as O
+
+    def scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False):
+        return O.selective_scan(u, delta, A, B, C, D, z, delta_bias, delta_softplus, dt=torch.float64)[0].to(u.dtype)
+
+    tr = HybridTrainer(cfg, device=torch.device("cpu"), use_kernels=False, cuda_graph=True, loss_fn=eager_loss_fn,
+                       scan_fn=scan)
+    assert tr.cuda_graph is False
+    idx, tgt = synthetic_batch(1, 16, cfg.vocab_size, seed=0, device="cpu")
+    l0 = tr.step(idx, tgt).item()
+    assert tr._graph is None and l0 > 0
