@@ -144,6 +144,18 @@ __device__ __forceinline__ void load_tile(float (&v)[ITEMS], const float* row, i
   }
 }
 
+// Same tile row as step pairs: (v[2j], v[2j+1]) from the lane's 16-byte loads.
+template <int ITEMS>
+__device__ __forceinline__ void load_tile2(float2 (&v)[ITEMS / 2], const float* row, int lane) {
+  const float4* r4 = reinterpret_cast<const float4*>(row) + lane;
+#pragma unroll
+  for (int q = 0; q < ITEMS / 4; ++q) {
+    const float4 f = r4[q * 32];
+    v[2 * q] = make_float2(f.x, f.y);
+    v[2 * q + 1] = make_float2(f.z, f.w);
+  }
+}
+
 // Issue (one thread, bulk path) or perform (all threads, unaligned rows) the
 // copy of the B and C tiles [N][CH] of the chunk starting at t0 into the
 // staging buffer ([2][N][CH] of T).
@@ -243,12 +255,18 @@ __device__ __forceinline__ void fwd_states(int n0, int N, const float (&dlt)[ITE
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     const float A2 = __shfl_sync(0xffffffffu, A_l, n0 + k) * kLog2e;  // lane n holds A[d, n]
-    float Bv[ITEMS];
-    load_tile<ITEMS>(Bv, tile + (n0 + k) * CH, lane);
+    float2 Bv[ITEMS / 2];
+    load_tile2<ITEMS>(Bv, tile + (n0 + k) * CH, lane);
+    const float2 A22 = make_float2(A2, A2);
+    // step pairs as paired fp32 instructions (exact per element)
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      a[k][i] = ex2(dlt[i] * A2);
-      h[k][i] = du[i] * Bv[i];
+    for (int j = 0; j < ITEMS / 2; ++j) {
+      const float2 t = __fmul2_rn(make_float2(dlt[2 * j], dlt[2 * j + 1]), A22);
+      a[k][2 * j] = ex2(t.x);
+      a[k][2 * j + 1] = ex2(t.y);
+      const float2 hv = __fmul2_rn(make_float2(du[2 * j], du[2 * j + 1]), Bv[j]);
+      h[k][2 * j] = hv.x;
+      h[k][2 * j + 1] = hv.y;
     }
     P[k] = ex2(S * A2);  // = prod of the lane's a
   }
@@ -282,12 +300,16 @@ __device__ __forceinline__ void fwd_states(int n0, int N, const float (&dlt)[ITE
     if (lane == 0) { Pe = 1.f; He = 0.f; }
     const float newc = __shfl_sync(0xffffffffu, fmaf(P[k], carry, H[k]), 31);
     float hh = fmaf(Pe, carry, He);
-    float Cv[ITEMS];
-    load_tile<ITEMS>(Cv, tile + (N + n0 + k) * CH, lane);
+    float2 Cv[ITEMS / 2];
+    load_tile2<ITEMS>(Cv, tile + (N + n0 + k) * CH, lane);
 #pragma unroll
-    for (int i = 0; i < ITEMS; ++i) {
-      hh = fmaf(a[k][i], hh, h[k][i]);
-      y[i] = fmaf(Cv[i], hh, y[i]);
+    for (int j = 0; j < ITEMS / 2; ++j) {
+      float2 hv;
+      hv.x = hh = fmaf(a[k][2 * j], hh, h[k][2 * j]);
+      hv.y = hh = fmaf(a[k][2 * j + 1], hh, h[k][2 * j + 1]);
+      const float2 yv = __ffma2_rn(Cv[j], hv, make_float2(y[2 * j], y[2 * j + 1]));
+      y[2 * j] = yv.x;
+      y[2 * j + 1] = yv.y;
     }
     if (save != nullptr) save[n0 + k] = hh;
     if (lane == 0) carry_row[n0 + k] = newc;
@@ -415,8 +437,8 @@ sscan_bwd_kernel(SsParams p) {
   const int N = p.N, L = p.L;
   T* stage = reinterpret_cast<T*>(smem + 128);
   float* tile = reinterpret_cast<float*>(smem + 128 + stage_bytes<T, CH>(N));
-  float* sdB = tile + 2 * N * CH;  // [N][ITEMS][32]
-  float* sdC = sdB + N * CH;       // [N][ITEMS][32]
+  float* sdB = tile + 2 * N * CH;  // [N][ITEMS/2][32] float2 (step pairs)
+  float* sdC = sdB + N * CH;       // [N][ITEMS/2][32] float2
   const int cpc = p.nw * p.cpw;
   float* sg = sdC + N * CH;        // adjoint carries [cpc][N] (pre-multiplied by a)
   float* sdA = sg + cpc * N;       // dA partials [cpc][N]
@@ -476,9 +498,20 @@ sscan_bwd_kernel(SsParams p) {
 #pragma unroll
         for (int i = 0; i < ITEMS; ++i) dy[i] *= zz[i] * sigmoid_f(zz[i]);
       }
-      float yacc[ITEMS], ddl[ITEMS], duacc[ITEMS];
+      // Step pairs (2j, 2j+1) as float2: the per-step products and accumulations below run as
+      // paired fp32 instructions (__fmul2_rn / __ffma2_rn / __fadd2_rn, exact per element), only
+      // the sequential chains and the ex2 stay scalar.
+      constexpr int P = ITEMS / 2;
+      float2 uu2[P], dlt2[P], dy2[P], yacc2[P], ddl2[P], duacc2[P];
 #pragma unroll
-      for (int i = 0; i < ITEMS; ++i) { yacc[i] = Dd * uu[i]; ddl[i] = 0.f; duacc[i] = dy[i] * Dd; }
+      for (int j = 0; j < P; ++j) {
+        uu2[j] = make_float2(uu[2 * j], uu[2 * j + 1]);
+        dlt2[j] = make_float2(dlt[2 * j], dlt[2 * j + 1]);
+        dy2[j] = make_float2(dy[2 * j], dy[2 * j + 1]);
+        yacc2[j] = make_float2(Dd * uu[2 * j], Dd * uu[2 * j + 1]);
+        ddl2[j] = make_float2(0.f, 0.f);
+        duacc2[j] = make_float2(dy[2 * j] * Dd, dy[2 * j + 1] * Dd);
+      }
       const float Sr = S - dlt[0];  // sum of delta' over the lane's steps 1..ITEMS-1
       // lane n holds A[d, n] and the saved chunk-start state n: one load each per
       // channel and chunk, broadcast by shuffle inside the state loop
@@ -493,69 +526,102 @@ sscan_bwd_kernel(SsParams p) {
         const int n = nn + nstart < N ? nn + nstart : nn + nstart - N;
         const float An = __shfl_sync(0xffffffffu, A_l, n);
         const float A2 = An * kLog2e;
-        float a[ITEMS], h[ITEMS], Bv[ITEMS], Cv[ITEMS];
-        load_tile<ITEMS>(Bv, tile + n * CH, lane);
-        load_tile<ITEMS>(Cv, tile + (N + n) * CH, lane);
+        float2 a2[P], h2[P], Bv2[P], Cv2[P];
+        load_tile2<ITEMS>(Bv2, tile + n * CH, lane);
+        load_tile2<ITEMS>(Cv2, tile + (N + n) * CH, lane);
         // ---- forward recompute of the states inside the chunk
+        const float2 A22 = make_float2(A2, A2);
 #pragma unroll
-        for (int i = 0; i < ITEMS; ++i) {
-          a[i] = ex2(dlt[i] * A2);
-          h[i] = dlt[i] * uu[i] * Bv[i];
+        for (int j = 0; j < P; ++j) {
+          const float2 t = __fmul2_rn(dlt2[j], A22);
+          a2[j] = make_float2(ex2(t.x), ex2(t.y));
+          h2[j] = __fmul2_rn(__fmul2_rn(dlt2[j], uu2[j]), Bv2[j]);
         }
-        float H = h[0];
+        float H = h2[0].x;
+        H = fmaf(a2[0].y, H, h2[0].y);
 #pragma unroll
-        for (int i = 1; i < ITEMS; ++i) H = fmaf(a[i], H, h[i]);
-        float P = ex2(S * A2);
+        for (int j = 1; j < P; ++j) {
+          H = fmaf(a2[j].x, H, h2[j].x);
+          H = fmaf(a2[j].y, H, h2[j].y);
+        }
+        float Pp = ex2(S * A2);
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
-          const float Pp = __shfl_up_sync(0xffffffffu, P, off);
-          const float Hp = __shfl_up_sync(0xffffffffu, H, off);
-          if (lane >= off) { H = fmaf(P, Hp, H); P *= Pp; }
+          const float Pu = __shfl_up_sync(0xffffffffu, Pp, off);
+          const float Hu = __shfl_up_sync(0xffffffffu, H, off);
+          if (lane >= off) { H = fmaf(Pp, Hu, H); Pp *= Pu; }
         }
         const float hc = __shfl_sync(0xffffffffu, hc_l, n);
-        float Pe = __shfl_up_sync(0xffffffffu, P, 1);
+        float Pe = __shfl_up_sync(0xffffffffu, Pp, 1);
         float He = __shfl_up_sync(0xffffffffu, H, 1);
         if (lane == 0) { Pe = 1.f; He = 0.f; }
         const float hin = fmaf(Pe, hc, He);
+        float2 hp2[P];  // the state before each step: (h[2j-1], h[2j]) with h[-1] = hin
         {
           float hh = hin;
 #pragma unroll
-          for (int i = 0; i < ITEMS; ++i) {
-            hh = fmaf(a[i], hh, h[i]);
-            h[i] = hh;
-            yacc[i] = fmaf(Cv[i], hh, yacc[i]);
+          for (int j = 0; j < P; ++j) {
+            hp2[j].x = hh;
+            hh = fmaf(a2[j].x, hh, h2[j].x);
+            h2[j].x = hh;
+            hp2[j].y = hh;
+            hh = fmaf(a2[j].y, hh, h2[j].y);
+            h2[j].y = hh;
+            yacc2[j] = __ffma2_rn(Cv2[j], h2[j], yacc2[j]);
           }
         }
         // ---- reverse scan of the adjoint g_t = dy_t C_t + a_{t+1} g_{t+1}
-        const float a_next_lane = __shfl_down_sync(0xffffffffu, a[0], 1);
-        const float ra_last = (lane == 31) ? 1.f : a_next_lane;
-        float G = dy[ITEMS - 1] * Cv[ITEMS - 1];
+        float2 dyC2[P];
 #pragma unroll
-        for (int i = ITEMS - 2; i >= 0; --i) G = fmaf(a[i + 1], G, dy[i] * Cv[i]);
+        for (int j = 0; j < P; ++j) dyC2[j] = __fmul2_rn(dy2[j], Cv2[j]);
+        const float a_next_lane = __shfl_down_sync(0xffffffffu, a2[0].x, 1);
+        const float ra_last = (lane == 31) ? 1.f : a_next_lane;
+        float G = dyC2[P - 1].y;
+        G = fmaf(a2[P - 1].y, G, dyC2[P - 1].x);
+#pragma unroll
+        for (int j = P - 2; j >= 0; --j) {
+          G = fmaf(a2[j + 1].x, G, dyC2[j].y);
+          G = fmaf(a2[j].y, G, dyC2[j].x);
+        }
         float Q = ex2(Sr * A2) * ra_last;  // = prod of the lane's a_{t+1}
         scan_down(Q, G, lane);
         const float gc = sg[cl * N + n];  // a_{t0+CH} * g_{t0+CH}
         const float Qd = __shfl_down_sync(0xffffffffu, Q, 1);
         const float Gd = __shfl_down_sync(0xffffffffu, G, 1);
-        const float gfirst0 = __shfl_sync(0xffffffffu, a[0] * fmaf(Q, gc, G), 0);
+        const float gfirst0 = __shfl_sync(0xffffffffu, a2[0].x * fmaf(Q, gc, G), 0);
         float gg = (lane == 31) ? gc : fmaf(Qd, gc, Gd);
-        float dAl = 0.f;
-        float gsv[ITEMS];  // the adjoint per step, for the dB contribution below
+        float2 gsv2[P];  // the adjoint per step
+        gg = fmaf(ra_last, gg, dyC2[P - 1].y);
+        gsv2[P - 1].y = gg;
+        gg = fmaf(a2[P - 1].y, gg, dyC2[P - 1].x);
+        gsv2[P - 1].x = gg;
 #pragma unroll
-        for (int i = ITEMS - 1; i >= 0; --i) {
-          const float ra = (i == ITEMS - 1) ? ra_last : a[i + 1];
-          gg = fmaf(ra, gg, dy[i] * Cv[i]);
-          const float hp = (i > 0) ? h[i - 1] : hin;
-          const float ea = gg * hp * a[i];  // dL/d(delta' A) of step i
-          dAl = fmaf(ea, dlt[i], dAl);
-          const float gB = gg * Bv[i];
-          ddl[i] = fmaf(ea, An, fmaf(gB, uu[i], ddl[i]));
-          duacc[i] = fmaf(gB, dlt[i], duacc[i]);
-          gsv[i] = gg;
+        for (int j = P - 2; j >= 0; --j) {
+          gg = fmaf(a2[j + 1].x, gg, dyC2[j].y);
+          gsv2[j].y = gg;
+          gg = fmaf(a2[j].y, gg, dyC2[j].x);
+          gsv2[j].x = gg;
         }
+        const float2 An2 = make_float2(An, An);
+        float2 dAl2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = P - 1; j >= 0; --j) {
+          const float2 ea = __fmul2_rn(__fmul2_rn(gsv2[j], hp2[j]), a2[j]);  // dL/d(delta' A) per step
+          dAl2 = __ffma2_rn(ea, dlt2[j], dAl2);
+          const float2 gB = __fmul2_rn(gsv2[j], Bv2[j]);
+          ddl2[j] = __ffma2_rn(ea, An2, __ffma2_rn(gB, uu2[j], ddl2[j]));
+          duacc2[j] = __ffma2_rn(gB, dlt2[j], duacc2[j]);
+        }
+        float dAl = dAl2.x + dAl2.y;
         // row n of sdB / sdC under its lock: a short plain read-modify-write section
-        // (no per-element atomics)
+        // (no per-element atomics); [n][pair][lane] float2 slots, one 64-bit access per pair
         {
+          float2 vb[P], vc[P];
+#pragma unroll
+          for (int j = 0; j < P; ++j) {
+            vb[j] = __fmul2_rn(__fmul2_rn(gsv2[j], dlt2[j]), uu2[j]);
+            vc[j] = __fmul2_rn(dy2[j], h2[j]);
+          }
           bool owned = true;
           if (lane == 0) {
             uint32_t spins = 0;
@@ -566,11 +632,12 @@ sscan_bwd_kernel(SsParams p) {
           }
           owned = __shfl_sync(0xffffffffu, owned, 0);  // also orders the lanes after lane 0's acquire
           if (owned) {
+            float2* rb = reinterpret_cast<float2*>(sdB) + n * (CH / 2) + lane;
+            float2* rc = reinterpret_cast<float2*>(sdC) + n * (CH / 2) + lane;
 #pragma unroll
-            for (int i = 0; i < ITEMS; ++i) {
-              const int si = n * CH + i * 32 + lane;  // [n][item][lane]: conflict-free
-              sdB[si] += gsv[i] * dlt[i] * uu[i];
-              sdC[si] += dy[i] * h[i];
+            for (int j = 0; j < P; ++j) {
+              rb[j * 32] = __fadd2_rn(rb[j * 32], vb[j]);
+              rc[j * 32] = __fadd2_rn(rc[j * 32], vc[j]);
             }
           }
           __syncwarp();  // every lane's row update is ordered before lane 0's release
@@ -579,6 +646,13 @@ sscan_bwd_kernel(SsParams p) {
         dAl = warp_sum(dAl);
         if (lane == n) dAl_keep += dAl;
         if (lane == 0) sg[cl * N + n] = gfirst0;
+      }
+      float yacc[ITEMS], ddl[ITEMS], duacc[ITEMS];
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        yacc[2 * j] = yacc2[j].x; yacc[2 * j + 1] = yacc2[j].y;
+        ddl[2 * j] = ddl2[j].x; ddl[2 * j + 1] = ddl2[j].y;
+        duacc[2 * j] = duacc2[j].x; duacc[2 * j + 1] = duacc2[j].y;
       }
       // ---- per-step outputs
       float dDl = 0.f, dbl = 0.f;
@@ -609,16 +683,17 @@ sscan_bwd_kernel(SsParams p) {
       if (lane < N) sdA[cl * N + lane] += dAl_keep;
     }
     __syncthreads();  // chunk consumed; sdB/sdC complete
-    // flush the [n][item][lane] accumulators: 4 consecutive steps per thread, v4 reductions
+    // flush the [n][pair][lane] float2 accumulators: 4 consecutive steps per thread, v4 reductions
     const int nq = N * CH / 4;
     for (int q = threadIdx.x; q < nq; q += blockDim.x) {
       const int n = q / (CH / 4), t = (q - n * (CH / 4)) * 4;
-      const int ln = t / ITEMS, i = t - ln * ITEMS;
-      const int base = n * CH + ln;
-      const float4 vb = make_float4(sdB[base + (i + 0) * 32], sdB[base + (i + 1) * 32], sdB[base + (i + 2) * 32],
-                                    sdB[base + (i + 3) * 32]);
-      const float4 vc = make_float4(sdC[base + (i + 0) * 32], sdC[base + (i + 1) * 32], sdC[base + (i + 2) * 32],
-                                    sdC[base + (i + 3) * 32]);
+      const int ln = t / ITEMS, i = t - ln * ITEMS;  // i even: pairs i/2 and i/2 + 1
+      const float2* b2 = reinterpret_cast<const float2*>(sdB) + n * (CH / 2) + ln;
+      const float2* c2 = reinterpret_cast<const float2*>(sdC) + n * (CH / 2) + ln;
+      const float2 b0 = b2[(i / 2) * 32], b1 = b2[(i / 2 + 1) * 32];
+      const float2 c0 = c2[(i / 2) * 32], c1 = c2[(i / 2 + 1) * 32];
+      const float4 vb = make_float4(b0.x, b0.y, b1.x, b1.y);
+      const float4 vc = make_float4(c0.x, c0.y, c1.x, c1.y);
       const int64_t off = (int64_t)n * L + t0 + t;
       if (t + 4 <= len && ((reinterpret_cast<uintptr_t>(dBg + off) & 15) == 0)) {
         red_add_v4(dBg + off, vb);
