@@ -58,11 +58,19 @@ __device__ __forceinline__ void ce_grad_vec(const float (&e)[VEC], bool is_t, in
       if (is_t && k == tk) g -= tsub;
       const float t = xc * p.inv_softcap;
       o[k] = g * (1.f - t * t);
-    } else {
-      o[k] = fmaf(ex2(fmaf(e[k], kLog2e, off)), sc_p, -sub);
     }
   }
   if constexpr (!CAP) {
+    // step pairs as paired fp32 (exact per element): (x log2e + off) -> ex2 -> (* sc_p - sub)
+    const float2 l2 = make_float2(kLog2e, kLog2e), off2 = make_float2(off, off);
+    const float2 sc2 = make_float2(sc_p, sc_p), ms2 = make_float2(-sub, -sub);
+#pragma unroll
+    for (int k = 0; k < VEC; k += 2) {
+      const float2 t = __ffma2_rn(make_float2(e[k], e[k + 1]), l2, off2);
+      const float2 r = __ffma2_rn(make_float2(ex2(t.x), ex2(t.y)), sc2, ms2);
+      o[k] = r.x;
+      o[k + 1] = r.y;
+    }
     if (is_t) sub_at<VEC>(o, tk, tsub);
   }
 }
@@ -107,12 +115,17 @@ ce_rows_fwd_kernel(float* __restrict__ losses, float* __restrict__ lse_out, floa
       const float mn = fmaxf(m, lm);
       if (mn != -INFINITY) {
         const float off = -mn * kLog2e;
-        float acc = s * ex2(fmaf(m, kLog2e, off));
+        // two running partial sums (paired FFMA for the exponent arguments, paired FADD)
+        const float2 l2 = make_float2(kLog2e, kLog2e), off2 = make_float2(off, off);
+        float2 acc2 = make_float2(s * ex2(fmaf(m, kLog2e, off)), 0.f);
 #pragma unroll
         for (int q = 0; q < kBatch; ++q)
 #pragma unroll
-          for (int k = 0; k < VEC; ++k) acc += ex2(fmaf(e[q][k], kLog2e, off));
-        s = acc;
+          for (int k = 0; k < VEC; k += 2) {
+            const float2 t = __ffma2_rn(make_float2(e[q][k], e[q][k + 1]), l2, off2);
+            acc2 = __fadd2_rn(acc2, make_float2(ex2(t.x), ex2(t.y)));
+          }
+        s = acc2.x + acc2.y;
         m = mn;
       }
     }
