@@ -66,3 +66,30 @@ def test_wrappers_refuse_cpu_tensors():
     import torch
     with pytest.raises(RuntimeError, match="CUDA"):
         _ak.rmsnorm_fwd(torch.zeros(2, 8), torch.ones(8))
+
+
+def test_new_entry_points_validate_before_any_cuda_call():
+    """Argument checks of the strided RoPE, the device-scalar scale and the collapsed scan with
+    saved states, all before any CUDA call (no GPU here)."""
+    lib = _ak.lib()
+    fake = ctypes.c_void_p(256)  # never dereferenced: every call below fails validation first
+    # ak_rope_strided: mode must be 1, -1 or 0
+    rc = lib.ak_rope_strided(fake, fake, fake, fake, 1, 2, 4, 8, 64, 8, 16, 64, 32, 8, 2, 1, None)
+    assert rc != 0 and b"mode" in lib.ak_last_error()
+    # ... and rotation modes need the tables (copy mode does not)
+    rc = lib.ak_rope_strided(fake, fake, None, None, 1, 2, 4, 7, 64, 8, 16, 64, 32, 8, 1, 1, None)
+    assert rc != 0 and b"D must be even" in lib.ak_last_error()
+    # ak_scale_by_device_scalar: negative size / missing scalar
+    assert lib.ak_scale_by_device_scalar(fake, -1, fake, 1, None) != 0
+    assert lib.ak_scale_by_device_scalar(fake, 10, None, 1, None) != 0
+    assert lib.ak_scale_by_device_scalar(None, 0, None, 1, None) == 0  # empty: nothing to do
+    # collapsed scan: carries size and the smaller workspace when they are given
+    n = ctypes.c_size_t(0)
+    assert lib.ak_scan1_carries_size(2, 300, 40, ctypes.byref(n)) == 0
+    assert n.value == 2 * 5 * 40 * 4  # one state per 64-step chunk
+    rc = lib.ak_scan1_bwd_ex(fake, fake, fake, fake, fake, fake, ctypes.c_size_t(2 * 40 * 4 - 4), fake, fake, fake,
+                             fake, fake, fake, fake, 2, 300, 40, None)
+    assert rc != 0 and b"workspace" in lib.ak_last_error()
+    rc = lib.ak_scan1_bwd_ex(fake, fake, fake, fake, fake, fake, ctypes.c_size_t(2 * 40 * 4), None, fake, fake,
+                             fake, fake, fake, fake, 2, 300, 40, None)  # no carries: needs them in the workspace
+    assert rc != 0 and b"workspace" in lib.ak_last_error()
