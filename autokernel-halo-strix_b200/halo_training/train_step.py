@@ -121,6 +121,10 @@ class HybridTrainer:
             with torch.cuda.graph(self._graph, stream=self._side_stream(), capture_error_mode="thread_local"):
                 self._static_loss = self._eager_step(*self._static)
         else:
+            if idx.shape != self._static[0].shape or targets.shape != self._static[1].shape:
+                raise ValueError(f"HybridTrainer(cuda_graph=True): the step was captured for inputs "
+                                 f"{tuple(self._static[0].shape)} / {tuple(self._static[1].shape)}, got "
+                                 f"{tuple(idx.shape)} / {tuple(targets.shape)}")
             self._static[0].copy_(idx, non_blocking=True)
             self._static[1].copy_(targets, non_blocking=True)
         self._graph.replay()

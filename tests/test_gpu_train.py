@@ -117,3 +117,5 @@ def test_cuda_graph_step_matches_eager():
     for a, b in zip(*curves):
         assert abs(a - b) < 2e-3 * max(1.0, abs(a)), (curves[0], curves[1])
     assert curves[1][-1] < curves[1][0]
+    with pytest.raises(ValueError, match="captured"):
+        tr.step(idx[:, :128], tgt[:, :128])  # a captured step keeps its input shape
