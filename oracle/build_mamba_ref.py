@@ -59,22 +59,36 @@ def load_built():
     return mod
 
 
-def main() -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--jobs", type=int, default=os.cpu_count() or 4)
-    args = ap.parse_args()
-    src = Path(args.reference) / "external" / "mamba" / "csrc" / "selective_scan"
+def default_reference() -> Path:
+    """$AK_REFERENCE, else a `reference` checkout beside this repository."""
+    return Path(os.environ.get("AK_REFERENCE", str(Path(__file__).resolve().parents[2] / "reference")))
+
+
+def build(reference: Path | None = None, jobs: int | None = None, verbose: bool = False) -> Path | None:
+    """Compile (incrementally, through ninja) the comparator into oracle/_ref/mamba/; returns the
+    module path, or None when the reference sources are not present."""
+    src = Path(reference or default_reference()) / "external" / "mamba" / "csrc" / "selective_scan"
     if not src.is_dir():
-        print(f"reference sources not found at {src}; nothing built", file=sys.stderr)
-        return
+        if verbose:
+            print(f"reference sources not found at {src}; nothing built", file=sys.stderr)
+        return None
     OUT.mkdir(parents=True, exist_ok=True)
-    os.environ.setdefault("MAX_JOBS", str(args.jobs))
+    os.environ.setdefault("MAX_JOBS", str(jobs or os.cpu_count() or 4))
     from torch.utils.cpp_extension import load
     load(name="selective_scan_cuda", sources=[str(src / s) for s in SOURCES],
          extra_cflags=["-O3", "-std=c++17"], extra_cuda_cflags=NVCC_FLAGS, extra_include_paths=[str(src)],
-         build_directory=str(OUT), verbose=True)
-    print("built", built_module_path())
+         build_directory=str(OUT), verbose=verbose)
+    return built_module_path()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=str(default_reference()))
+    ap.add_argument("--jobs", type=int, default=os.cpu_count() or 4)
+    args = ap.parse_args()
+    out = build(Path(args.reference), args.jobs, verbose=True)
+    if out is not None:
+        print("built", out)
 
 
 if __name__ == "__main__":

@@ -3,8 +3,8 @@ CPU code paths on seeded inputs.
 
     python tests/golden/make_golden.py [--reference PATH]
 
-Needs a checkout of joelhenwang/autokernel-halo-strix (default /root/reference,
-read-only is fine).  Every output stored here comes from the reference's code:
+Needs a checkout of joelhenwang/autokernel-halo-strix (default: $AK_REFERENCE, else a
+`reference` directory beside this repository; read-only is fine).  Every output stored here comes from the reference's code:
   rmsnorm.npz      reference.rmsnorm_ref (reference.py:26-29) + autograd, and the
                    fp32 branch of kernels/hip/_torch_ops._rmsnorm_backward (:73-97)
   softmax.npz      reference.softmax_ref (reference.py:15-17) + autograd
@@ -36,6 +36,7 @@ The fixtures are committed; the GPU box never needs the reference.
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 import types
 from pathlib import Path
@@ -75,7 +76,8 @@ def _np(t):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("AK_REFERENCE",
+                                                          str(Path(__file__).resolve().parents[3] / "reference")))
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.path.insert(0, str(ref))
