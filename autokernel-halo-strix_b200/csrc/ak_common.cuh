@@ -187,16 +187,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait on phase `parity`.  Gives up after ~kMaxSpins polls (far above
-// any legitimate copy latency), records AK_ERR_TIMEOUT in *err and returns
-// false so the kernel can finish instead of hanging the GPU.
+// Report a failed bounded wait through the caller's status word (nullable).
+// The word may live in device memory or in mapped pinned host memory (the
+// Python layer uses the latter, so the host reads it without a CUDA call); a
+// plain store plus a system-scope fence works for both, where an atomic on
+// host memory would need PCIe atomics.
+__device__ __forceinline__ void report_status(int* status, int code) {
+  if (status != nullptr) {
+    *reinterpret_cast<volatile int*>(status) = code;
+    __threadfence_system();
+  }
+}
+
+// Bounded wait on phase `parity`.  Gives up after `max_spins` polls (the
+// default is far above any legitimate copy latency), writes AK_ERR_TIMEOUT to
+// *status and returns false so the kernel can finish instead of hanging the GPU.
 constexpr uint32_t kMaxSpins = 1u << 22;
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
-  for (uint32_t i = 0; i < kMaxSpins; ++i) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status,
+                                                  uint32_t max_spins = kMaxSpins) {
+  for (uint32_t i = 0; i < max_spins; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if (i > 64) __nanosleep(32);
   }
-  if (err) atomicExch(err, (int)AK_ERR_TIMEOUT);
+  report_status(status, (int)AK_ERR_TIMEOUT);
   return false;
 }
 

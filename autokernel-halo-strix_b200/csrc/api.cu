@@ -35,3 +35,41 @@ int sm_count() {
 extern "C" int ak_version(void) { return (0 << 16) | (1 << 8) | 0; }
 
 extern "C" const char* ak_last_error(void) { return ak::g_last_error; }
+
+// ---------------------------------------------------------------------------
+// Device status words
+// ---------------------------------------------------------------------------
+namespace ak {
+namespace {
+
+// One thread arms an mbarrier that expects one arrival, then waits on it with
+// the given poll limit.  Nothing ever arrives, so the wait runs out, the status
+// word receives AK_ERR_TIMEOUT and the kernel returns.  No copy is in flight on
+// the barrier, so abandoning it is harmless.
+__global__ void bounded_wait_probe(int* status, uint32_t max_spins) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  mbar_fence_init();
+  mbar_wait_bounded(&bar, 0u, status, max_spins);
+}
+
+}  // namespace
+}  // namespace ak
+
+extern "C" int ak_status_device_pointer(void* host_word, void** dev_ptr) {
+  ak::clear_error();
+  AK_REQUIRE(host_word != nullptr && dev_ptr != nullptr, AK_ERR_ARG, "ak_status_device_pointer: null pointer");
+  AK_CUDA_TRY(cudaHostGetDevicePointer(dev_ptr, host_word, 0), "ak_status_device_pointer");
+  return AK_OK;
+}
+
+extern "C" int ak_test_bounded_wait(int* status, int max_spins, void* stream) {
+  ak::clear_error();
+  AK_REQUIRE(max_spins >= 1 && max_spins <= (1 << 20), AK_ERR_ARG,
+             "ak_test_bounded_wait: max_spins must be in [1, 2^20], got %d", max_spins);
+  cudaStream_t st = (cudaStream_t)stream;
+  ak::bounded_wait_probe<<<1, 32, 0, st>>>(status, (uint32_t)max_spins);
+  AK_CHECK_LAUNCH("ak_test_bounded_wait");
+  return AK_OK;
+}

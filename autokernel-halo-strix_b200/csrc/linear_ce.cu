@@ -43,8 +43,6 @@ constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;  // two accumulators
 constexpr int kTPitch = BM + 8;    // transpose staging row pitch (16-byte aligned rows)
 
-__device__ int g_lce_err;
-
 enum Epi : int { EPI_STATS = 0, EPI_GRAD = 1, EPI_STORE_BF16 = 2, EPI_STORE_F32 = 3 };
 
 struct GemmArgs {
@@ -65,6 +63,7 @@ struct GemmArgs {
   void* C;                  // [M][N]
   int64_t ldc;
   int accumulate;           // EPI_STORE_F32: C += acc
+  int* status;              // caller's status word: AK_ERR_TIMEOUT when a bounded wait gave up
 };
 
 // ---------------------------------------------------------------------------
@@ -182,7 +181,7 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int kb = 0; kb < ktiles; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-          mbar_wait_bounded(&empty[s], ph ^ 1u, &g_lce_err);
+          mbar_wait_bounded(&empty[s], ph ^ 1u, g.status);
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
           unsigned char* st = tiles + s * STAGE_BYTES;
           tma_load_2d(st, &tmA, g.a_k0 + kb * BK, mt * BM, &full[s]);
@@ -197,12 +196,12 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int it = 0, local = 0;
       for (int t = blockIdx.x; t < ntile_total; t += gridDim.x, ++local) {
         const int acc = local & 1;
-        mbar_wait_bounded(&tempty[acc], ((uint32_t)(local >> 1) & 1u) ^ 1u, &g_lce_err);
+        mbar_wait_bounded(&tempty[acc], ((uint32_t)(local >> 1) & 1u) ^ 1u, g.status);
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < ktiles; ++kb, ++it) {
           const int s = it % STAGES;
-          mbar_wait_bounded(&full[s], (uint32_t)(it / STAGES) & 1u, &g_lce_err);
+          mbar_wait_bounded(&full[s], (uint32_t)(it / STAGES) & 1u, g.status);
           tc_fence_after();
           const unsigned char* st = tiles + s * STAGE_BYTES;
           const uint64_t ad = smem_desc_sw128(st), bd = smem_desc_sw128(st + A_BYTES);
@@ -224,7 +223,7 @@ tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int t = blockIdx.x; t < ntile_total; t += gridDim.x, ++local) {
       const int mt = t % mtiles, nt = t / mtiles;
       const int acc = local & 1;
-      mbar_wait_bounded(&tfull[acc], (uint32_t)(local >> 1) & 1u, &g_lce_err);
+      mbar_wait_bounded(&tfull[acc], (uint32_t)(local >> 1) & 1u, g.status);
       tc_fence_after();
       const int row = mt * BM + rl;
       const bool rv = row < g.M;
@@ -572,7 +571,8 @@ Ws carve(void* base, int64_t N, int64_t D, int64_t V) {
 
 template <typename T>
 int run(float* loss, float* lse, void* dH, void* dW, const Ws& w, const void* H, const void* W,
-        const int64_t* labels, int64_t N, int64_t D, int64_t V, int64_t ignore_index, cudaStream_t st) {
+        const int64_t* labels, int64_t N, int64_t D, int64_t V, int64_t ignore_index, int* status,
+        cudaStream_t st) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   const int ntiles = (int)((V + BN - 1) / BN);
   // 0. K-major copies of W^T and H^T for the gradient GEMMs
@@ -591,6 +591,7 @@ int run(float* loss, float* lse, void* dH, void* dW, const Ws& w, const void* H,
   // 1. logits tiles -> per-row partial (max, sum exp)
   {
     GemmArgs g{};
+    g.status = status;
     g.M = (int)N; g.N = (int)V; g.K = (int)D;
     g.part = w.part; g.tlogit = w.tlogit; g.labels = labels; g.ignore_index = ignore_index;
     if ((rc = launch_gemm<T, EPI_STATS>(tH, tW, g, st))) return rc;
@@ -610,6 +611,7 @@ int run(float* loss, float* lse, void* dH, void* dW, const Ws& w, const void* H,
     if ((rc = make_tmap(&tGT, w.GT, V, nr, BM, bf16))) return rc;
     {
       GemmArgs g{};
+    g.status = status;
       g.M = (int)nr; g.N = (int)V; g.K = (int)D;
       g.labels = labels + r0; g.ignore_index = ignore_index;
       g.lse = lse + r0; g.scale = w.inv_valid;
@@ -618,12 +620,14 @@ int run(float* loss, float* lse, void* dH, void* dW, const Ws& w, const void* H,
     }
     if (dH) {  // dH[r0:r0+nr] = G W  (A = G [nr, V], B = W^T [D, V])
       GemmArgs g{};
+    g.status = status;
       g.M = (int)nr; g.N = (int)D; g.K = (int)V;
       g.C = static_cast<T*>(dH) + r0 * D; g.ldc = D;
       if ((rc = launch_gemm<T, EPI_STORE_BF16>(tG, tWT, g, st))) return rc;
     }
     if (dW) {  // dW += G^T H  (A = G^T [V, nr], B = H^T [D, N] columns r0..r0+nr)
       GemmArgs g{};
+    g.status = status;
       g.M = (int)V; g.N = (int)D; g.K = (int)nr; g.b_k0 = (int)r0;
       g.C = w.dWacc; g.ldc = D; g.accumulate = r0 > 0;
       if ((rc = launch_gemm<T, EPI_STORE_F32>(tGT, tHT, g, st))) return rc;
@@ -661,7 +665,7 @@ extern "C" int ak_linear_ce_workspace_size(int64_t N, int64_t D, int64_t V, size
 
 extern "C" int ak_linear_ce_fwdbwd(float* loss, float* lse, void* dH, void* dW, void* workspace, size_t ws_bytes,
                                    const void* H, const void* W, const int64_t* labels, int64_t N, int64_t D,
-                                   int64_t V, int64_t ignore_index, int dt, void* stream) {
+                                   int64_t V, int64_t ignore_index, int dt, int* status, void* stream) {
   clear_error();
   int rc = check_shape(N, D, V, dt);
   if (rc) return rc;
@@ -674,8 +678,8 @@ extern "C" int ak_linear_ce_fwdbwd(float* loss, float* lse, void* dH, void* dW, 
   void* base = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
   const Ws w = carve(base, N, D, V);
   cudaStream_t st = (cudaStream_t)stream;
-  if (dt == AK_BF16) return run<__nv_bfloat16>(loss, lse, dH, dW, w, H, W, labels, N, D, V, ignore_index, st);
-  return run<__half>(loss, lse, dH, dW, w, H, W, labels, N, D, V, ignore_index, st);
+  if (dt == AK_BF16) return run<__nv_bfloat16>(loss, lse, dH, dW, w, H, W, labels, N, D, V, ignore_index, status, st);
+  return run<__half>(loss, lse, dH, dW, w, H, W, labels, N, D, V, ignore_index, status, st);
 }
 
 extern "C" int ak_linear_ce_logits_grad_workspace_size(int64_t N, int64_t V, size_t* bytes) {
@@ -688,7 +692,7 @@ extern "C" int ak_linear_ce_logits_grad_workspace_size(int64_t N, int64_t V, siz
 
 extern "C" int ak_linear_ce_logits_grad(float* loss, float* lse, void* G, void* workspace, size_t ws_bytes,
                                         const void* H, const void* W, const int64_t* labels, int64_t N, int64_t D,
-                                        int64_t V, int64_t ignore_index, int dt, void* stream) {
+                                        int64_t V, int64_t ignore_index, int dt, int* status, void* stream) {
   clear_error();
   int rc = check_shape(N, D, V, dt);
   if (rc) return rc;
@@ -710,6 +714,7 @@ extern "C" int ak_linear_ce_logits_grad(float* loss, float* lse, void* G, void* 
   if ((rc = make_tmap(&tH, H, N, D, BM, bf16))) return rc;
   if ((rc = make_tmap(&tW, W, V, D, BN, bf16))) return rc;
   GemmArgs g{};
+    g.status = status;
   g.M = (int)N; g.N = (int)V; g.K = (int)D;
   g.part = part; g.tlogit = tlogit; g.labels = labels; g.ignore_index = ignore_index; g.G = G;
   if (bf16) rc = launch_gemm<__nv_bfloat16, EPI_STATS>(tH, tW, g, st);

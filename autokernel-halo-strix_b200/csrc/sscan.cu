@@ -51,8 +51,6 @@ static_assert(32 * kItems == kStateStride, "chunk must equal the state stride");
 constexpr int kFwdItems = 16;      // forward steps per lane when shared memory allows (chunk 512)
 constexpr int kFwdInterleave = 1;  // states interleaved per pass at 16 steps per lane (registers)
 
-__device__ int g_sscan_err;  // AK_ERR_TIMEOUT if a bounded wait gave up
-
 struct SsParams {
   const void* u;
   const void* delta;
@@ -76,6 +74,7 @@ struct SsParams {
   float* part;  // [batch][dim][N+2]
   int batch, dim, L, N, groups, dpg, nw, cpw, nsaved;
   int softplus, bulk, vec_io;
+  int* status;  // caller's status word: AK_ERR_TIMEOUT when a bounded wait gave up (nullable)
 };
 
 __device__ __forceinline__ float softplus_f(float x) { return x <= 20.f ? log1pf(__expf(x)) : x; }
@@ -211,7 +210,7 @@ __device__ __forceinline__ void fetch_chunk(const SsParams& p, T* stage, float* 
                                             int t0, int next_t0, const T* Bg, const T* Cg) {
   constexpr int CH = 32 * ITEMS;
   if (p.bulk) {
-    mbar_wait_bounded(bar, (uint32_t)(phase & 1), &g_sscan_err);
+    mbar_wait_bounded(bar, (uint32_t)(phase & 1), p.status);
   } else {
     stage_bc<T, CH>(p, stage, bar, t0, Bg, Cg, false);
     __syncthreads();
@@ -626,7 +625,7 @@ sscan_bwd_kernel(SsParams p) {
           if (lane == 0) {
             uint32_t spins = 0;
             while (lock_try_acquire(&slock[n]) != 0) {
-              if (++spins > kMaxSpins) { atomicExch(&g_sscan_err, (int)AK_ERR_TIMEOUT); owned = false; break; }
+              if (++spins > kMaxSpins) { report_status(p.status, (int)AK_ERR_TIMEOUT); owned = false; break; }
               if (spins > 16) __nanosleep(20);
             }
           }
@@ -791,7 +790,7 @@ extern "C" int ak_selective_scan_fwd(void* out, float* last_state, float* chunk_
                                      const void* delta, const float* A, const void* Bm, const void* Cm,
                                      const float* D, const void* z, const float* delta_bias, int delta_softplus,
                                      int64_t batch, int64_t dim, int64_t seqlen, int64_t dstate, int64_t groups,
-                                     int dt, void* stream) {
+                                     int dt, int* status, void* stream) {
   clear_error();
   int rc = validate(batch, dim, seqlen, dstate, groups, dt);
   if (rc) return rc;
@@ -806,6 +805,7 @@ extern "C" int ak_selective_scan_fwd(void* out, float* last_state, float* chunk_
   SsParams p{};
   p.u = u; p.delta = delta; p.A = A; p.Bm = Bm; p.Cm = Cm; p.D = D; p.z = z; p.bias = delta_bias;
   p.out = out; p.last_state = last_state; p.chunk_states = chunk_states;
+  p.status = status;
   p.batch = (int)batch; p.dim = (int)dim; p.L = (int)seqlen; p.N = (int)dstate; p.groups = (int)groups;
   p.dpg = (int)(dim / groups);
   p.softplus = delta_softplus ? 1 : 0;
@@ -847,7 +847,8 @@ extern "C" int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB
                                      const void* u, const void* delta, const float* A, const void* Bm,
                                      const void* Cm, const float* D, const void* z, const float* delta_bias,
                                      const float* chunk_states, int delta_softplus, int64_t batch, int64_t dim,
-                                     int64_t seqlen, int64_t dstate, int64_t groups, int dt, void* stream) {
+                                     int64_t seqlen, int64_t dstate, int64_t groups, int dt, int* status,
+                                     void* stream) {
   clear_error();
   int rc = validate(batch, dim, seqlen, dstate, groups, dt);
   if (rc) return rc;
@@ -877,6 +878,7 @@ extern "C" int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB
   p.u = u; p.delta = delta; p.A = A; p.Bm = Bm; p.Cm = Cm; p.D = D; p.z = z; p.bias = delta_bias;
   p.dout = dout; p.chunk_states_in = chunk_states;
   p.du = du; p.ddelta = ddelta; p.dz = dz;
+  p.status = status;
   float* ws = (float*)workspace;
   p.dB_acc = ws;
   p.dC_acc = ws + nbc;

@@ -48,9 +48,9 @@ SIGNATURES = {
     "ak_ce_rows_reduce": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _f, _vp],
     "ak_ce_inv_valid": [_vp, _vp, _i64, _i64, _vp],
     "ak_linear_ce_logits_grad_workspace_size": [_i64, _i64, ctypes.POINTER(_sz)],
-    "ak_linear_ce_logits_grad": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_linear_ce_logits_grad": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp, _vp],
     "ak_linear_ce_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
-    "ak_linear_ce_fwdbwd": [_vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp],
+    "ak_linear_ce_fwdbwd": [_vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp, _vp],
     "ak_scan1_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ak_scan1_bwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_scan1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
@@ -62,10 +62,12 @@ SIGNATURES = {
     "ak_causal_conv1d_bwd": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _i, _vp],
     "ak_selective_scan_state_stride": [],
     "ak_selective_scan_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
-                              _i64, _i64, _i64, _i64, _i64, _i, _vp],
+                              _i64, _i64, _i64, _i64, _i64, _i, _vp, _vp],
     "ak_selective_scan_bwd_workspace_size": [_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_selective_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp,
-                              _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64, _i64, _i, _vp],
+                              _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64, _i64, _i, _vp, _vp],
+    "ak_status_device_pointer": [_vp, ctypes.POINTER(_vp)],
+    "ak_test_bounded_wait": [_vp, _i, _vp],
 }
 
 
@@ -144,6 +146,74 @@ def _size_query(name: str, *dims: int) -> int:
     out = ctypes.c_size_t(0)
     call(name, *dims, ctypes.byref(out))
     return int(out.value)
+
+
+# ---------------------------------------------------------------------------
+# Device status words (bounded-wait timeouts)
+# ---------------------------------------------------------------------------
+AK_ERR_TIMEOUT = 5
+STATUS_SLOTS = ("selective_scan_fwd", "selective_scan_bwd", "linear_ce", "bounded_wait_test")
+
+
+class _StatusWords:
+    """One pinned host int32 per kernel family on one device.  The kernels write AK_ERR_TIMEOUT
+    into it through its device address when a bounded wait runs out, so the host reads a failure
+    without a CUDA call: the next call of the same family raises it, and `check_status` raises it
+    after synchronising."""
+
+    def __init__(self, device: torch.device):
+        self.host = torch.zeros(len(STATUS_SLOTS), dtype=torch.int32, pin_memory=True)
+        dev_ptr = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            call("ak_status_device_pointer", ctypes.c_void_p(self.host.data_ptr()), ctypes.byref(dev_ptr))
+        self.base = int(dev_ptr.value)
+
+    def raise_if_set(self, slots) -> None:
+        for i in slots:
+            code = int(self.host[i])
+            if code != 0:
+                self.host[i] = 0
+                raise AkError(f"{STATUS_SLOTS[i]}: a bounded device-side wait gave up (status {code}, "
+                              "AK_ERR_TIMEOUT); the outputs of that call are invalid")
+
+
+_status: dict = {}
+
+
+def _status_words(device: torch.device) -> _StatusWords:
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    sw = _status.get(key)
+    if sw is None:
+        with _lock:
+            sw = _status.get(key)
+            if sw is None:
+                sw = _status[key] = _StatusWords(torch.device("cuda", key))
+    return sw
+
+
+def status_ptr(device: torch.device, slot: str):
+    """Device address of the status word of `slot`; raises first if an earlier call of that
+    family reported a timeout."""
+    sw = _status_words(device)
+    i = STATUS_SLOTS.index(slot)
+    sw.raise_if_set((i,))
+    return ctypes.c_void_p(sw.base + 4 * i)
+
+
+def check_status(device: Optional[torch.device] = None, synchronize: bool = True) -> None:
+    """Raise AkError if any kernel on `device` (default: current) reported a bounded-wait
+    timeout; with synchronize=True every call issued so far is covered."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if synchronize:
+        torch.cuda.synchronize(dev)
+    _status_words(dev).raise_if_set(range(len(STATUS_SLOTS)))
+
+
+def test_bounded_wait(device: torch.device, max_spins: int = 1000) -> None:
+    """Run the library's bounded-wait probe (a wait nothing completes), then check the status."""
+    dev = torch.device(device)
+    call("ak_test_bounded_wait", status_ptr(dev, "bounded_wait_test"), int(max_spins), stream(dev))
+    check_status(dev, synchronize=True)
 
 
 # ---------------------------------------------------------------------------
@@ -529,7 +599,7 @@ def linear_ce_logits_grad(hidden, weight, labels, ignore_index=-100):
     ws_bytes = _size_query("ak_linear_ce_logits_grad_workspace_size", N, V)
     ws = workspace(ws_bytes, dev)
     call("ak_linear_ce_logits_grad", ptr(loss), ptr(lse), ptr(G), ptr(ws), ws_bytes, ptr(h), ptr(w), ptr(lab), N, D,
-         V, int(ignore_index), dtype_code(h), stream(dev))
+         V, int(ignore_index), dtype_code(h), status_ptr(dev, "linear_ce"), stream(dev))
     return loss, lse, G
 
 
@@ -548,7 +618,7 @@ def linear_ce_fwdbwd(hidden, weight, labels, ignore_index=-100, need_dh=True, ne
     ws_bytes = _size_query("ak_linear_ce_workspace_size", N, D, V)
     ws = workspace(ws_bytes, dev)
     call("ak_linear_ce_fwdbwd", ptr(loss), ptr(lse), ptr(dH), ptr(dW), ptr(ws), ws_bytes, ptr(h), ptr(w), ptr(lab),
-         N, D, V, int(ignore_index), dtype_code(h), stream(dev))
+         N, D, V, int(ignore_index), dtype_code(h), status_ptr(dev, "linear_ce"), stream(dev))
     return loss, lse, dH, dW
 
 
@@ -639,7 +709,8 @@ def selective_scan_fwd(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta
     nsaved = (L + state_stride() - 1) // state_stride()
     states = torch.empty(batch, dim, nsaved, N, **f32) if save_states else None
     call("ak_selective_scan_fwd", ptr(out), ptr(last), ptr(states), ptr(u), ptr(delta), ptr(A), ptr(B4), ptr(C4),
-         ptr(D), ptr(z), ptr(delta_bias), int(bool(delta_softplus)), batch, dim, L, N, G, dtype_code(u), stream(dev))
+         ptr(D), ptr(z), ptr(delta_bias), int(bool(delta_softplus)), batch, dim, L, N, G, dtype_code(u),
+         status_ptr(dev, "selective_scan_fwd"), stream(dev))
     return out, last, states
 
 
@@ -673,7 +744,7 @@ def selective_scan_bwd(dout, u, delta, A, B, C, D, z, delta_bias, delta_softplus
     call("ak_selective_scan_bwd", ptr(du), ptr(ddelta), ptr(dA), ptr(dB), ptr(dC), ptr(dD), ptr(dz), ptr(dbias),
          ptr(ws), ws_bytes, ptr(dout), ptr(u), ptr(delta), ptr(A), ptr(B4), ptr(C4), ptr(D), ptr(z),
          ptr(delta_bias), ptr(chunk_states), int(bool(delta_softplus)), batch, dim, L, N, G, dtype_code(u),
-         stream(dev))
+         status_ptr(dev, "selective_scan_bwd"), stream(dev))
     if B.dim() == 3:
         dB = dB.squeeze(1)
     if C.dim() == 3:

@@ -45,6 +45,13 @@ NCU_TRAFFIC_BYTES = {
     # x2 for B=8 (every input, output and B/C tile is per batch row, so traffic is linear in B)
     "sscan_bwd": 2 * (106_179_072 + 42_633_984),
 }
+# smsp__inst_executed.sum (warp-instructions) per launch of the scan backward at the headline
+# shape, from the same kind of capture (B=4, doubled: the instruction count is linear in B).
+# The backward is issue-bound, so its roofline is the SM's issue rate: 148 SMs x 4 schedulers x
+# one warp-instruction per clock at the clock sampled during the timed region.
+NCU_WARP_INST = {
+    "sscan_bwd": 2 * 343_400_000,
+}
 
 
 # ----------------------------------------------------------------------------
@@ -677,6 +684,11 @@ def run_ours(args, world, rank, local):
     fwd_avg = statistics.mean(fwd_ms)
     achieved = bwd_b / (bwd_avg / 1e3) / 1e9
     traffic = NCU_TRAFFIC_BYTES.get("sscan_bwd")
+    inst = NCU_WARP_INST["sscan_bwd"] * cfg["batch"] / 8
+    sm_mhz = clocks.get("sm_mhz") or 1965.0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    issue_peak = sms * 4 * sm_mhz * 1e6 / 1e9  # G warp-instructions / s
+    issue_achieved = inst / (bwd_avg / 1e3) / 1e9
     if args.no_e2e:
         e2e_ms, h2d, d2h, e2e_value = float("nan"), 0, 0, None
     else:
@@ -685,6 +697,7 @@ def run_ours(args, world, rank, local):
         e2e_value = round(world * (fwd_b + bwd_b) / (e2e_ms / 1e3) / 1e9, 2)
     ops = time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak) if (rank == 0 and not args.no_ops) else None
     train = None if args.no_train else time_train(dev, args.train_steps, 3, world, rank)
+    sharded = None
     if rank != 0:
         return
     line = {
@@ -708,10 +721,16 @@ def run_ours(args, world, rank, local):
                    "fwd_ms": round(fwd_avg, 4), "bwd_ms": round(bwd_avg, 4),
                    "fwd_GBps": round(fwd_b / (fwd_avg / 1e3) / 1e9, 1),
                    "sfu_exp2_per_pass": cfg["batch"] * cfg["dim"] * cfg["L"] * cfg["N"]},
-        "roofline": {"kernel": "selective_scan_bwd (C-ABI call)", "bound": "hbm", "achieved": round(achieved, 1),
-                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                     "traffic": traffic, "peak_kind": peak_kind,
-                     "algorithmic_bytes_per_launch": bwd_b},
+        "roofline": {"kernel": "selective_scan_bwd (C-ABI call)", "bound": "issue",
+                     "achieved": round(issue_achieved, 1), "peak": round(issue_peak, 1),
+                     "unit": "G warp-instructions/s", "frac": round(issue_achieved / issue_peak, 4),
+                     "warp_instructions_per_launch": int(inst),
+                     "issue_peak_def": f"{sms} SMs x 4 schedulers x 1 warp-instruction/clk at the sampled "
+                                       f"median SM clock {sm_mhz:.0f} MHz; instructions from ncu "
+                                       "smsp__inst_executed.sum",
+                     "hbm": {"achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                             "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind},
+                     "traffic": traffic, "algorithmic_bytes_per_launch": bwd_b},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
                 "api": "kernels.mamba_scan.selective_scan_fn + autograd backward, pinned host inputs, "
@@ -728,6 +747,23 @@ def run_ours(args, world, rank, local):
         line["cpu_baseline"] = cpu_sscan_sample()
         if not args.no_ops:
             line["cpu_baseline"]["ops"] = cpu_ops_sample()["ops"]
+    if sharded is not None:
+        line["sharded_ops"] = sharded
+    # last key, so a tail of the output still carries every op's roofline fraction
+    summary = {}
+    if ops is not None:
+        for k, v in ops.items():
+            if isinstance(v, dict):
+                f = v.get("frac", v.get("frac_bf16"))
+                if f is not None:
+                    summary[k] = f
+    if train is not None:
+        summary["train_tok_s"] = train["tok_s"]
+    if sharded is not None:
+        for k, v in sharded.items():
+            if isinstance(v, dict) and "efficiency" in v:
+                summary[f"sharded_eff_{k}"] = v["efficiency"]
+    line["ops_summary"] = summary
     emit(line)
 
 

@@ -14,6 +14,13 @@
  *   - Element types are given by ak_dtype codes.
  *   - Functions keep no mutable global state beyond a per-device attribute
  *     cache, so they are reentrant and thread-safe.
+ *   - Kernels that wait on asynchronous copies or on each other (the mamba
+ *     scan and the tensor-core linear + CE) bound every wait.  When a wait runs
+ *     out they write AK_ERR_TIMEOUT to the caller's `status` word (nullable; a
+ *     device int, or a pinned host int whose device address comes from
+ *     ak_status_device_pointer) and finish without hanging; their outputs are
+ *     then invalid.  The word is only ever written on failure, so the caller
+ *     zeroes it once and reads it after the stream has passed the call.
  *
  * Each declaration names the reference interface it replaces, as a path inside
  * the joelhenwang/autokernel-halo-strix project.
@@ -50,6 +57,19 @@ typedef enum {
 AK_API int ak_version(void);
 /* Message for the last failing call on this thread ("" if none). */
 AK_API const char* ak_last_error(void);
+
+/* Device address of a pinned (cudaHostAlloc) host word, for use as the
+ * `status` argument: kernels then report straight into host memory, so the
+ * host can read a timeout without a CUDA call or a stream sync.  No
+ * counterpart in the reference, whose kernels have no bounded waits; it turns
+ * the device-side failure into the RuntimeError its TORCH_CHECKs raise
+ * (kernels/hip/rmsnorm.py:119-123). */
+AK_API int ak_status_device_pointer(void* host_word, void** dev_ptr);
+
+/* Test hook for the status path: launches one thread that waits on an
+ * mbarrier nothing completes, with a limit of max_spins polls (1..2^20), so
+ * the wait runs out and *status receives AK_ERR_TIMEOUT.  Asynchronous. */
+AK_API int ak_test_bounded_wait(int* status, int max_spins, void* stream);
 
 /* ------------------------------------------------------------------------ *
  * RMSNorm
@@ -172,7 +192,7 @@ AK_API int ak_linear_ce_workspace_size(int64_t N, int64_t D, int64_t V, size_t* 
 AK_API int ak_linear_ce_fwdbwd(float* loss, float* lse, void* dH, void* dW, void* workspace,
                    size_t ws_bytes, const void* H, const void* W, const int64_t* labels,
                    int64_t N, int64_t D, int64_t V, int64_t ignore_index, int dt,
-                   void* stream);
+                   int* status, void* stream);
 
 /* Workspace bytes for ak_linear_ce_logits_grad. */
 AK_API int ak_linear_ce_logits_grad_workspace_size(int64_t N, int64_t V, size_t* bytes);
@@ -187,7 +207,7 @@ AK_API int ak_linear_ce_logits_grad_workspace_size(int64_t N, int64_t V, size_t*
 AK_API int ak_linear_ce_logits_grad(float* loss, float* lse, void* G, void* workspace,
                    size_t ws_bytes, const void* H, const void* W, const int64_t* labels,
                    int64_t N, int64_t D, int64_t V, int64_t ignore_index, int dt,
-                   void* stream);
+                   int* status, void* stream);
 
 /* ------------------------------------------------------------------------ *
  * Collapsed (single-state) selective scan, fp32, layout (B, L, d)
@@ -256,7 +276,7 @@ AK_API int ak_selective_scan_fwd(void* out, float* last_state, float* chunk_stat
                           const void* z, const float* delta_bias,
                           int delta_softplus, int64_t batch, int64_t dim,
                           int64_t seqlen, int64_t dstate, int64_t groups, int dt,
-                          void* stream);
+                          int* status, void* stream);
 
 AK_API int ak_selective_scan_bwd_workspace_size(int64_t batch, int64_t dim,
                                          int64_t seqlen, int64_t dstate,
@@ -275,7 +295,8 @@ AK_API int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB, vo
                           const void* z, const float* delta_bias,
                           const float* chunk_states, int delta_softplus,
                           int64_t batch, int64_t dim, int64_t seqlen,
-                          int64_t dstate, int64_t groups, int dt, void* stream);
+                          int64_t dstate, int64_t groups, int dt, int* status,
+                          void* stream);
 
 /* ---- Fused residual add + RMSNorm (dual output) --------------------------
  * hidden = x + residual (rounded to dt_x); normed = hidden * rsqrt(mean(hidden^2)

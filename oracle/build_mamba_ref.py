@@ -5,7 +5,8 @@ It is the GPU comparator for the headline selective scan: the vendored mamba_ssm
 (external/mamba/csrc/selective_scan/*, cub block scans, SIMT) that the reference would run on a
 CUDA GPU, compiled from their sources where they lie in the reference checkout with the compile
 flags of external/mamba/setup.py:228-244 and the architecture set to sm_100a.  Nothing here is
-part of the product path; `bench.py` times it beside our kernels when the built module is present.
+part of the product path; tests/test_gpu_mamba_comparator.py checks parity with it and asserts that
+our scan is faster than it at the headline configuration.
 
     python oracle/build_mamba_ref.py [--reference PATH] [--jobs N]
 

@@ -48,7 +48,7 @@ def test_shape_validation_reports_error_without_gpu():
     assert rc == 3  # AK_ERR_SHAPE
     assert b"bad shape" in lib.ak_last_error()
     rc = lib.ak_selective_scan_fwd(None, None, None, None, None, None, None, None, None, None, None, 1,
-                                   2, 4, 16, 65, 1, 1, None)
+                                   2, 4, 16, 65, 1, 1, None, None)
     assert rc == 3 and b"dstate" in lib.ak_last_error()
     rc = lib.ak_softmax_fwd(None, None, 0, 16, 1, None)  # empty: nothing to do
     assert rc == 0 and lib.ak_last_error() == b""
