@@ -14,7 +14,7 @@
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import List, NamedTuple
+from typing import List
 
 import torch
 import torch.nn as nn
@@ -38,7 +38,7 @@ class Pattern:
 _RMSNORM_CLASS_NAMES = {"RMSNorm", "LlamaRMSNorm", "MistralRMSNorm", "Qwen2RMSNorm", "T5LayerNorm"}
 
 
-class ResidualPair(NamedTuple):
+class ResidualPair:
     """Residual stream value base + delta, not yet added.
 
     Passed between chained pre-norm blocks (`chain_residual_blocks`): the next
@@ -46,9 +46,20 @@ class ResidualPair(NamedTuple):
     (`autokernel::fused_res_rmsnorm_mixed`), so the add never runs as its own
     kernel and its backward needs no gradient-accumulation add either.
     base: fp32 residual stream; delta: 16-bit block output (autocast).
+
+    Deliberately not a tuple: a caller loop written for blocks that return
+    tuples (`h = block(h); if isinstance(h, tuple): h = h[0]`) would keep only
+    `base` and silently drop the block output.  Indexing or unpacking a pair
+    raises instead.
     """
-    base: torch.Tensor
-    delta: torch.Tensor
+    __slots__ = ("base", "delta")
+
+    def __init__(self, base: torch.Tensor, delta: torch.Tensor):
+        self.base = base
+        self.delta = delta
+
+    def __repr__(self) -> str:
+        return f"ResidualPair(base={tuple(self.base.shape)} {self.base.dtype}, delta={tuple(self.delta.shape)} {self.delta.dtype})"
 
     def materialize(self) -> torch.Tensor:
         return self.base + self.delta

@@ -710,21 +710,49 @@ constexpr size_t kNoAllocFloats = (size_t)1 << 20;
 static __device__ __align__(256) float g_rms_noalloc_scratch[kNoAllocFloats];
 
 // Device address of g_rms_noalloc_scratch per device (host code cannot use the
-// symbol's name as a device pointer); resolved once per device.
+// symbol's name as a device pointer).  The array lives in the device's current
+// context, so the cached address is keyed on that context: after a device reset
+// (a new primary context) the first call resolves it again.
 std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[64] = {nullptr};
+struct NoAllocSlot {
+  void* ctx;
+  float* ptr;
+};
+NoAllocSlot g_noalloc[64] = {};
+
+typedef int (*CtxGetCurrentFn)(void**);  // CUresult cuCtxGetCurrent(CUcontext*)
+
+int current_context(void** ctx) {
+  static CtxGetCurrentFn fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    AK_CUDA_TRY(cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q),
+                "ak_rmsnorm_bwd_noalloc: driver entry point");
+    AK_REQUIRE(f != nullptr && q == cudaDriverEntryPointSuccess, AK_ERR_LAUNCH,
+               "ak_rmsnorm_bwd_noalloc: cuCtxGetCurrent unavailable");
+    fn = reinterpret_cast<CtxGetCurrentFn>(f);
+  }
+  AK_REQUIRE(fn(ctx) == 0, AK_ERR_LAUNCH, "ak_rmsnorm_bwd_noalloc: cuCtxGetCurrent failed");
+  return AK_OK;
+}
 
 int noalloc_scratch(float** out) {
   int dev = 0;
   AK_CUDA_TRY(cudaGetDevice(&dev), "ak_rmsnorm_bwd_noalloc: cudaGetDevice");
   AK_REQUIRE(dev >= 0 && dev < 64, AK_ERR_ARG, "ak_rmsnorm_bwd_noalloc: device index %d out of range", dev);
+  void* ctx = nullptr;
+  int rc = current_context(&ctx);  // NULL until the runtime has made a context current on this thread
+  if (rc) return rc;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_ptr[dev] == nullptr) {
+  if (g_noalloc[dev].ptr == nullptr || ctx == nullptr || g_noalloc[dev].ctx != ctx) {
     void* p = nullptr;
     AK_CUDA_TRY(cudaGetSymbolAddress(&p, g_rms_noalloc_scratch), "ak_rmsnorm_bwd_noalloc: cudaGetSymbolAddress");
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+    if ((rc = current_context(&ctx))) return rc;  // current now
+    g_noalloc[dev].ctx = ctx;
+    g_noalloc[dev].ptr = static_cast<float*>(p);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = g_noalloc[dev].ptr;
   return AK_OK;
 }
 

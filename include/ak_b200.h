@@ -102,7 +102,8 @@ AK_API int ak_rmsnorm_bwd(void* dx, void* dw, int dt_dw, void* workspace, size_t
  * (2^20 floats) that every GPU loading the library keeps until exit; N up to
  * 2^20 is accepted, larger N returns AK_ERR_SHAPE.  The first call on a device
  * looks up that array's device address (cudaGetSymbolAddress), so make it
- * before any stream capture.  All calls share the array: calls that overlap
+ * before any stream capture; the address is cached per device and context and
+ * looked up again after a device reset gives the device a new context.  All calls share the array: calls that overlap
  * on the GPU (different streams, or several host threads) race on it and must
  * be serialised by the caller.  Allocates nothing. */
 AK_API int ak_rmsnorm_bwd_noalloc(void* dx, void* dw, int dt_dw, const void* dy,

@@ -1,4 +1,5 @@
 """autokernel.optimize / report / restore / list_patterns on CPU (no kernel calls)."""
+import pytest
 import torch
 import torch.nn as nn
 
@@ -172,6 +173,12 @@ def test_residual_chain_marking(monkeypatch):
     assert chain_residual_blocks(nn.Sequential(nn.Linear(2, 2))) == 0
     p = ResidualPair(torch.ones(2), torch.full((2,), 2.0))
     assert torch.equal(p.materialize(), torch.full((2,), 3.0))
+    # not a tuple: code that unwraps tuple outputs (h = h[0]) fails loudly instead of dropping delta
+    assert not isinstance(p, tuple)
+    with pytest.raises(TypeError):
+        p[0]
+    with pytest.raises(TypeError):
+        base, delta = p
 
 
 def test_trainer_cuda_graph_flag_ignored_on_cpu():
