@@ -2,125 +2,227 @@
 //
 // Semantics: kernels/hip/chunked_linear_cross_entropy.py:55-175 of the reference
 // (mean CE over rows with label != ignore_index of logits = H W^T, with dH and
-// dW), without its fp16 coercion, host sync, or materialised logits:
+// dW), without its fp16 coercion, host sync or cuBLAS GEMMs.  Per chunk of up to
+// kChunkRows rows:
 //
-//   1. logits tiles = H W^T by tcgen05.mma; the epilogue reduces each 128x256
-//      tile to per-row (max, sum exp) partials and picks the target logit —
-//      logits never reach HBM;
-//   2. a small kernel merges the partials into lse, the per-row loss and the
-//      mean (n_valid counted on the device);
-//   3. per chunk of rows the logits tiles are recomputed and the epilogue
-//      writes G = (softmax - onehot) / n_valid directly in bf16, row-major and
-//      transposed;
-//   4. dH = G W and dW += G^T H by the same tcgen05 GEMM (operands pre-transposed
-//      once so every GEMM reads K-major tiles).
+//   1. logits = H_c W^T on the tensor cores; the epilogue reduces each tile to
+//      per-row (max, sum exp) partials, picks the target logit and stores the
+//      16-bit logits into the chunk buffer G_c;
+//   2. a row kernel merges the partials into lse and the per-row loss;
+//   3. a streaming kernel turns G_c in place into (softmax - onehot) / n_valid;
+//   4. one grouped launch of the same GEMM kernel computes dW (+)= G_c^T H_c and
+//      dH_c = G_c W, reading G_c, H and W in their row-major layouts (the
+//      operands whose contiguous dimension is M or N use MN-major shared-memory
+//      descriptors, so nothing is transposed).
 //
-// GEMM kernel: C[M,N] = A[M,K] B[N,K]^T with bf16/fp16 A, B (K contiguous) and
-// fp32 accumulation in TMEM.  Persistent CTAs of 10 warps: warp 0 issues TMA
-// loads (128B-swizzled 128x64 and 256x64 boxes) into a 4-stage ring, warp 1
-// issues tcgen05.mma (M=128, N=256, K=16) from one thread into one of two TMEM
-// accumulators (2 x 256 columns), warps 2-9 (two warpgroups, one per 128-column
-// half) run the epilogue on the other accumulator via tcgen05.ld, so a tile's
-// epilogue overlaps the next tile's MMAs.  All mbarrier waits are bounded (error flag + return, never a hang).
-// No cluster, no TMA multicast.
+// Full logits never exist: G_c holds kChunkRows rows at most.  Why G_c is
+// materialised at all: an accumulator for dH (128 rows x D = 768 fp32) or dW
+// (128 vocab rows x 768) does not fit the 512 TMEM columns next to a logits
+// tile, and keeping one of them outside TMEM costs more HBM traffic than
+// writing and re-reading G_c once.
+//
+// GEMM kernel: C[M,N] = A[M,K] B[N,K]^T, bf16/fp16 operands, fp32 accumulation.
+// Clusters of two CTAs on a TPC issue tcgen05.mma.cta_group::2 (M = 256 split
+// over the pair, N = 256): each CTA stages its 128 rows of A and its 128 rows of
+// B per 64-deep K block by TMA (no multicast) and accumulates its 128 x 256
+// half of the tile in its own TMEM.  Per CTA: warp 0 issues TMA into a 6-stage
+// ring (both CTAs' copies complete on the leader CTA's barrier), warp 1 of the
+// leader issues the MMAs from one thread into one of two TMEM accumulators,
+// warps 2-9 (two warpgroups, one per 128-column half) run the epilogue on the
+// other accumulator, so a tile's epilogue overlaps the next tile's MMAs.
+// Persistent: each CTA pair walks the tiles of up to two problems (the dW and
+// dH contractions share one launch).  Every mbarrier wait is bounded: on a
+// timeout AK_ERR_TIMEOUT goes to the caller's status word and the kernel still
+// finishes.
 #include "ak_common.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 namespace ak {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue (2 warpgroups)
-constexpr int kEpiThreads = 256;
-constexpr int kHalf = BN / 2;   // columns per epilogue warpgroup
-constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2;
-constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int BM = 128;            // rows of A per CTA (256 per CTA pair)
+constexpr int BN = 256;            // tile columns (each CTA stages half of B)
+constexpr int BK = 64;
+constexpr int STAGES = 6;
+constexpr int kEpiGroups = 2;      // epilogue warpgroups, one per 128-column half of the tile
+constexpr int kEpiWarps = 4 * kEpiGroups;
+constexpr int kThreads = 32 * (2 + kEpiWarps);  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int kGroupCols = BN / kEpiGroups;
+constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = (BN / 2) * BK * 2;
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA
 constexpr int TMEM_COLS = 2 * BN;  // two accumulators
-constexpr int kTPitch = BM + 8;    // transpose staging row pitch (16-byte aligned rows)
+constexpr int64_t kChunkRows = 16384;
 
-enum Epi : int { EPI_STATS = 0, EPI_GRAD = 1, EPI_STORE_BF16 = 2, EPI_STORE_F32 = 3 };
+enum Epi : int { EPI_STATS = 0, EPI_STORE = 1, EPI_NONE = 2 };  // EPI_NONE: accumulate only (timing)
 
-struct GemmArgs {
-  int M, N, K;              // C is M x N; A is M x K, B is N x K
-  int b_row0, a_k0, b_k0;   // coordinate offsets into the B rows and the K dimension
-  // EPI_STATS
-  float2* part;             // [M][ntiles] (max, sum exp2-domain)
+struct Prob {
+  int M, N, K;
+  int a_mn, b_mn;           // 1: the operand's M (N) dimension is contiguous in memory
+  int epi;
+  int mtiles, ntiles, tiles;
+  // EPI_STATS: per-row (max, sum exp2) partial per 128-column half, target logit,
+  // and optionally the 16-bit logits (C, ldc)
+  float2* part;             // [M][kEpiGroups * ntiles]
   float* tlogit;            // [M]
-  const int64_t* labels;    // [M] (already offset to the rows of this GEMM)
+  const int64_t* labels;    // [M]
   int64_t ignore_index;
-  // EPI_GRAD
-  const float* lse;         // [M]
-  const float* scale;       // device scalar: 1 / n_valid
-  void* G;                  // [M][N] row-major, 16-bit
-  void* GT;                 // [N][ldgt] (column block starting at gt_col0)
-  int64_t ldgt, gt_col0;
-  // EPI_STORE
-  void* C;                  // [M][N]
+  // EPI_STORE: C = acc (+ add_f32) (+ C if accumulate), fp32 (c_f32) or 16-bit
+  void* C;
   int64_t ldc;
-  int accumulate;           // EPI_STORE_F32: C += acc
-  int* status;              // caller's status word: AK_ERR_TIMEOUT when a bounded wait gave up
+  const float* add_f32;     // nullable, same layout as C
+  const float* scale;       // nullable device scalar multiplying acc (before add_f32 / accumulate)
+  int c_f32, accumulate;
+};
+
+struct Group {
+  Prob p[2];
+  int nprob, total;
+  int* status;
 };
 
 // ---------------------------------------------------------------------------
 // PTX helpers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Cluster-wide barrier.  The warp reconverges first: in the producer and MMA
+// warps one lane runs the pipeline while the others wait here.
+__device__ __forceinline__ void cluster_sync() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Tiled 2-D TMA load into this CTA's shared memory; the transaction bytes are
+// counted on `bar`, which may be the peer CTA's barrier (cluster address).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
       : "memory");
 }
 
-// K-major, 128-byte swizzled operand tile: rows of 64 16-bit elements (128 B),
-// 8-row swizzle atoms 1024 B apart (SBO), LBO unused (1), Blackwell version 1,
-// layout type SWIZZLE_128B (2).
-__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
-  const uint64_t addr = smem_u32(p);
+// 128-byte swizzled operand tile descriptor.  K-major: rows of 64 16-bit K
+// elements (128 B), 8-row atoms 1024 B apart (SBO), LBO unused.  MN-major: rows
+// of 64 contiguous M (or N) elements per K index, 8-K-row atoms 1024 B apart
+// (SBO), and the next 64 M (N) elements `mn_block` bytes further (LBO).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, bool mn, uint32_t mn_block) {
   uint64_t d = 0;
-  d |= (addr >> 4) & 0x3FFFull;           // start address
-  d |= (uint64_t)1 << 16;                 // leading byte offset (16 B units)
-  d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset
-  d |= (uint64_t)1 << 46;                 // version
-  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((mn ? (mn_block >> 4) : 1u) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (Blackwell)
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
   return d;
 }
 
-// kind::f16 instruction descriptor: fp32 accumulate, A/B type, K-major both, N, M.
-__host__ __device__ constexpr uint32_t make_idesc(bool bf16, int m, int n) {
-  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((uint32_t)(n >> 3) << 17) |
-         ((uint32_t)(m >> 4) << 24);
+// kind::f16 instruction descriptor: fp32 accumulate, A/B type, majorness, N, M.
+__host__ __device__ constexpr uint32_t make_idesc(bool bf16, int m, int n, int a_mn, int b_mn) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((uint32_t)a_mn << 15) |
+         ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
+__device__ __forceinline__ void mma2(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                     uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+// Arrive on `bar` (cluster address: this CTA's or the peer's) once every
+// tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void commit2(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+// Arrive on a barrier given by cluster address (this CTA's or the peer's).  The
+// default CTA-scope release: the arrival only has to follow this thread's TMEM
+// reads (completed by tcgen05.wait::ld and fenced by tcgen05.fence), not make
+// its global stores visible, which a cluster-scope release would wait for.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded waits.  The first wait of a CTA that runs out reports AK_ERR_TIMEOUT
+// and raises the CTA's abort flag; every later wait of that CTA then returns at
+// once, so a broken pipeline ends the kernel after one time-out instead of one
+// per stage.  `cluster` waits also acquire what the peer CTA released before
+// arriving.
+struct Waiter {
+  int* status;
+  volatile int* abort;
+};
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitimate wait in one launch
+
+template <bool kCluster>
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const Waiter& w) {
+  if (*w.abort) return false;
+  if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    if (i > 64) __nanosleep(32);
+    if ((i & 255u) == 0) {
+      if (*w.abort) return false;
+      if (global_ns() - t0 > kWaitLimitNs) break;
+    }
+  }
+  *w.abort = 1;
+  report_status(w.status, (int)AK_ERR_TIMEOUT);
+  return false;
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane, as an asynchronous
+// load (tmem_ld_issue) completed by tmem_ld_wait.  The wait names the
+// destination registers as in-out operands, so no use of them can be moved
+// above it; a load of the next columns can run while the current ones are used.
+struct Tm32 {
   uint32_t r[32];
+};
+
+__device__ __forceinline__ void tmem_ld_issue(uint32_t taddr, Tm32& t) {
+  uint32_t* r = t.r;
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
       "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -129,263 +231,423 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait(Tm32& t) {
+  uint32_t* r = t.r;
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// ---- 16-bit row tiles through shared memory -------------------------------
+// A warp's 32 rows x 64 columns (one row per lane, two 32-column halves) are
+// written to a 4 KB tile (row r at r * 128 B, 16-byte chunk c stored at chunk
+// position c ^ (r & 7): conflict-free on both sides) and leave as 16-byte
+// global stores that cover four full 128-byte lines per instruction, instead
+// of 32 partial lines when every lane stores its own row.
+constexpr int kStageWarpBytes = 32 * 128;
+
+template <typename T>
+__device__ __forceinline__ void stage_put(uint32_t stg, int lane, int half, const float (&v)[32]) {
 #pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  for (int q = 0; q < 4; ++q) {
+    Frag<T, 8> f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f.v[e] = from_f<T>(v[8 * q + e]);
+    const uint4 u = *reinterpret_cast<const uint4*>(&f);
+    const uint32_t pos = (uint32_t)((4 * half + q) ^ (lane & 7));
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(stg + (uint32_t)lane * 128u + pos * 16u),
+                 "r"(u.x), "r"(u.y), "r"(u.z), "r"(u.w)
+                 : "memory");
+  }
+}
+
+// Rows row0 .. row0+31 (those below nrows), 64 columns starting at col.
+template <typename T>
+__device__ __forceinline__ void stage_flush(uint32_t stg, int lane, T* C, int64_t ldc, int64_t row0, int nrows,
+                                            int col) {
+  const int q = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int R = 4 * i + (lane >> 3);
+    uint4 u;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                 : "r"(stg + (uint32_t)R * 128u + (uint32_t)((q ^ (R & 7)) * 16))
+                 : "memory");
+    if (R < nrows) *reinterpret_cast<uint4*>(C + (row0 + R) * ldc + col + 8 * q) = u;
+  }
+}
+
+// Global tile index -> (problem, m tile, n tile).  Tiles are visited in groups
+// of kGroupM m tiles: inside a group the m tile varies fastest, so the ~74 CTA
+// pairs working at one time cover a compact block of about 8 m tiles x 9 n
+// tiles, and both operands' tiles are reused from L2 instead of one of them
+// streaming from HBM once per tile row or column.
+constexpr int kGroupM = 8;
+
+__device__ __forceinline__ void decode_tile(const Group& g, int t, int& pi, int& mt, int& nt) {
+  pi = (g.nprob > 1 && t >= g.p[0].tiles) ? 1 : 0;
+  const Prob& P = pi ? g.p[1] : g.p[0];
+  const int l = pi ? t - g.p[0].tiles : t;
+  const int per_group = kGroupM * P.ntiles;
+  const int grp = l / per_group, r = l - grp * per_group;
+  const int m0 = grp * kGroupM;
+  const int gm = min(kGroupM, P.mtiles - m0);
+  mt = m0 + r % gm;
+  nt = r / gm;
 }
 
 // ---------------------------------------------------------------------------
-// The GEMM kernel
+// Epilogues (one lane = one row of the warp's 32; a warpgroup = 128 rows x its columns)
 // ---------------------------------------------------------------------------
-template <typename T, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
-tn_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
+// Softmax statistics of 32 logits of this lane's row (natural units in v).
+__device__ __forceinline__ void stats_chunk(const float (&v)[32], int cbase, int N, float& m, float& s) {
+  float2 v2[16];
+  const float2 l2e = make_float2(kLog2e, kLog2e);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v2[j] = __fmul2_rn(make_float2(v[2 * j], v[2 * j + 1]), l2e);
+  if (cbase + 32 > N) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (cbase + 2 * j >= N) v2[j].x = -INFINITY;
+      if (cbase + 2 * j + 1 >= N) v2[j].y = -INFINITY;
+    }
+  }
+  float lm = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) lm = fmaxf(lm, fmaxf(v2[j].x, v2[j].y));
+  const float mn = fmaxf(m, lm);
+  if (mn != -INFINITY) {
+    const float2 neg = make_float2(-mn, -mn);
+    float2 a2 = make_float2(s * ex2(m - mn), 0.f);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 d = __fadd2_rn(v2[j], neg);
+      a2 = __fadd2_rn(a2, make_float2(ex2(d.x), ex2(d.y)));
+    }
+    s = a2.x + a2.y;
+    m = mn;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void put_row16(T* crow, int cbase, int N, const float (&v)[32]) {
+  if (cbase + 32 <= N) {
+#pragma unroll
+    for (int q = 0; q < 32; q += 8) {
+      float f[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = v[q + e];
+      store_frag<T, 8>(crow + cbase + q, f);
+    }
+  } else {
+    for (int j = 0; j < 32; ++j)
+      if (cbase + j < N) crow[cbase + j] = from_f<T>(v[j]);
+  }
+}
+
+// Per-row (max, sum exp2) partial of this warpgroup's 128 columns, the target
+// logit and, with P.C, the 16-bit logits.  TMEM loads run one 32-column chunk
+// ahead of the arithmetic.
+template <typename T>
+__device__ __forceinline__ void epi_stats(const Prob& P, uint32_t tbase, int row0, int lane, int64_t lab,
+                                          int col0, int eg, uint32_t stg) {
+  const int row = row0 + lane;
+  const bool rv = row < P.M;
+  const int nrows = min(32, P.M - row0);
+  float m = -INFINITY, s = 0.f;  // s: sum of exp2(x log2e - m), m in log2 units
+  T* C = reinterpret_cast<T*>(P.C);
+  const int c0 = eg * kGroupCols;
+  Tm32 buf[2];
+  __syncwarp();
+  tmem_ld_issue(tbase + (uint32_t)c0, buf[0]);
+  tmem_ld_wait(buf[0]);
+#pragma unroll
+  for (int k = 0; k < kGroupCols / 32; ++k) {
+    if (k + 1 < kGroupCols / 32) tmem_ld_issue(tbase + (uint32_t)(c0 + 32 * (k + 1)), buf[(k + 1) & 1]);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(buf[k & 1].r[j]);
+    const int cbase = col0 + c0 + 32 * k;
+    if (C != nullptr) {
+      // logits kept in 16 bits for the gradient pass (the statistics use the fp32 values)
+      if (col0 + c0 + 32 * (k | 1) + 32 <= P.N) {  // this 64-column block is inside the matrix
+        stage_put<T>(stg, lane, k & 1, v);
+        if (k & 1) {
+          __syncwarp();
+          stage_flush<T>(stg, lane, C, P.ldc, row0, nrows, cbase - 32);
+          __syncwarp();
+        }
+      } else if (rv) {
+        put_row16<T>(C + (int64_t)row * P.ldc, cbase, P.N, v);
+      }
+    }
+    // the target logit (a predicated store per column keeps v in registers)
+    const int rel = (int)(lab - cbase);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j == rel) P.tlogit[row] = v[j];
+    stats_chunk(v, cbase, P.N, m, s);
+    if (k + 1 < kGroupCols / 32) tmem_ld_wait(buf[(k + 1) & 1]);
+  }
+  if (rv) P.part[(int64_t)row * (kEpiGroups * P.ntiles) + kEpiGroups * (col0 / BN) + eg] = make_float2(m, s);
+}
+
+// C = acc * scale (+ add_f32) (+ C if accumulate), fp32 or 16-bit (staged rows).
+template <typename T>
+__device__ __forceinline__ void epi_store(const Prob& P, uint32_t tbase, int row0, int lane, int col0, int eg,
+                                          uint32_t stg) {
+  const int row = row0 + lane;
+  const bool rv = row < P.M;
+  const int nrows = min(32, P.M - row0);
+  const int c0 = eg * kGroupCols;
+  const float sc = P.scale != nullptr ? *P.scale : 1.f;
+  Tm32 buf[2];
+  __syncwarp();
+  tmem_ld_issue(tbase + (uint32_t)c0, buf[0]);
+  tmem_ld_wait(buf[0]);
+#pragma unroll
+  for (int k = 0; k < kGroupCols / 32; ++k) {
+    if (k + 1 < kGroupCols / 32) tmem_ld_issue(tbase + (uint32_t)(c0 + 32 * (k + 1)), buf[(k + 1) & 1]);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(buf[k & 1].r[j]) * sc;
+    const int cbase = col0 + c0 + 32 * k;
+    const int64_t off = (int64_t)row * P.ldc + cbase;
+    const bool full = cbase + 32 <= P.N;
+    if (P.add_f32 != nullptr && rv) {
+      const float* a = P.add_f32 + off;
+      if (full) {
+#pragma unroll
+        for (int q = 0; q < 32; q += 4) {
+          const float4 o = *reinterpret_cast<const float4*>(a + q);
+          v[q] += o.x; v[q + 1] += o.y; v[q + 2] += o.z; v[q + 3] += o.w;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j)
+          if (cbase + j < P.N) v[j] += a[j];
+      }
+    }
+    if (P.c_f32) {
+      if (rv) {
+        float* crow = reinterpret_cast<float*>(P.C) + off;
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 32; q += 4) {
+            float4* p4 = reinterpret_cast<float4*>(crow + q);
+            float4 o = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+            if (P.accumulate) {
+              const float4 old = *p4;
+              o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+            }
+            *p4 = o;
+          }
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (cbase + j < P.N) crow[j] = v[j] + (P.accumulate ? crow[j] : 0.f);
+        }
+      }
+    } else {
+      T* C = reinterpret_cast<T*>(P.C);
+      if (col0 + c0 + 32 * (k | 1) + 32 <= P.N) {
+        stage_put<T>(stg, lane, k & 1, v);
+        if (k & 1) {
+          __syncwarp();
+          stage_flush<T>(stg, lane, C, P.ldc, row0, nrows, cbase - 32);
+          __syncwarp();
+        }
+      } else if (rv) {
+        put_row16<T>(C + (int64_t)row * P.ldc, cbase, P.N, v);
+      }
+    }
+    if (k + 1 < kGroupCols / 32) tmem_ld_wait(buf[(k + 1) & 1]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// The GEMM kernel (clusters of 2 CTAs)
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tB0,
+                const __grid_constant__ CUtensorMap tA1, const __grid_constant__ CUtensorMap tB1,
+                const __grid_constant__ Group g) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // 1024-byte alignment for the swizzled tiles
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* tiles = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;  // [2]
-  uint64_t* tempty = tfull + 2;      // [2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);  // leader: TMA bytes of both CTAs
+  uint64_t* empty = full + STAGES;                                             // each CTA: its stage is free
+  uint64_t* tfull = empty + STAGES;   // [2] each CTA: accumulator ready
+  uint64_t* tempty = tfull + 2;       // [2] leader: both CTAs' epilogues done with the accumulator
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  T* sT = reinterpret_cast<T*>(smem + STAGES * STAGE_BYTES + 256);  // [2][32][kTPitch] transpose staging
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mtiles = (g.M + BM - 1) / BM, ntiles = (g.N + BN - 1) / BN;
-  const int ntile_total = mtiles * ntiles;
-  const int ktiles = (g.K + BK - 1) / BK;  // the K tail is zero-filled by TMA in both operands
+  const uint32_t rank = cluster_rank();
+  const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
 
+  const Waiter wt{g.status, abort_flag};
   if (threadIdx.x == 0) {
+    *abort_flag = 0;
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], kEpiThreads); }
+    for (int a = 0; a < 2; ++a) { mbar_init(&tfull[a], 1); mbar_init(&tempty[a], 2 * kEpiWarps); }
     mbar_fence_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer (both CTAs)
     if (lane == 0) {
+      const uint32_t full0 = peer_addr(smem_u32(&full[0]), 0);  // the leader's barriers
       int it = 0;
-      for (int t = blockIdx.x; t < ntile_total; t += gridDim.x) {
-        const int mt = t % mtiles, nt = t / mtiles;
+      for (int t = pair; t < g.total; t += npairs) {
+        int pi, mt, nt;
+        decode_tile(g, t, pi, mt, nt);
+        const Prob& P = pi ? g.p[1] : g.p[0];
+        const CUtensorMap* mA = pi ? &tA1 : &tA0;
+        const CUtensorMap* mB = pi ? &tB1 : &tB0;
+        const int m0 = mt * (2 * BM) + (int)rank * BM;
+        const int n0 = nt * BN + (int)rank * (BN / 2);
+        const int ktiles = (P.K + BK - 1) / BK;  // the K tail is zero-filled by TMA in both operands
         for (int kb = 0; kb < ktiles; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-          mbar_wait_bounded(&empty[s], ph ^ 1u, g.status);
-          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-          unsigned char* st = tiles + s * STAGE_BYTES;
-          tma_load_2d(st, &tmA, g.a_k0 + kb * BK, mt * BM, &full[s]);
-          tma_load_2d(st + A_BYTES, &tmB, g.b_k0 + kb * BK, g.b_row0 + nt * BN, &full[s]);
+          wait_bar<false>(&empty[s], ph ^ 1u, wt);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
+          const uint32_t bar = full0 + (uint32_t)(s * 8);
+          const uint32_t st = smem_u32(tiles + s * STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (P.a_mn) {
+            tma_load_2d(st, mA, m0, k0, bar);
+            tma_load_2d(st + A_BYTES / 2, mA, m0 + 64, k0, bar);
+          } else {
+            tma_load_2d(st, mA, k0, m0, bar);
+          }
+          if (P.b_mn) {
+            tma_load_2d(st + A_BYTES, mB, n0, k0, bar);
+            tma_load_2d(st + A_BYTES + B_BYTES / 2, mB, n0 + 64, k0, bar);
+          } else {
+            tma_load_2d(st + A_BYTES, mB, k0, n0, bar);
+          }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc(sizeof(T) == 2 && !std::is_same<T, __half>::value, BM, BN);
+    // ---------------- MMA issuer (leader CTA only)
+    if (rank == 0 && lane == 0) {
+      constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+      const uint32_t peer_empty0 = peer_addr(smem_u32(&empty[0]), 1);
+      const uint32_t peer_tfull0 = peer_addr(smem_u32(&tfull[0]), 1);
       int it = 0, local = 0;
-      for (int t = blockIdx.x; t < ntile_total; t += gridDim.x, ++local) {
+      for (int t = pair; t < g.total; t += npairs, ++local) {
+        int pi, mt, nt;
+        decode_tile(g, t, pi, mt, nt);
+        const Prob& P = pi ? g.p[1] : g.p[0];
+        const uint32_t idesc = make_idesc(kBf16, 2 * BM, BN, P.a_mn, P.b_mn);
+        // K = 16 steps inside a 64-deep stage: 32 B along a K-major row, or two
+        // 8-row atoms (2048 B) of an MN-major tile
+        const uint32_t astep = P.a_mn ? (2048u >> 4) : 2u, bstep = P.b_mn ? (2048u >> 4) : 2u;
         const int acc = local & 1;
-        mbar_wait_bounded(&tempty[acc], ((uint32_t)(local >> 1) & 1u) ^ 1u, g.status);
+        wait_bar<true>(&tempty[acc], ((uint32_t)(local >> 1) & 1u) ^ 1u, wt);
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)(acc * BN);
+        const int ktiles = (P.K + BK - 1) / BK;
         for (int kb = 0; kb < ktiles; ++kb, ++it) {
           const int s = it % STAGES;
-          mbar_wait_bounded(&full[s], (uint32_t)(it / STAGES) & 1u, g.status);
+          wait_bar<false>(&full[s], (uint32_t)(it / STAGES) & 1u, wt);
           tc_fence_after();
-          const unsigned char* st = tiles + s * STAGE_BYTES;
-          const uint64_t ad = smem_desc_sw128(st), bd = smem_desc_sw128(st + A_BYTES);
+          const uint32_t st = smem_u32(tiles + s * STAGE_BYTES);
+          const uint64_t ad = smem_desc_sw128(st, P.a_mn, A_BYTES / 2);
+          const uint64_t bd = smem_desc_sw128(st + A_BYTES, P.b_mn, B_BYTES / 2);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)  // advance 32 B (16 elements) inside the swizzle row
-            mma_f16(dcol, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) ? 1u : 0u);
-          mma_commit(&empty[s]);
+          for (int k = 0; k < BK / 16; ++k)
+            mma2(dcol, ad + (uint64_t)(astep * k), bd + (uint64_t)(bstep * k), idesc, (kb | k) ? 1u : 0u);
+          commit2(smem_u32(&empty[s]));
+          commit2(peer_empty0 + (uint32_t)(s * 8));
         }
-        mma_commit(&tfull[acc]);
+        commit2(smem_u32(&tfull[acc]));
+        commit2(peer_tfull0 + (uint32_t)(acc * 8));
       }
     }
   } else {
-    // ---------------- epilogue: warps 2..5 own TMEM lanes 32*(warp%4) ...
+    // ---------------- epilogue (both CTAs): warps 2..9 own TMEM lanes 32*(warp%4) ...
     const int quad = warp & 3;
-    const int eg = (warp - 2) >> 2;           // epilogue warpgroup: column half
-    T* sTg = sT + eg * 32 * kTPitch;
-    const int rl = quad * 32 + lane;  // row within the tile
+    const int eg = (warp - 2) >> 2;  // epilogue warpgroup: column half
+    const uint32_t stg = smem_u32(smem + STAGES * STAGE_BYTES + 256) + (uint32_t)((warp - 2) * kStageWarpBytes);
+    const uint32_t tempty0 = peer_addr(smem_u32(&tempty[0]), 0);
     int local = 0;
-    for (int t = blockIdx.x; t < ntile_total; t += gridDim.x, ++local) {
-      const int mt = t % mtiles, nt = t / mtiles;
+    for (int t = pair; t < g.total; t += npairs, ++local) {
+      int pi, mt, nt;
+      decode_tile(g, t, pi, mt, nt);
+      const Prob& P = pi ? g.p[1] : g.p[0];
       const int acc = local & 1;
-      mbar_wait_bounded(&tfull[acc], (uint32_t)(local >> 1) & 1u, g.status);
+      const int row0 = mt * (2 * BM) + (int)rank * BM + quad * 32;  // this warp's 32 rows
+      // the row's label is loaded before the wait, so its latency hides behind the MMAs
+      const int64_t lab = (P.epi == EPI_STATS && row0 + lane < P.M) ? P.labels[row0 + lane] : -1;
+      wait_bar<false>(&tfull[acc], (uint32_t)(local >> 1) & 1u, wt);
       tc_fence_after();
-      const int row = mt * BM + rl;
-      const bool rv = row < g.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      const int col0 = nt * BN;
-      if constexpr (EPI == EPI_STATS) {
-        const int64_t lab = rv ? g.labels[row] : -1;
-        float m = -INFINITY, s = 0.f;  // s: sum of exp2(x*log2e - m) with m in log2 units
-        for (int c = eg * kHalf; c < (eg + 1) * kHalf; c += 32) {
-          float v[32];
-          tmem_ld32(tbase + (uint32_t)c, v);
-          if (g.G != nullptr) {
-            // logits kept in 16 bits for the gradient pass; the statistics use the
-            // same rounded values so that softmax and lse stay consistent
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = to_f<T>(from_f<T>(v[j]));
-            const int cbase = col0 + c;
-            T* lrow = reinterpret_cast<T*>(g.G) + (int64_t)row * g.N;
-            if (rv && cbase + 32 <= g.N) {
-#pragma unroll
-              for (int q = 0; q < 32; q += 8) {
-                float f[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = v[q + e];
-                store_frag<T, 8>(lrow + cbase + q, f);
-              }
-            } else if (rv) {
-              for (int j = 0; j < 32; ++j)
-                if (cbase + j < g.N) lrow[cbase + j] = from_f<T>(v[j]);
-            }
-          }
-          float lm = -INFINITY;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = col0 + c + j;
-            v[j] = (col < g.N) ? v[j] * kLog2e : -INFINITY;
-            lm = fmaxf(lm, v[j]);
-            if (col == lab && rv) g.tlogit[row] = v[j] * kLn2;
-          }
-          const float mn = fmaxf(m, lm);
-          if (mn != -INFINITY) {
-            float a = s * ex2(m - mn);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) a += ex2(v[j] - mn);
-            s = a;
-            m = mn;
-          }
-        }
-        if (rv) g.part[(int64_t)row * (2 * ntiles) + 2 * nt + eg] = make_float2(m, s);
-      } else if constexpr (EPI == EPI_GRAD) {
-        const int64_t lab = rv ? g.labels[row] : g.ignore_index;
-        const bool ign = (lab == g.ignore_index);
-        const float sc = ign ? 0.f : *g.scale;
-        const float lse2 = rv ? g.lse[row] * kLog2e : 0.f;
-        T* grow = reinterpret_cast<T*>(g.G) + (int64_t)row * g.N;
-        T* gt = reinterpret_cast<T*>(g.GT);
-        for (int c = eg * kHalf; c < (eg + 1) * kHalf; c += 32) {
-          float v[32];
-          tmem_ld32(tbase + (uint32_t)c, v);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = col0 + c + j;
-            float gv = ex2(fmaf(v[j], kLog2e, -lse2)) * sc;
-            if (col == lab) gv -= sc;
-            v[j] = gv;
-          }
-          const int cbase = col0 + c;
-          if (rv) {
-            if (cbase + 32 <= g.N) {
-#pragma unroll
-              for (int q = 0; q < 32; q += 8) {
-                float f[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = v[q + e];
-                store_frag<T, 8>(grow + cbase + q, f);
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (cbase + j < g.N) grow[cbase + j] = from_f<T>(v[j]);
-            }
-          }
-          // G^T: transpose the 128x32 block through shared memory, then 16-byte
-          // coalesced stores of 8 consecutive rows per thread.
-#pragma unroll
-          for (int j = 0; j < 32; ++j) sTg[j * kTPitch + rl] = from_f<T>(v[j]);
-          asm volatile("bar.sync %0, 128;" ::"r"(1 + eg) : "memory");
-          const int e = (threadIdx.x - 64) & 127;
-#pragma unroll
-          for (int q = e; q < 32 * (BM / 8); q += 128) {
-            const int cj = q / (BM / 8), rc = q - cj * (BM / 8);
-            const int r0 = mt * BM + rc * 8;
-            if (cbase + cj < g.N && r0 < g.M)
-              *reinterpret_cast<int4*>(gt + (int64_t)(cbase + cj) * g.ldgt + g.gt_col0 + r0) =
-                  *reinterpret_cast<const int4*>(sTg + cj * kTPitch + rc * 8);
-          }
-          asm volatile("bar.sync %0, 128;" ::"r"(1 + eg) : "memory");
-        }
-      } else {
-        for (int c = eg * kHalf; c < (eg + 1) * kHalf; c += 32) {
-          float v[32];
-          tmem_ld32(tbase + (uint32_t)c, v);
-          const int cbase = col0 + c;
-          if (!rv) continue;
-          if constexpr (EPI == EPI_STORE_BF16) {
-            T* crow = reinterpret_cast<T*>(g.C) + (int64_t)row * g.ldc;
-            if (cbase + 32 <= g.N) {
-#pragma unroll
-              for (int q = 0; q < 32; q += 8) {
-                float f[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = v[q + e];
-                store_frag<T, 8>(crow + cbase + q, f);
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (cbase + j < g.N) crow[cbase + j] = from_f<T>(v[j]);
-            }
-          } else {
-            float* crow = reinterpret_cast<float*>(g.C) + (int64_t)row * g.ldc;
-            if (cbase + 32 <= g.N) {
-#pragma unroll
-              for (int q = 0; q < 32; q += 4) {
-                float4* p4 = reinterpret_cast<float4*>(crow + cbase + q);
-                float4 o = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-                if (g.accumulate) {
-                  const float4 old = *p4;
-                  o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-                }
-                *p4 = o;
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (cbase + j < g.N) crow[cbase + j] = v[j] + (g.accumulate ? crow[cbase + j] : 0.f);
-            }
-          }
-        }
-      }
+      if (P.epi == EPI_STATS) epi_stats<T>(P, tbase, row0, lane, lab, nt * BN, eg, stg);
+      else if (P.epi == EPI_STORE) epi_store<T>(P, tbase, row0, lane, nt * BN, eg, stg);
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0 + (uint32_t)(acc * 8));
     }
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // every MMA has completed and been read; no more remote arrivals
   tc_fence_after();
   if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                  : "memory");
 }
 
 // ---------------------------------------------------------------------------
 // Side kernels
 // ---------------------------------------------------------------------------
-// Merge the per-tile partials: lse (natural log), per-row loss, and the mean.
+// 1 / max(1, number of rows whose label is not ignore_index), on the device.
+__global__ void __launch_bounds__(1024)
+lce_inv_valid(float* __restrict__ inv_valid, const int64_t* __restrict__ labels, int64_t M, int64_t ignore_index) {
+  __shared__ float r[32];
+  float n = 0.f;
+  for (int64_t i = threadIdx.x; i < M; i += blockDim.x) n += (labels[i] != ignore_index) ? 1.f : 0.f;
+  n = warp_sum(n);
+  if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = n;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += r[i];
+    inv_valid[0] = 1.f / fmaxf(s, 1.f);
+  }
+}
+
+// Merge the per-tile partials: lse (natural log) and the per-row loss.
 __global__ void __launch_bounds__(256)
 lce_rows_reduce(float* __restrict__ lse, float* __restrict__ losses, const float2* __restrict__ part,
-                const float* __restrict__ tlogit, const int64_t* __restrict__ labels, int M, int ntiles,
+                const float* __restrict__ tlogit, const int64_t* __restrict__ labels, int M, int nparts,
                 int64_t ignore_index) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= M) return;
   float m = -INFINITY, s = 0.f;
-  for (int t = lane; t < ntiles; t += 32) {
-    const float2 p = part[(int64_t)warp * ntiles + t];
+  for (int t = lane; t < nparts; t += 32) {
+    const float2 p = part[(int64_t)warp * nparts + t];
     const float mn = fmaxf(m, p.x);
     if (mn != -INFINITY) { s = s * ex2(m - mn) + p.y * ex2(p.x - mn); m = mn; }
   }
@@ -403,57 +665,34 @@ lce_rows_reduce(float* __restrict__ lse, float* __restrict__ losses, const float
   }
 }
 
+// loss[0] = inv_valid * sum of the per-row losses (ignored rows hold 0), fixed order.
 __global__ void __launch_bounds__(1024)
-lce_mean(float* __restrict__ loss, float* __restrict__ inv_valid, const float* __restrict__ losses,
-         const int64_t* __restrict__ labels, int64_t M, int64_t ignore_index) {
-  __shared__ float r0[32], r1[32];
-  float a = 0.f, n = 0.f;
+lce_loss(float* __restrict__ loss, const float* __restrict__ losses, const float* __restrict__ inv_valid, int64_t M) {
+  __shared__ float r[32];
+  float a = 0.f;
 #pragma unroll 4
-  for (int64_t i = threadIdx.x; i < M; i += blockDim.x) {
-    const int64_t lb = labels[i];
-    const float li = losses[i];  // unconditional: both loads in flight together
-    if (lb != ignore_index) { a += li; n += 1.f; }
-  }
+  for (int64_t i = threadIdx.x; i < M; i += blockDim.x) a += losses[i];
   a = warp_sum(a);
-  n = warp_sum(n);
-  if ((threadIdx.x & 31) == 0) { r0[threadIdx.x >> 5] = a; r1[threadIdx.x >> 5] = n; }
+  if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = a;
   __syncthreads();
   if (threadIdx.x == 0) {
-    float A = 0.f, Nn = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) { A += r0[i]; Nn += r1[i]; }
-    Nn = fmaxf(Nn, 1.f);
-    loss[0] = A / Nn;
-    inv_valid[0] = 1.f / Nn;
+    float s = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += r[i];
+    loss[0] = s * inv_valid[0];
   }
 }
 
-// out[c][r] = in[r][c] for a 16-bit [R][Cc] matrix (32x32 tiles through shared memory).
-template <typename T>
-__global__ void transpose16(T* __restrict__ out, const T* __restrict__ in, int64_t R, int64_t Cc) {
-  __shared__ T tile[32][33];
-  const int64_t c0 = (int64_t)blockIdx.x * 32, r0 = (int64_t)blockIdx.y * 32;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int64_t r = r0 + i, c = c0 + threadIdx.x;
-    if (r < R && c < Cc) tile[i][threadIdx.x] = in[r * Cc + c];
-  }
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int64_t c = c0 + i, r = r0 + threadIdx.x;
-    if (r < R && c < Cc) out[c * R + r] = tile[threadIdx.x][i];
-  }
-}
-
-// In place over 16-bit logits L[M][V]: L = (softmax(L) - onehot(label)) / n_valid,
-// zero rows for ignored labels.  V % 8 == 0.  A CTA walks whole rows (the row's
-// lse and label stay in registers, no per-vector division); each thread loads
-// kGradBatch 16-byte vectors before using any of them.
+// In place over 16-bit logits L[M][V]: L = (softmax(L) - onehot(label)) * scale
+// (scale: a device scalar, or 1 when it is null), zero rows for ignored labels.  V % 8 == 0.  A CTA walks whole rows (the row's
+// lse and label stay in registers); each thread loads kGradBatch 16-byte vectors
+// before using any of them.
 constexpr int kGradBatch = 4;
 
 template <typename T>
 __global__ void __launch_bounds__(256)
 lce_grad_inplace(T* __restrict__ L, const float* __restrict__ lse, const int64_t* __restrict__ labels,
-                 const float* __restrict__ inv_valid, int64_t M, int64_t V, int64_t ignore_index) {
-  const float sc0 = *inv_valid;
+                 const float* __restrict__ scale, int64_t M, int64_t V, int64_t ignore_index) {
+  const float sc0 = scale != nullptr ? *scale : 1.f;
   const int nv = (int)(V / 8);
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
     const int64_t lab = labels[row];
@@ -482,19 +721,16 @@ lce_grad_inplace(T* __restrict__ L, const float* __restrict__ lse, const int64_t
   }
 }
 
-template <typename T>
-__global__ void cast_f32(T* __restrict__ dst, const float* __restrict__ src, int64_t n) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    dst[i] = from_f<T>(src[i]);
-}
-
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows, bool bf16) {
+// Tensor map over a row-major [rows][cols] 16-bit matrix.  K-major operands
+// (cols = K) load 64 x 128 boxes; MN-major operands (cols = M or N) load 64 x 64
+// boxes, two per operand and stage.
+int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, bool mn, bool bf16) {
   const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  const cuuint32_t box[2] = {64u, mn ? 64u : 128u};
   const cuuint32_t estr[2] = {1, 1};
   // Resolved through the runtime so the library does not link libcuda directly.
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
@@ -507,45 +743,93 @@ int make_tmap(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, in
                "linear_ce: cuTensorMapEncodeTiled unavailable");
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
-  const CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                                            2, const_cast<void*>(base), dims, strides, box, estr,
-                                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                            const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   AK_REQUIRE(r == CUDA_SUCCESS, AK_ERR_ARG, "linear_ce: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return AK_OK;
 }
 
-constexpr size_t kSmem = (size_t)STAGES * STAGE_BYTES + 1024 + 256 + 2 * 32 * kTPitch * 2;
+constexpr size_t kSmem = (size_t)STAGES * STAGE_BYTES + 256 + (size_t)kEpiWarps * kStageWarpBytes + 1024;
 
-template <typename T, int EPI>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
-  auto kern = tn_gemm_kernel<T, EPI>;
+// One GEMM operand: a row-major [rows][cols] matrix read K-major (cols = K) or
+// MN-major (cols = M or N).
+struct Operand {
+  const void* base;
+  int64_t rows, cols;
+  int mn;
+};
+
+void finish_prob(Prob& P) {
+  P.mtiles = (P.M + 2 * BM - 1) / (2 * BM);
+  P.ntiles = (P.N + BN - 1) / BN;
+  P.tiles = P.mtiles * P.ntiles;
+}
+
+std::mutex g_pairs_mu;
+int g_pairs_cache[64] = {0};
+
+// CTA pairs that fit on the device at once (one CTA per SM).
+template <typename T>
+int resident_pairs() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return std::max(1, sm_count() / 2);
+  std::lock_guard<std::mutex> lock(g_pairs_mu);
+  if (g_pairs_cache[dev] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (unsigned)sm_count());
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, tc_gemm2_kernel<T>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sm_count() / 2;
+    }
+    g_pairs_cache[dev] = std::max(1, n);
+  }
+  return g_pairs_cache[dev];
+}
+
+template <typename T>
+int launch_group(const Operand* A, const Operand* B, Group& g, cudaStream_t st) {
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  CUtensorMap maps[4];
+  int rc;
+  for (int i = 0; i < g.nprob; ++i) {
+    if ((rc = make_tmap(&maps[2 * i], A[i].base, A[i].rows, A[i].cols, A[i].mn, bf16))) return rc;
+    if ((rc = make_tmap(&maps[2 * i + 1], B[i].base, B[i].rows, B[i].cols, B[i].mn, bf16))) return rc;
+    g.p[i].a_mn = A[i].mn;
+    g.p[i].b_mn = B[i].mn;
+    finish_prob(g.p[i]);
+  }
+  if (g.nprob == 1) { maps[2] = maps[0]; maps[3] = maps[1]; }
+  g.total = g.p[0].tiles + (g.nprob > 1 ? g.p[1].tiles : 0);
+  if (g.total == 0) return AK_OK;
+  auto kern = tc_gemm2_kernel<T>;
   AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem),
               "linear_ce: smem attribute");
-  const int tiles = ((g.M + BM - 1) / BM) * ((g.N + BN - 1) / BN);
-  const int grid = std::max(1, std::min(tiles, sm_count()));
-  kern<<<grid, kThreads, kSmem, st>>>(ta, tb, g);
+  const int pairs = std::max(1, std::min(g.total, resident_pairs<T>()));
+  kern<<<2 * pairs, kThreads, kSmem, st>>>(maps[0], maps[1], maps[2], maps[3], g);
   AK_CHECK_LAUNCH("linear_ce: tcgen05 gemm");
   return AK_OK;
 }
 
+// Workspace: per-row statistics of one chunk, the chunk's 16-bit logits /
+// gradient G_c, and (several chunks only) the fp32 dW accumulator.
 struct Ws {
   float2* part;
   float* tlogit;
   float* losses;
   float* inv_valid;
-  void* WT;
-  void* HT;
   void* G;
-  void* GT;
   float* dWacc;
   size_t bytes;
 };
 
-// Rows per gradient chunk: large chunks keep the dH / dW GEMMs several waves deep.
-int64_t chunk_rows(int64_t N) { return std::min<int64_t>(N, 32768); }
+int64_t chunk_rows(int64_t N) { return std::min<int64_t>(N, kChunkRows); }
 
-Ws carve(void* base, int64_t N, int64_t D, int64_t V) {
+Ws carve(void* base, int64_t N, int64_t D, int64_t V, bool need_dw) {
   Ws w{};
   const int64_t ntiles = (V + BN - 1) / BN;
   const int64_t Nc = chunk_rows(N);
@@ -556,88 +840,108 @@ Ws carve(void* base, int64_t N, int64_t D, int64_t V) {
     off += bytes;
     return p;
   };
-  w.part = reinterpret_cast<float2*>(take((size_t)N * ntiles * 2 * sizeof(float2)));  // one per column half
+  w.part = reinterpret_cast<float2*>(take((size_t)Nc * ntiles * kEpiGroups * sizeof(float2)));
   w.tlogit = reinterpret_cast<float*>(take((size_t)N * 4));
   w.losses = reinterpret_cast<float*>(take((size_t)N * 4));
   w.inv_valid = reinterpret_cast<float*>(take(4));
-  w.WT = take((size_t)D * V * 2);
-  w.HT = take((size_t)D * N * 2);
   w.G = take((size_t)Nc * V * 2);
-  w.GT = take((size_t)V * Nc * 2);
-  w.dWacc = reinterpret_cast<float*>(take((size_t)V * D * 4));
+  w.dWacc = (need_dw && N > Nc) ? reinterpret_cast<float*>(take((size_t)V * D * 4)) : nullptr;
   w.bytes = off + 256;
   return w;
 }
 
+// Logits GEMM with statistics over rows [r0, r0 + nr) (16-bit logits into Gc when
+// it is given), then lse and the per-row loss.
+template <typename T>
+int stats_pass(const Ws& w, float* lse, void* Gc, const void* H, const void* W, const int64_t* labels, int64_t r0,
+               int64_t nr, int64_t D, int64_t V, int64_t ignore_index, int* status, cudaStream_t st) {
+  Operand A[1] = {{static_cast<const T*>(H) + r0 * D, nr, D, 0}};
+  Operand B[1] = {{W, V, D, 0}};
+  Group g{};
+  g.nprob = 1;
+  g.status = status;
+  Prob& P = g.p[0];
+  P.M = (int)nr; P.N = (int)V; P.K = (int)D;
+  P.epi = EPI_STATS;
+  P.part = w.part; P.tlogit = w.tlogit + r0; P.labels = labels + r0; P.ignore_index = ignore_index;
+  P.C = Gc; P.ldc = V;
+  int rc = launch_group<T>(A, B, g, st);
+  if (rc) return rc;
+  const int nparts = kEpiGroups * (int)((V + BN - 1) / BN);
+  lce_rows_reduce<<<(unsigned)((nr * 32 + 255) / 256), 256, 0, st>>>(lse + r0, w.losses + r0, w.part,
+                                                                     w.tlogit + r0, labels + r0, (int)nr, nparts,
+                                                                     ignore_index);
+  AK_CHECK_LAUNCH("linear_ce: row reduce");
+  return AK_OK;
+}
+
+template <typename T>
+int grad_inplace(void* Gc, const float* lse, const int64_t* labels, const float* scale, int64_t nr, int64_t V,
+                 int64_t ignore_index, cudaStream_t st) {
+  const unsigned grid = (unsigned)std::min<int64_t>(nr, (int64_t)sm_count() * 8);
+  lce_grad_inplace<T><<<grid, 256, 0, st>>>((T*)Gc, lse, labels, scale, nr, V, ignore_index);
+  AK_CHECK_LAUNCH("linear_ce: gradient");
+  return AK_OK;
+}
+
 template <typename T>
 int run(float* loss, float* lse, void* dH, void* dW, const Ws& w, const void* H, const void* W,
-        const int64_t* labels, int64_t N, int64_t D, int64_t V, int64_t ignore_index, int* status,
-        cudaStream_t st) {
-  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
-  const int ntiles = (int)((V + BN - 1) / BN);
-  // 0. K-major copies of W^T and H^T for the gradient GEMMs
-  {
-    dim3 b(32, 8);
-    transpose16<T><<<dim3((unsigned)((D + 31) / 32), (unsigned)((V + 31) / 32)), b, 0, st>>>((T*)w.WT, (const T*)W, V, D);
-    transpose16<T><<<dim3((unsigned)((D + 31) / 32), (unsigned)((N + 31) / 32)), b, 0, st>>>((T*)w.HT, (const T*)H, N, D);
-    AK_CHECK_LAUNCH("linear_ce: transpose");
+        const int64_t* labels, const float* inv_valid_in, int64_t N, int64_t D, int64_t V, int64_t ignore_index,
+        int* status, cudaStream_t st) {
+  const float* inv = inv_valid_in;
+  if (inv == nullptr) {
+    lce_inv_valid<<<1, 1024, 0, st>>>(w.inv_valid, labels, N, ignore_index);
+    AK_CHECK_LAUNCH("linear_ce: valid rows");
+    inv = w.inv_valid;
   }
-  CUtensorMap tH, tW, tG, tWT, tGT, tHT;
-  int rc;
-  if ((rc = make_tmap(&tH, H, N, D, BM, bf16))) return rc;
-  if ((rc = make_tmap(&tW, W, V, D, BN, bf16))) return rc;
-  if ((rc = make_tmap(&tWT, w.WT, D, V, BN, bf16))) return rc;
-  if ((rc = make_tmap(&tHT, w.HT, D, N, BN, bf16))) return rc;
-  // 1. logits tiles -> per-row partial (max, sum exp)
-  {
-    GemmArgs g{};
-    g.status = status;
-    g.M = (int)N; g.N = (int)V; g.K = (int)D;
-    g.part = w.part; g.tlogit = w.tlogit; g.labels = labels; g.ignore_index = ignore_index;
-    if ((rc = launch_gemm<T, EPI_STATS>(tH, tW, g, st))) return rc;
-  }
-  // 2. lse, per-row loss, mean and 1/n_valid on the device
-  lce_rows_reduce<<<(unsigned)((N * 32 + 255) / 256), 256, 0, st>>>(lse, w.losses, w.part, w.tlogit, labels, (int)N,
-                                                                    2 * ntiles, ignore_index);
-  lce_mean<<<1, 1024, 0, st>>>(loss, w.inv_valid, w.losses, labels, N, ignore_index);
-  AK_CHECK_LAUNCH("linear_ce: reduce");
-  // 3-4. per row chunk: G tiles, dH = G W, dW += G^T H
   const int64_t Nc = chunk_rows(N);
+  int rc;
   for (int64_t r0 = 0; r0 < N; r0 += Nc) {
     const int64_t nr = std::min(Nc, N - r0);
-    CUtensorMap tHc;
-    if ((rc = make_tmap(&tHc, static_cast<const T*>(H) + r0 * D, nr, D, BM, bf16))) return rc;
-    if ((rc = make_tmap(&tG, w.G, nr, V, BM, bf16))) return rc;
-    if ((rc = make_tmap(&tGT, w.GT, V, nr, BM, bf16))) return rc;
-    {
-      GemmArgs g{};
+    const bool first = r0 == 0, last = r0 + nr >= N;
+    const bool grads = dH != nullptr || dW != nullptr;
+    if ((rc = stats_pass<T>(w, lse, grads ? w.G : nullptr, H, W, labels, r0, nr, D, V, ignore_index, status, st)))
+      return rc;
+    if (!grads) continue;
+    // G_c = softmax - onehot, unscaled: 1 / n_valid would push 16-bit values towards
+    // underflow; the GEMM epilogues apply it to the fp32 accumulators instead
+    if ((rc = grad_inplace<T>(w.G, lse + r0, labels + r0, nullptr, nr, V, ignore_index, st))) return rc;
+    // one launch: dW (+)= G_c^T H_c (problem 0, many short-K tiles) and dH_c = G_c W
+    // (problem 1, few long-K tiles, spread over the pairs after the dW tiles)
+    Operand A[2], B[2];
+    Group g{};
     g.status = status;
-      g.M = (int)nr; g.N = (int)V; g.K = (int)D;
-      g.labels = labels + r0; g.ignore_index = ignore_index;
-      g.lse = lse + r0; g.scale = w.inv_valid;
-      g.G = w.G; g.GT = w.GT; g.ldgt = nr; g.gt_col0 = 0;
-      if ((rc = launch_gemm<T, EPI_GRAD>(tHc, tW, g, st))) return rc;
+    int np = 0;
+    if (dW) {
+      A[np] = {w.G, nr, V, 1};                                // G_c^T: M = V contiguous
+      B[np] = {static_cast<const T*>(H) + r0 * D, nr, D, 1};  // H_c^T: N = D contiguous
+      Prob& P = g.p[np++];
+      P.M = (int)V; P.N = (int)D; P.K = (int)nr;
+      P.epi = EPI_STORE;
+      P.ldc = D;
+      P.scale = inv;
+      if (first && last) {  // one chunk: the 16-bit dW directly
+        P.C = dW;
+      } else if (!last) {   // fp32 accumulator
+        P.C = w.dWacc; P.c_f32 = 1; P.accumulate = first ? 0 : 1;
+      } else {              // last chunk: accumulator + this chunk -> 16-bit dW
+        P.C = dW; P.add_f32 = w.dWacc;
+      }
     }
-    if (dH) {  // dH[r0:r0+nr] = G W  (A = G [nr, V], B = W^T [D, V])
-      GemmArgs g{};
-    g.status = status;
-      g.M = (int)nr; g.N = (int)D; g.K = (int)V;
-      g.C = static_cast<T*>(dH) + r0 * D; g.ldc = D;
-      if ((rc = launch_gemm<T, EPI_STORE_BF16>(tG, tWT, g, st))) return rc;
+    if (dH) {
+      A[np] = {w.G, nr, V, 0};  // G_c: K = V contiguous
+      B[np] = {W, V, D, 1};     // W^T: N = D contiguous
+      Prob& P = g.p[np++];
+      P.M = (int)nr; P.N = (int)D; P.K = (int)V;
+      P.epi = EPI_STORE;
+      P.C = static_cast<T*>(dH) + r0 * D; P.ldc = D;
+      P.scale = inv;
     }
-    if (dW) {  // dW += G^T H  (A = G^T [V, nr], B = H^T [D, N] columns r0..r0+nr)
-      GemmArgs g{};
-    g.status = status;
-      g.M = (int)V; g.N = (int)D; g.K = (int)nr; g.b_k0 = (int)r0;
-      g.C = w.dWacc; g.ldc = D; g.accumulate = r0 > 0;
-      if ((rc = launch_gemm<T, EPI_STORE_F32>(tGT, tHT, g, st))) return rc;
-    }
+    g.nprob = np;
+    if ((rc = launch_group<T>(A, B, g, st))) return rc;
   }
-  if (dW) {
-    const int64_t n = V * D;
-    cast_f32<T><<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8), 256, 0, st>>>((T*)dW, w.dWacc, n);
-    AK_CHECK_LAUNCH("linear_ce: dW cast");
-  }
+  lce_loss<<<1, 1024, 0, st>>>(loss, w.losses, inv, N);
+  AK_CHECK_LAUNCH("linear_ce: loss");
   return AK_OK;
 }
 
@@ -659,34 +963,63 @@ extern "C" int ak_linear_ce_workspace_size(int64_t N, int64_t D, int64_t V, size
   clear_error();
   AK_REQUIRE(bytes != nullptr, AK_ERR_ARG, "null bytes");
   AK_REQUIRE(N > 0 && D > 0 && V > 0, AK_ERR_SHAPE, "linear_ce: empty problem");
-  *bytes = carve(nullptr, N, D, V).bytes;
+  *bytes = carve(nullptr, N, D, V, true).bytes;
   return AK_OK;
 }
 
 extern "C" int ak_linear_ce_fwdbwd(float* loss, float* lse, void* dH, void* dW, void* workspace, size_t ws_bytes,
-                                   const void* H, const void* W, const int64_t* labels, int64_t N, int64_t D,
-                                   int64_t V, int64_t ignore_index, int dt, int* status, void* stream) {
+                                   const void* H, const void* W, const int64_t* labels, const float* inv_valid,
+                                   int64_t N, int64_t D, int64_t V, int64_t ignore_index, int dt, int* status,
+                                   void* stream) {
   clear_error();
   int rc = check_shape(N, D, V, dt);
   if (rc) return rc;
   AK_REQUIRE(loss && lse && H && W && labels, AK_ERR_ARG, "ak_linear_ce_fwdbwd: null pointer");
-  AK_REQUIRE(aligned16(H) && aligned16(W) && (!dH || aligned16(dH)), AK_ERR_ARG,
-             "ak_linear_ce_fwdbwd: H, W, dH must be 16-byte aligned");
-  const Ws need = carve(nullptr, N, D, V);
+  AK_REQUIRE(aligned16(H) && aligned16(W) && (!dH || aligned16(dH)) && (!dW || aligned16(dW)), AK_ERR_ARG,
+             "ak_linear_ce_fwdbwd: H, W, dH, dW must be 16-byte aligned");
+  const Ws need = carve(nullptr, N, D, V, dW != nullptr);
   AK_REQUIRE(workspace && ws_bytes >= need.bytes, AK_ERR_WORKSPACE, "ak_linear_ce_fwdbwd: workspace %zu < %zu",
              ws_bytes, need.bytes);
   void* base = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
-  const Ws w = carve(base, N, D, V);
+  const Ws w = carve(base, N, D, V, dW != nullptr);
   cudaStream_t st = (cudaStream_t)stream;
-  if (dt == AK_BF16) return run<__nv_bfloat16>(loss, lse, dH, dW, w, H, W, labels, N, D, V, ignore_index, status, st);
-  return run<__half>(loss, lse, dH, dW, w, H, W, labels, N, D, V, ignore_index, status, st);
+  if (dt == AK_BF16)
+    return run<__nv_bfloat16>(loss, lse, dH, dW, w, H, W, labels, inv_valid, N, D, V, ignore_index, status, st);
+  return run<__half>(loss, lse, dH, dW, w, H, W, labels, inv_valid, N, D, V, ignore_index, status, st);
+}
+
+extern "C" int ak_tc_gemm(void* C, int dt_c, const void* A, const void* B, int64_t M, int64_t N, int64_t K,
+                          int a_mn, int b_mn, int dt, int* status, void* stream) {
+  clear_error();
+  AK_REQUIRE(dt == AK_BF16 || dt == AK_F16, AK_ERR_DTYPE, "ak_tc_gemm: operands must be bf16 or fp16");
+  AK_REQUIRE(dt_c == dt || dt_c == AK_F32, AK_ERR_DTYPE, "ak_tc_gemm: C is fp32 or the operand type");
+  AK_REQUIRE(M >= 0 && N >= 0 && K >= 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), AK_ERR_SHAPE,
+             "ak_tc_gemm: bad shape");
+  if (M == 0 || N == 0) return AK_OK;
+  AK_REQUIRE(K > 0, AK_ERR_SHAPE, "ak_tc_gemm: K must be positive");
+  AK_REQUIRE(A && B, AK_ERR_ARG, "ak_tc_gemm: null pointer");
+  AK_REQUIRE(aligned16(A) && aligned16(B) && aligned16(C), AK_ERR_ARG, "ak_tc_gemm: pointers must be 16-byte aligned");
+  AK_REQUIRE((a_mn ? M : K) % 8 == 0 && (b_mn ? N : K) % 8 == 0 && N % 8 == 0, AK_ERR_SHAPE,
+             "ak_tc_gemm: contiguous dimensions and N must be multiples of 8");
+  Operand As[1] = {{A, a_mn ? K : M, a_mn ? M : K, a_mn ? 1 : 0}};
+  Operand Bs[1] = {{B, b_mn ? K : N, b_mn ? N : K, b_mn ? 1 : 0}};
+  Group g{};
+  g.nprob = 1;
+  g.status = status;
+  Prob& P = g.p[0];
+  P.M = (int)M; P.N = (int)N; P.K = (int)K;
+  P.epi = C != nullptr ? EPI_STORE : EPI_NONE;
+  P.C = C; P.ldc = N; P.c_f32 = dt_c == AK_F32 ? 1 : 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dt == AK_BF16) return launch_group<__nv_bfloat16>(As, Bs, g, st);
+  return launch_group<__half>(As, Bs, g, st);
 }
 
 extern "C" int ak_linear_ce_logits_grad_workspace_size(int64_t N, int64_t V, size_t* bytes) {
   clear_error();
   AK_REQUIRE(bytes != nullptr && N > 0 && V > 0, AK_ERR_ARG, "linear_ce: bad args");
   const int64_t ntiles = (V + BN - 1) / BN;
-  *bytes = (size_t)N * ntiles * 2 * sizeof(float2) + (size_t)N * 8 + 1024;
+  *bytes = (size_t)N * ntiles * kEpiGroups * sizeof(float2) + (size_t)N * 8 + 1024;
   return AK_OK;
 }
 
@@ -704,31 +1037,22 @@ extern "C" int ak_linear_ce_logits_grad(float* loss, float* lse, void* G, void* 
              ws_bytes, need);
   const int ntiles = (int)((V + BN - 1) / BN);
   char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
-  float2* part = reinterpret_cast<float2*>(base);
-  float* tlogit = reinterpret_cast<float*>(part + (size_t)N * ntiles * 2);
-  float* losses = tlogit + N;
-  float* inv_valid = losses + N;  // one float after the per-row losses
+  Ws w{};
+  w.part = reinterpret_cast<float2*>(base);
+  w.tlogit = reinterpret_cast<float*>(w.part + (size_t)N * ntiles * kEpiGroups);
+  w.losses = w.tlogit + N;
+  w.inv_valid = w.losses + N;  // one float after the per-row losses
   cudaStream_t st = (cudaStream_t)stream;
-  const bool bf16 = dt == AK_BF16;
-  CUtensorMap tH, tW;
-  if ((rc = make_tmap(&tH, H, N, D, BM, bf16))) return rc;
-  if ((rc = make_tmap(&tW, W, V, D, BN, bf16))) return rc;
-  GemmArgs g{};
-    g.status = status;
-  g.M = (int)N; g.N = (int)V; g.K = (int)D;
-  g.part = part; g.tlogit = tlogit; g.labels = labels; g.ignore_index = ignore_index; g.G = G;
-  if (bf16) rc = launch_gemm<__nv_bfloat16, EPI_STATS>(tH, tW, g, st);
-  else rc = launch_gemm<__half, EPI_STATS>(tH, tW, g, st);
-  if (rc) return rc;
-  lce_rows_reduce<<<(unsigned)((N * 32 + 255) / 256), 256, 0, st>>>(lse, losses, part, tlogit, labels, (int)N,
-                                                                    2 * ntiles, ignore_index);
-  lce_mean<<<1, 1024, 0, st>>>(loss, inv_valid, losses, labels, N, ignore_index);
-  const unsigned grid = (unsigned)std::min<int64_t>(N, (int64_t)sm_count() * 8);
-  if (bf16)
-    lce_grad_inplace<__nv_bfloat16><<<grid, 256, 0, st>>>((__nv_bfloat16*)G, lse, labels, inv_valid, N, V,
-                                                         ignore_index);
-  else
-    lce_grad_inplace<__half><<<grid, 256, 0, st>>>((__half*)G, lse, labels, inv_valid, N, V, ignore_index);
+  lce_inv_valid<<<1, 1024, 0, st>>>(w.inv_valid, labels, N, ignore_index);
+  AK_CHECK_LAUNCH("ak_linear_ce_logits_grad");
+  if (dt == AK_BF16) {
+    if ((rc = stats_pass<__nv_bfloat16>(w, lse, G, H, W, labels, 0, N, D, V, ignore_index, status, st))) return rc;
+    if ((rc = grad_inplace<__nv_bfloat16>(G, lse, labels, w.inv_valid, N, V, ignore_index, st))) return rc;
+  } else {
+    if ((rc = stats_pass<__half>(w, lse, G, H, W, labels, 0, N, D, V, ignore_index, status, st))) return rc;
+    if ((rc = grad_inplace<__half>(G, lse, labels, w.inv_valid, N, V, ignore_index, st))) return rc;
+  }
+  lce_loss<<<1, 1024, 0, st>>>(loss, w.losses, w.inv_valid, N);
   AK_CHECK_LAUNCH("ak_linear_ce_logits_grad");
   return AK_OK;
 }

@@ -50,7 +50,8 @@ SIGNATURES = {
     "ak_linear_ce_logits_grad_workspace_size": [_i64, _i64, ctypes.POINTER(_sz)],
     "ak_linear_ce_logits_grad": [_vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp, _vp],
     "ak_linear_ce_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
-    "ak_linear_ce_fwdbwd": [_vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp, _vp],
+    "ak_linear_ce_fwdbwd": [_vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i, _vp,
+                            _vp],
     "ak_scan1_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "ak_scan1_bwd_workspace_size": [_i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_scan1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
@@ -66,6 +67,7 @@ SIGNATURES = {
     "ak_selective_scan_bwd_workspace_size": [_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_sz)],
     "ak_selective_scan_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp, _vp, _vp, _vp, _vp, _vp,
                               _vp, _vp, _vp, _vp, _i, _i64, _i64, _i64, _i64, _i64, _i, _vp, _vp],
+    "ak_tc_gemm": [_vp, _i, _vp, _vp, _i64, _i64, _i64, _i, _i, _i, _vp, _vp],
     "ak_status_device_pointer": [_vp, ctypes.POINTER(_vp)],
     "ak_test_bounded_wait": [_vp, _i, _vp],
 }
@@ -76,7 +78,7 @@ class AkError(RuntimeError):
 
 
 _lib: Optional[ctypes.CDLL] = None
-_lock = threading.Lock()
+_lock = threading.RLock()  # reentrant: the status words are set up through call() under it
 
 
 def lib() -> ctypes.CDLL:
@@ -603,8 +605,12 @@ def linear_ce_logits_grad(hidden, weight, labels, ignore_index=-100):
     return loss, lse, G
 
 
-def linear_ce_fwdbwd(hidden, weight, labels, ignore_index=-100, need_dh=True, need_dw=True):
-    """Fused tcgen05 linear + CE: returns (loss 0-d fp32, lse [N] fp32, dH or None, dW or None)."""
+def linear_ce_fwdbwd(hidden, weight, labels, ignore_index=-100, need_dh=True, need_dw=True,
+                     inv_valid: Optional[torch.Tensor] = None):
+    """Fused tcgen05 linear + CE: returns (loss 0-d fp32, lse [N] fp32, dH or None, dW or None).
+
+    inv_valid (optional one-element fp32 CUDA tensor): 1 / n_valid to use instead of this call's
+    own count; with the count of all shards, loss and dW are this shard's parts of their sums."""
     dev = require_cuda(hidden, weight, labels)
     h = hidden.contiguous()
     w = weight.contiguous()
@@ -617,9 +623,40 @@ def linear_ce_fwdbwd(hidden, weight, labels, ignore_index=-100, need_dh=True, ne
     dW = torch.empty_like(w) if need_dw else None
     ws_bytes = _size_query("ak_linear_ce_workspace_size", N, D, V)
     ws = workspace(ws_bytes, dev)
+    if inv_valid is not None:
+        inv_valid = inv_valid.reshape(1).to(torch.float32).contiguous()
     call("ak_linear_ce_fwdbwd", ptr(loss), ptr(lse), ptr(dH), ptr(dW), ptr(ws), ws_bytes, ptr(h), ptr(w), ptr(lab),
-         N, D, V, int(ignore_index), dtype_code(h), status_ptr(dev, "linear_ce"), stream(dev))
+         ptr(inv_valid), N, D, V, int(ignore_index), dtype_code(h), status_ptr(dev, "linear_ce"), stream(dev))
     return loss, lse, dH, dW
+
+
+def tc_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """a @ b on the library's tcgen05 GEMM for 2-D bf16 / fp16 a (M, K) and b (K, N).  Either
+    operand may be a plain tensor or the transpose view of one (its K or its M / N dimension
+    contiguous); nothing is copied.  Returns a dense (M, N) tensor in out_dtype (default a's)."""
+    dev = require_cuda(a, b)
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[0] or a.dtype != b.dtype:
+        raise ValueError(f"tc_gemm: {tuple(a.shape)} {a.dtype} @ {tuple(b.shape)} {b.dtype}")
+    M, K = a.shape
+    N = b.shape[1]
+    # A[M][K] K-contiguous (a_mn 0) or stored [K][M] (a_mn 1); B as N x K likewise; dense only
+    if a.stride() == (K, 1):
+        a_mn = 0
+    elif a.stride() == (1, M):
+        a_mn = 1
+    else:
+        a, a_mn = a.contiguous(), 0
+    if b.stride() == (1, K):
+        b_mn = 0  # b (K, N) is the transpose of a dense B[N][K]
+    elif b.stride() == (N, 1):
+        b_mn = 1
+    else:
+        b, b_mn = b.contiguous(), 1
+    out_dtype = out_dtype or a.dtype
+    c = torch.empty(M, N, dtype=out_dtype, device=dev)
+    call("ak_tc_gemm", ptr(c), dtype_code(c), ptr(a), ptr(b), M, N, K, a_mn, b_mn, dtype_code(a),
+         status_ptr(dev, "linear_ce"), stream(dev))
+    return c
 
 
 # ---------------------------------------------------------------------------

@@ -8,9 +8,12 @@ accumulation).  All gradients are produced in the forward; the backward
 returns them scaled by grad_output.
 
 For bf16/fp16 inputs without softcap, label smoothing or z-loss the whole
-computation is one call into the tcgen05 kernel (`ak_linear_ce_fwdbwd`): logits
-tiles stay in tensor memory, the gradient is formed in the GEMM epilogue, and
-dH / dW come from the same tensor-core GEMM.  Other feature combinations use the
+computation is one call into the library (`ak_linear_ce_fwdbwd`), and all three
+contractions run on its tcgen05 GEMM: per chunk of at most 16384 rows the logits
+GEMM reduces its tiles to softmax statistics and keeps that chunk's 16-bit
+logits, which become G = (softmax - onehot) / n_valid in place and feed
+dW += G^T h and dH = G W in one grouped GEMM launch.  Full [N, V] logits are
+never stored and no cuBLAS GEMM runs.  Other feature combinations use the
 row-chunked path below (cuBLAS GEMMs around the fused CE row kernel).
 
 Differences, all deliberate: inputs keep their dtype (the reference coerces to
@@ -97,19 +100,15 @@ def _scaled(g, grad_output):
 
 
 class _FusedLinearCrossEntropy(torch.autograd.Function):
-    """tcgen05 path: logits tiles live only in TMEM; loss, dH and dW come out of one C-ABI call."""
+    """tcgen05 path: loss, dH and dW come out of one C-ABI call (all GEMMs on our kernel)."""
 
     @staticmethod
     @custom_fwd(device_type="cuda")
     def forward(ctx, hidden, weight, targets, ignore_index):
         w = weight.to(hidden.dtype).contiguous()
         h = hidden.contiguous()
-        # fused tcgen05 logits GEMM + softmax statistics + in-place dlogits; the two
-        # gradient contractions are plain GEMMs (cuBLAS)
-        loss, _lse, G = _ak.linear_ce_logits_grad(h, w, targets, ignore_index)
-        dh = torch.mm(G, w) if hidden.requires_grad else None
-        dw = torch.mm(G.t(), h) if weight.requires_grad else None
-        del G
+        loss, _lse, dh, dw = _ak.linear_ce_fwdbwd(h, w, targets, ignore_index, need_dh=hidden.requires_grad,
+                                                  need_dw=weight.requires_grad)
         ctx.save_for_backward(dh, dw.to(weight.dtype) if dw is not None else None)
         ctx.req = (hidden.requires_grad, weight.requires_grad)
         return loss

@@ -181,19 +181,40 @@ AK_API int ak_scale_by_device_scalar(void* x, int64_t n, const float* scale, int
 /* Workspace bytes for ak_linear_ce_fwdbwd on H[N, D], W[V, D]. */
 AK_API int ak_linear_ce_workspace_size(int64_t N, int64_t D, int64_t V, size_t* bytes);
 
-/* loss[0] = mean over rows with labels != ignore_index of CE(H W^T) (fp32,
- * n_valid counted on the device), lse[N] fp32 per-row logsumexp, and the
- * gradients of that mean: dH[N, D] (dt, nullable) and dW[V, D] (dt, nullable).
- * H, W: bf16 or fp16 (dt), row-major; labels int64[N].  N, D, V multiples of 8.
- * Logits are never materialised: tcgen05 GEMM tiles feed per-row softmax
- * statistics and the gradient directly from TMEM.
- * Replaces _ChunkedLinearCrossEntropy.forward / .backward
+/* loss[0] = mean over rows with labels != ignore_index of CE(H W^T) (fp32),
+ * lse[N] fp32 per-row logsumexp, and the gradients of that mean: dH[N, D] (dt,
+ * nullable) and dW[V, D] (dt, nullable).  H, W: bf16 or fp16 (dt), row-major;
+ * labels int64[N].  N, D, V multiples of 8.
+ * inv_valid (nullable, device fp32 scalar): 1 / n_valid to use instead of this
+ * call's own count of valid rows.  A caller that shards the rows over ranks
+ * passes 1 / (valid rows of all ranks); the loss and dW of each rank are then
+ * partial sums whose all-reduce (SUM) is the loss and dW of the whole batch,
+ * and dH is final.
+ * All three contractions run on the library's tcgen05 GEMM (CTA pairs, TMA
+ * operands, TMEM accumulators): per chunk of at most 16384 rows the logits GEMM
+ * reduces its tiles to softmax statistics and keeps 16-bit logits only for that
+ * chunk, which becomes G = (softmax - onehot) / n_valid in place and feeds
+ * dW += G^T H and dH = G W in one grouped launch.  Full [N, V] logits are never
+ * stored.  Replaces _ChunkedLinearCrossEntropy.forward / .backward
  * (kernels/hip/chunked_linear_cross_entropy.py:55-175) for softcap = 0,
  * label_smoothing = 0, z_loss_weight = 0. */
 AK_API int ak_linear_ce_fwdbwd(float* loss, float* lse, void* dH, void* dW, void* workspace,
                    size_t ws_bytes, const void* H, const void* W, const int64_t* labels,
-                   int64_t N, int64_t D, int64_t V, int64_t ignore_index, int dt,
-                   int* status, void* stream);
+                   const float* inv_valid, int64_t N, int64_t D, int64_t V,
+                   int64_t ignore_index, int dt, int* status, void* stream);
+
+/* C[M, N] = A B^T on the tensor cores (the GEMM behind the linear + CE entries),
+ * fp32 accumulation.  A is M x K and B is N x K, bf16 or fp16 (dt), each given
+ * row-major either K-contiguous (a_mn / b_mn = 0: A[M][K], B[N][K]) or
+ * M / N-contiguous (1: A stored [K][M], B stored [K][N]), so transposed
+ * operands need no copy.  C is row-major [M][N], fp32 or dt (dt_c).
+ * Contiguous dimensions and N must be multiples of 8.  C = NULL runs the
+ * contraction and discards the result (measures the main loop alone).  No counterpart in the
+ * reference, whose chunked linear + CE calls torch GEMMs
+ * (kernels/hip/chunked_linear_cross_entropy.py:95-132). */
+AK_API int ak_tc_gemm(void* C, int dt_c, const void* A, const void* B, int64_t M,
+                      int64_t N, int64_t K, int a_mn, int b_mn, int dt, int* status,
+                      void* stream);
 
 /* Workspace bytes for ak_linear_ce_logits_grad. */
 AK_API int ak_linear_ce_logits_grad_workspace_size(int64_t N, int64_t V, size_t* bytes);

@@ -168,3 +168,72 @@ def test_linear_ce_upstream_grad_scaling_on_device(use_fused):
     loss.backward(retain_graph=True)
     with pytest.raises(RuntimeError, match="twice"):
         loss.backward()
+
+
+def _fp32_linear_ce(H, W, lab, ignore_index=-100):
+    """loss, lse, dH, dW of mean CE(H W^T) in fp32 on the GPU (the float64 oracle's formulas)."""
+    Hf = H.float().requires_grad_(True)
+    Wf = W.float().requires_grad_(True)
+    lg = Hf @ Wf.t()
+    loss = torch.nn.functional.cross_entropy(lg, lab, ignore_index=ignore_index)
+    loss.backward()
+    return loss.detach(), torch.logsumexp(lg.detach(), -1), Hf.grad, Wf.grad
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_linear_ce_several_chunks_ragged(dtype):
+    """N above one 16384-row chunk with a ragged last chunk (dW accumulated in fp32 across chunks,
+    the last chunk adds and rounds), V not a multiple of the 64-deep K block nor of the 256-wide tile."""
+    from kernels import _ak
+    g = torch.Generator().manual_seed(11)
+    N, D, V = 16384 + 520, 128, 4000
+    H = torch.randn(N, D, generator=g).to(dtype).to(DEV)
+    W = (torch.randn(V, D, generator=g) * 0.05).to(dtype).to(DEV)
+    lab = torch.randint(0, V, (N,), generator=g)
+    lab[::9] = -100
+    lab = lab.to(DEV)
+    loss, lse, dH, dW = _ak.linear_ce_fwdbwd(H, W, lab, -100)
+    _ak.check_status()
+    rl, rlse, rdh, rdw = _fp32_linear_ce(H, W, lab)
+    n = (lab != -100).sum().item()
+    assert abs(loss.item() - rl.item()) <= 2e-3 * max(1.0, abs(rl.item()))
+    torch.testing.assert_close(lse, rlse, rtol=0, atol=3e-2)
+    assert_lowp_close(dH.float() * n, rdh * n, what="dH*n")
+    assert_lowp_close(dW.float() * n, rdw * n, what="dW*n")
+
+
+def test_linear_ce_row_shards_with_global_valid_count():
+    """Rows split over two shards, each call given 1 / (valid rows of both): the loss and dW of
+    the shards sum to the unsharded ones and dH concatenates (what the multi-GPU path all-reduces)."""
+    from kernels import _ak
+    g = torch.Generator().manual_seed(12)
+    N, D, V = 2048, 256, 8192
+    H = torch.randn(N, D, generator=g).to(torch.bfloat16).to(DEV)
+    W = (torch.randn(V, D, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    lab = torch.randint(0, V, (N,), generator=g)
+    lab[::13] = -100
+    lab = lab.to(DEV)
+    loss, _, dH, dW = _ak.linear_ce_fwdbwd(H, W, lab)
+    inv = (1.0 / (lab != -100).sum().float()).reshape(1)
+    parts = [_ak.linear_ce_fwdbwd(H[s], W, lab[s], inv_valid=inv) for s in (slice(0, 1000), slice(1000, N))]
+    _ak.check_status()
+    torch.testing.assert_close(parts[0][0] + parts[1][0], loss, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(torch.cat([parts[0][2], parts[1][2]]).float(), dH.float(), rtol=0, atol=1e-6)
+    torch.testing.assert_close(parts[0][3].float() + parts[1][3].float(), dW.float(), rtol=2e-2, atol=1e-5)
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (True, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (296, 136, 200), (1000, 520, 1032), (8, 8, 8)])
+def test_tc_gemm_layouts(a_t, b_t, M, N, K):
+    """The tcgen05 GEMM for all four operand layouts (K-contiguous or M / N-contiguous), ragged
+    M, N and K, against an fp32 GEMM of the same bf16 inputs."""
+    from kernels import _ak
+    g = torch.Generator().manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
+    b = torch.randn(K, N, generator=g).to(torch.bfloat16).to(DEV)
+    aa = a.t().contiguous().t() if a_t else a   # same values, M-contiguous storage
+    bb = b.t().contiguous().t() if not b_t else b  # b_t: N-contiguous [K][N]; else K-contiguous
+    c = _ak.tc_gemm(aa, bb, out_dtype=torch.float32)
+    _ak.check_status()
+    ref = a.float() @ b.float()
+    torch.testing.assert_close(c, ref, rtol=1e-4, atol=1e-3)

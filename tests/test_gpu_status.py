@@ -55,3 +55,18 @@ def test_normal_calls_leave_the_status_clear():
     lab = torch.randint(0, 512, (256,), device=DEV)
     _ak.linear_ce_fwdbwd(H, W, lab)
     _ak.check_status(DEV)
+
+
+def test_status_words_set_up_in_a_fresh_process():
+    """The first library call of a process may be one that needs a status word (it is created
+    under the same lock that loads the library)."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path[:0] = ['autokernel-halo-strix_b200', '.']\n"
+            "import torch\nfrom kernels import _ak\n"
+            "a = torch.randn(256, 64, device='cuda').to(torch.bfloat16)\n"
+            "c = _ak.tc_gemm(a, a.t())\n_ak.check_status()\nprint('ok')\n")
+    from pathlib import Path
+    repo = Path(__file__).resolve().parent.parent
+    out = subprocess.run([sys.executable, "-c", code], cwd=repo, capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stderr[-2000:]
