@@ -227,6 +227,52 @@ def time_sscan(cfg, dev, steps, warmup, world):
     return total_ms, fwd_ms, bwd_ms, clk.summary(), host
 
 
+def time_comparator(dev, host, steps, warmup, our_fwd_ms, our_bwd_ms):
+    """The reference's own GPU kernel for the headline scan (mamba_ssm 2.3.0 `selective_scan_cuda`,
+    built for sm_100a from the reference sources into oracle/_ref/ by oracle/build_mamba_ref.py),
+    timed in this process on the same inputs with the same CUDA-event protocol as ours.  It is a
+    reference arm, not our measurement; None when the module was not built."""
+    try:
+        from oracle.build_mamba_ref import load_built
+        mod = load_built()
+    except Exception as e:  # noqa: BLE001 - a missing comparator never stops the bench
+        return {"unavailable": f"comparator failed to load: {e}"[:200]}
+    if mod is None:
+        return {"unavailable": "reference selective_scan_cuda not built (needs the reference checkout)"}
+    d = {k: v.to(dev) for k, v in host.items()}
+    B4, C4 = d["B"].unsqueeze(1), d["C"].unsqueeze(1)
+    st = torch.cuda.current_stream(dev)
+
+    def fwd():
+        return mod.fwd(d["u"], d["delta"], d["A"], B4, C4, d["D"], d["z"], d["delta_bias"], True)
+
+    def bwd(r):
+        out, x, _ = r
+        mod.bwd(d["u"], d["delta"], d["A"], B4, C4, d["D"], d["z"], d["delta_bias"], d["dout"], x, out, None,
+                True, False)
+
+    for _ in range(warmup):
+        bwd(fwd())
+    torch.cuda.synchronize(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for e in evs:
+        e[0].record(st)
+        r = fwd()
+        e[1].record(st)
+        bwd(r)
+        e[2].record(st)
+    torch.cuda.synchronize(dev)
+    rf = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    rb = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    del d
+    torch.cuda.empty_cache()
+    return {"impl": "mamba_ssm 2.3.0 selective_scan_cuda (reference sources, built for sm_100a)",
+            "fwd_ms": round(rf, 4), "bwd_ms": round(rb, 4), "total_ms": round(rf + rb, 4),
+            "ours_total_ms": round(our_fwd_ms + our_bwd_ms, 4),
+            "speedup_fwd": round(rf / our_fwd_ms, 3), "speedup_bwd": round(rb / our_bwd_ms, 3),
+            "speedup_total": round((rf + rb) / (our_fwd_ms + our_bwd_ms), 3)}
+
+
 def time_sscan_e2e(cfg, dev, steps, warmup, host, slices=4):
     """Same step through the public API (selective_scan_fn + autograd) with inputs in pinned
     host memory: every step copies all its inputs H2D and reads a result (last_state) back D2H.
@@ -612,6 +658,122 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
     return res
 
 
+def time_sharded_ops(dev, world, rank, steps, warmup, hbm_peak, bf16_peak):
+    """Strong scaling of the per-op BASELINE configs (the split of kernels/sharded.py): each
+    config's rows are split over the `world` ranks and every rank runs its block; the collectives
+    the split needs (linear + CE: valid count, loss and dW; scan: dA, dD, ddelta_bias) run inside
+    the timed region on the launching stream.  t_N = max over ranks of the CUDA-event time per
+    step.  t_1 = the whole config on one GPU, measured in the same run on every rank's own GPU at
+    once (no data is shared, so the ranks do not disturb each other) and max-reduced.  Efficiency
+    = t_1 / (N * t_N).  Each repetition is preceded by a 256 MB write that flushes L2 (its own
+    time, measured alone, is subtracted), so a block that fits in L2 is not read from it."""
+    from kernels import _ak, sharded
+    st = torch.cuda.current_stream(dev)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    def timed(fn, reps):
+        for _ in range(warmup):
+            flush.zero_()
+            fn()
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record(st)
+        for _ in range(reps):
+            flush.zero_()
+        b.record(st)
+        for _ in range(reps):
+            flush.zero_()
+            fn()
+        c.record(st)
+        torch.cuda.synchronize(dev)
+        return max(b.elapsed_time(c) - a.elapsed_time(b), 1e-6) / reps  # (flush + op) - flush
+
+    res = {}
+
+    def report(name, t1, tn, amount, unit, peak, **extra):
+        t1 = max_over_ranks(t1, world, dev)
+        tn = max_over_ranks(tn, world, dev)
+        agg = amount / (tn / 1e3) / (1e9 if unit == "GB/s" else 1e12)
+        # frac: aggregate over the sum of the ranks' peaks
+        res[name] = {"ms_1gpu": round(t1, 4), "ms_sharded": round(tn, 4), unit: round(agg, 1),
+                     "frac_per_gpu": round(agg / (world * peak), 3), "efficiency": round(t1 / (world * tn), 3),
+                     **extra}
+
+    def both(full_fn, local_fn, reps):
+        # the collectives in local_fn need every rank; full_fn runs on every rank's own GPU
+        return timed(full_fn, reps), timed(local_fn, reps)
+
+    # RMSNorm fp32 [8192, 768] fwd + bwd (config 0); the global dW is all-reduced (768 floats)
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn(8192, 768, generator=gen).to(dev)
+    w = (1 + 0.02 * torch.randn(768, generator=gen)).to(dev)
+    dy = torch.randn(8192, 768, generator=gen).to(dev)
+    xl, dyl = sharded.local_rows(x), sharded.local_rows(dy)
+    # dW left as this rank's partial sum (in data-parallel training the gradient all-reduce sums
+    # it); the time with its own 768-float all-reduce is reported beside it
+    t1, tn = both(lambda: (_ak.rmsnorm_fwd(x, w, 1e-6), _ak.rmsnorm_bwd(x, w, dy, 1e-6)),
+                  lambda: (_ak.rmsnorm_fwd(xl, w, 1e-6),
+                           sharded.rmsnorm_bwd_sharded(xl, w, dyl, 1e-6, global_dw=False)), steps * 2)
+    tg = timed(lambda: (_ak.rmsnorm_fwd(xl, w, 1e-6), sharded.rmsnorm_bwd_sharded(xl, w, dyl, 1e-6)), steps * 2)
+    E = 8192 * 768
+    report("rmsnorm_fp32_8192x768_fwd_bwd", t1, tn, 5 * E * 4 + 3 * 768 * 4, "GB/s", hbm_peak,
+           ms_sharded_with_dw_allreduce=round(max_over_ranks(tg, world, dev), 4))
+    del x, dy, xl, dyl
+
+    # Softmax causal bf16 [196608, 2048] fwd + bwd (config 3)
+    rows, cols = 96 * 2048, 2048
+    s = (torch.randn(rows, cols, device=dev) / 8).to(torch.bfloat16)
+    r = torch.arange(rows, device=dev) % cols
+    s.masked_fill_(torch.arange(cols, device=dev)[None, :] > r[:, None], float("-inf"))
+    dys = torch.randn(rows, cols, device=dev).to(torch.bfloat16)
+    sl, dysl = sharded.local_rows(s), sharded.local_rows(dys)
+    t1, tn = both(lambda: _ak.softmax_bwd(_ak.softmax_fwd(s), dys),
+                  lambda: _ak.softmax_bwd(_ak.softmax_fwd(sl), dysl), steps)
+    report("softmax_bf16_196608x2048_fwd_bwd", t1, tn, 5 * rows * cols * 2, "GB/s", hbm_peak)
+    del s, dys, sl, dysl, r
+    torch.cuda.empty_cache()
+
+    # Mamba selective scan (config 1): batch rows 8 / N per rank; dA, dD, ddelta_bias all-reduced
+    cfg = dict(HEADLINE)
+    host = make_sscan_inputs(cfg, dev, seed=1234)
+    d = {k: v.to(dev) for k, v in host.items()}
+    dl = {k: (sharded.local_rows(v) if v.dim() == 3 else v) for k, v in d.items()}
+
+    def scan(t, collect):
+        out, last, states = _ak.selective_scan_fwd(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
+                                                   t["delta_bias"], True)
+        gr = _ak.selective_scan_bwd(t["dout"], t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], t["z"],
+                                    t["delta_bias"], True, states)
+        if collect:
+            sharded.selective_scan_bwd_sharded(gr)
+
+    t1, tn = both(lambda: scan(d, False), lambda: scan(dl, True), steps)
+    fb, bb = sscan_bytes(cfg["batch"], cfg["dim"], cfg["L"], cfg["N"], cfg["groups"])
+    report("selective_scan_bf16_B8_D1536_L2048_N16_fwd_bwd", t1, tn, fb + bb, "GB/s", hbm_peak)
+    del d, dl, host
+    torch.cuda.empty_cache()
+
+    # Linear + CE bf16 (config 2): tokens 32768 / N per rank, W replicated; valid count, loss and
+    # dW (bf16, 77 MB) all-reduced
+    Nt, Dh, Vv = 32768, 768, 50304
+    gen = torch.Generator().manual_seed(0)
+    H = torch.randn(Nt, Dh, generator=gen).to(torch.bfloat16).to(dev)
+    W = (torch.randn(Vv, Dh, generator=gen) * 0.02).to(torch.bfloat16).to(dev)
+    lab = torch.randint(0, 50257, (Nt,), generator=gen)
+    lab[torch.randperm(Nt, generator=gen)[: Nt // 20]] = -100
+    lab = lab.to(dev)
+    Hl, labl = sharded.local_rows(H), sharded.local_rows(lab)
+    reps = max(3, steps // 4)
+    t1, tn = both(lambda: _ak.linear_ce_fwdbwd(H, W, lab, -100),
+                  lambda: sharded.linear_ce_sharded(Hl, W, labl, -100), reps)
+    report("linear_ce_bf16_32768x768x50304_fwd_bwd", t1, tn, 3 * 2 * Nt * Dh * Vv, "TFLOP/s", bf16_peak)
+    del H, W, lab, Hl, labl, flush
+    torch.cuda.empty_cache()
+    return {"n_gpus": world, "scaling": "strong (fixed total work split over the ranks)",
+            "l2": "256 MB write before each repetition, its time subtracted", **res}
+
+
 def profile_train_step(dev, micro_batch=16, seq=1024):
     """One 124M training step (the CUDA-graph step the bench times) bracketed by
     cudaProfilerStart / Stop after the eager warm-up, capture and one replay."""
@@ -695,9 +857,14 @@ def run_ours(args, world, rank, local):
         e2e_ms, h2d, d2h = time_sscan_e2e(cfg, dev, max(2, args.steps // 2), 2, host)
         e2e_ms = max_over_ranks(e2e_ms, world, dev)
         e2e_value = round(world * (fwd_b + bwd_b) / (e2e_ms / 1e3) / 1e9, 2)
+    comparator = None
+    if rank == 0 and world == 1 and not args.no_comparator:
+        comparator = time_comparator(dev, host, args.steps, args.warmup, fwd_avg, bwd_avg)
     ops = time_other_ops(dev, args.steps, args.warmup, hbm_peak, tf_peak) if (rank == 0 and not args.no_ops) else None
     train = None if args.no_train else time_train(dev, args.train_steps, 3, world, rank)
     sharded = None
+    if not args.no_sharded:
+        sharded = time_sharded_ops(dev, world, rank, args.steps, args.warmup, hbm_peak, tf_peak)
     if rank != 0:
         return
     line = {
@@ -739,6 +906,8 @@ def run_ours(args, world, rank, local):
         "gpu_launches": 4 * args.steps,
         "clocks": clocks,
     }
+    if comparator is not None:
+        line["comparator"] = comparator
     if ops is not None:
         line["ops"] = ops
     if train is not None:
@@ -759,6 +928,9 @@ def run_ours(args, world, rank, local):
                     summary[k] = f
     if train is not None:
         summary["train_tok_s"] = train["tok_s"]
+    if comparator is not None and "speedup_total" in comparator:
+        summary["scan_speedup_vs_reference_cuda"] = comparator["speedup_total"]
+        summary["scan_bwd_speedup_vs_reference_cuda"] = comparator["speedup_bwd"]
     if sharded is not None:
         for k, v in sharded.items():
             if isinstance(v, dict) and "efficiency" in v:
@@ -816,6 +988,8 @@ def main():
     ap.add_argument("--no-train", action="store_true", help="skip the 124M hybrid training step")
     ap.add_argument("--train-steps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the strong-scaled per-op block")
+    ap.add_argument("--no-comparator", action="store_true", help="skip timing the reference's own CUDA scan")
     ap.add_argument("--only-ops", action="store_true", help="print only the per-op sweep (quick runs)")
     ap.add_argument("--ops", default="", help="with --only-ops: comma list of rmsnorm,softmax,linear_ce,scan1,ce_rows,fused_res,silu_gate,rope,conv1d")
     ap.add_argument("--ce-rows", type=int, default=32768, help="with --only-ops: rows of the linear+CE case")
