@@ -117,7 +117,8 @@ def test_sscan_golden_cuda(groups):
 
 
 @pytest.mark.parametrize("b,dim,L,N,groups", [(2, 8, 300, 16, 1), (1, 4, 1, 8, 1), (2, 16, 513, 16, 2),
-                                              (1, 32, 1024, 16, 1), (2, 6, 77, 4, 3), (1, 64, 260, 32, 1)])
+                                              (1, 32, 1024, 16, 1), (2, 6, 77, 4, 3), (1, 64, 260, 32, 1),
+                                              (1, 40, 100, 20, 1), (3, 200, 64, 16, 4)])
 def test_sscan_fp32(b, dim, L, N, groups):
     _check_sscan(_sscan_inputs(b, dim, L, N, groups, torch.float32, seed=b * dim + L))
 

@@ -119,3 +119,95 @@ def test_cuda_graph_step_matches_eager():
     assert curves[1][-1] < curves[1][0]
     with pytest.raises(ValueError, match="captured"):
         tr.step(idx[:, :128], tgt[:, :128])  # a captured step keeps its input shape
+
+
+def _torch_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False):
+    """selective_scan_ref semantics (selective_scan_interface.py:115-181) as a plain fp32 PyTorch
+    loop on the inputs' device, autograd through the loop: the kernels-off scan of the eager model."""
+    f = torch.float32
+    delta = delta.to(f)
+    if delta_bias is not None:
+        delta = delta + delta_bias[..., None].to(f)
+    if delta_softplus:
+        delta = torch.nn.functional.softplus(delta)
+    batch, dim, L = u.shape
+    N = A.shape[1]
+    dA = torch.exp(delta.unsqueeze(-1) * A.to(f).view(1, dim, 1, N))
+    dBu = delta.unsqueeze(-1) * B.to(f).permute(0, 2, 1).unsqueeze(1) * u.to(f).unsqueeze(-1)
+    Cf = C.to(f)
+    x = torch.zeros(batch, dim, N, dtype=f, device=u.device)
+    ys = []
+    for i in range(L):
+        x = dA[:, :, i] * x + dBu[:, :, i]
+        ys.append(torch.einsum("bdn,bn->bd", x, Cf[:, :, i]))
+    out = torch.stack(ys, dim=2)
+    if D is not None:
+        out = out + u.to(f) * D.to(f).view(-1, 1)
+    if z is not None:
+        out = out * torch.nn.functional.silu(z.to(f))
+    return out.to(u.dtype)
+
+
+def _grads(tr, idx, tgt, bf16=True):
+    with torch.autocast("cuda", dtype=torch.bfloat16, enabled=bf16):
+        h = tr.model(idx)
+    loss = tr.loss_fn(h.reshape(-1, h.shape[-1]), tr.raw.lm_head_weight, tgt.reshape(-1))
+    loss.backward()
+    grads = {n: p.grad.float().clone() for n, p in tr.raw.named_parameters()}
+    tr.opt.zero_grad(set_to_none=True)
+    return loss.item(), grads
+
+
+def test_hybrid_124m_bf16_benchmarked_step_tracks_eager():
+    """The 124M step exactly as bench.py runs it (bf16 autocast, tcgen05 fused linear + CE, fused
+    RMSNorm / residual chain / conv / SwiGLU / RoPE kernels, whole-step CUDA graph) against the
+    same model with every kernel off (fp32 PyTorch scan loop, F.rms_norm, SDPA, F.cross_entropy,
+    eager steps), same seed and batch.  Reference check: scripts/test_autokernel_autograd_safety.py
+    :101-112 (every parameter gets a gradient).
+    Step 0: the yardstick is the same kernels-off model in fp32 (autocast off).  Both bf16 runs
+    (kernels on, kernels off) round their matmul operands to bf16 in different kernels and
+    orders, so their gradients scatter around the fp32 ones by a few percent, parameter by
+    parameter, either one ahead (measured: 2e-3 for the kernel path in fp32, about 4e-2 for
+    either path in bf16).  Bound: over all parameters together the kernel path's relative L2
+    error is at most 1.25 x the eager bf16 one; per parameter at most 3 x it + 1e-2, with cosine
+    > 0.99.
+    Then 20 AdamW steps on one batch (memorisation, so the loss moves): the losses stay within
+    1 % of the eager bf16 curve at every step, and both curves fall."""
+    from halo_training.hybrid_lm import HybridConfig
+    from halo_training.train_step import HybridTrainer, eager_loss_fn, synthetic_batch
+    cfg = HybridConfig()
+    dev = torch.device("cuda")
+    idx, tgt = synthetic_batch(2, 1024, cfg.vocab_size, seed=100, device="cuda")
+    on = HybridTrainer(cfg, device=dev, use_kernels=True, seed=0, cuda_graph=True)
+    off = HybridTrainer(cfg, device=dev, use_kernels=False, seed=0, scan_fn=_torch_scan, loss_fn=eager_loss_fn)
+    pon, poff = dict(on.raw.named_parameters()), dict(off.raw.named_parameters())
+    assert set(pon) == set(poff) and all(torch.equal(pon[k], poff[k]) for k in pon)
+
+    l_on, g_on = _grads(on, idx, tgt)
+    l_off, g_off = _grads(off, idx, tgt)
+    l_32, g_32 = _grads(off, idx, tgt, bf16=False)
+    assert abs(l_on - l_32) < 1e-2 and abs(l_off - l_32) < 1e-2, (l_on, l_off, l_32)
+    rows, num_on, num_off, den_all = [], 0.0, 0.0, 0.0
+    for name, ref in g_32.items():
+        got, eag = g_on[name], g_off[name]
+        assert torch.isfinite(got).all() and got.abs().sum() > 0, name
+        den = ref.norm().clamp_min(1e-30)
+        e_on, e_off = ((got - ref).norm() / den).item(), ((eag - ref).norm() / den).item()
+        cos = torch.nn.functional.cosine_similarity(got.flatten(), ref.flatten(), dim=0).item()
+        rows.append((e_on / max(e_off, 1e-12), name, e_on, e_off, cos))
+        num_on += (got - ref).square().sum().item()
+        num_off += (eag - ref).square().sum().item()
+        den_all += ref.square().sum().item()
+        assert e_on <= 3 * e_off + 1e-2 and cos > 0.99, \
+            f"{name}: kernels-on error {e_on:.3e}, eager bf16 error {e_off:.3e} (vs fp32), cosine {cos:.5f}"
+    tot_on, tot_off = (num_on / den_all) ** 0.5, (num_off / den_all) ** 0.5
+    print(f"step-0 gradients vs fp32: all parameters {tot_on:.3e} (kernels on) / {tot_off:.3e} (eager bf16); "
+          f"worst ratios {sorted(rows)[-3:]}")
+    assert tot_on <= 1.25 * tot_off, (tot_on, tot_off)
+
+    curve_on = [on.step(idx, tgt).item() for _ in range(20)]
+    curve_off = [off.step(idx, tgt).item() for _ in range(20)]
+    print("loss curves (kernels on, eager bf16):", list(zip(curve_on, curve_off)))
+    assert all(abs(a - b) <= 1e-2 * max(1.0, abs(b)) for a, b in zip(curve_on, curve_off)), \
+        list(zip(curve_on, curve_off))
+    assert curve_on[-1] < curve_on[0] - 0.5 and curve_off[-1] < curve_off[0] - 0.5
