@@ -747,6 +747,14 @@ __global__ void f32_to2(T* __restrict__ d0, const float* __restrict__ s0, T* __r
   }
 }
 
+// Channels per CTA: 16, halved (down to 4) while the grid would hold fewer than two CTAs per
+// SM, so small batches (one batch row per GPU when the batch is sharded) still fill the GPU.
+int max_channels_per_cta(int64_t batch, int64_t dim) {
+  int c = 16;
+  while (c > 4 && batch * (dim / c) < 2 * (int64_t)sm_count()) c /= 2;
+  return c;
+}
+
 // Channels per CTA: the largest candidate dividing dim/groups.
 void pick_layout(int dpg, int max_cpc, int* nw, int* cpw) {
   const int cands[] = {32, 16, 8, 4, 2, 1};
@@ -810,7 +818,7 @@ extern "C" int ak_selective_scan_fwd(void* out, float* last_state, float* chunk_
   p.dpg = (int)(dim / groups);
   p.softplus = delta_softplus ? 1 : 0;
   p.nsaved = nsaved_of(seqlen);
-  pick_layout(p.dpg, 16, &p.nw, &p.cpw);
+  pick_layout(p.dpg, max_channels_per_cta(batch, dim), &p.nw, &p.cpw);
   const int es = elem_size(dt);
   p.bulk = (((seqlen * es) % 16) == 0 && aligned16(Bm) && aligned16(Cm)) ? 1 : 0;
   p.vec_io = (((seqlen * es) % 16) == 0 && aligned16(u) && aligned16(delta) && aligned16(out) &&
@@ -887,7 +895,7 @@ extern "C" int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB
   p.dpg = (int)(dim / groups);
   p.softplus = delta_softplus ? 1 : 0;
   p.nsaved = nsaved_of(seqlen);
-  pick_layout(p.dpg, 16, &p.nw, &p.cpw);
+  pick_layout(p.dpg, max_channels_per_cta(batch, dim), &p.nw, &p.cpw);
   const int es = elem_size(dt);
   p.bulk = (((seqlen * es) % 16) == 0 && aligned16(Bm) && aligned16(Cm)) ? 1 : 0;
   p.vec_io = (((seqlen * es) % 16) == 0 && aligned16(u) && aligned16(delta) && aligned16(dout) && aligned16(du) &&

@@ -545,21 +545,39 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
         tf3 = flops / (ms3 / 1e3) / 1e12
         res[f"linear_ce_{tag}"] = {
             "ms": ms3, "TFLOP/s": round(tf3, 1), "frac_bf16": round(tf3 / bf16_peak, 3),
-            "note": "ChunkedLinearCrossEntropyLoss path: tcgen05 logits GEMM with fused softmax statistics and "
-                    "in-place dlogits, then dH/dW as plain cuBLAS GEMMs; algorithmic 3*2NDV"}
+            "note": "ChunkedLinearCrossEntropyLoss path (_FusedLinearCrossEntropy -> ak_linear_ce_fwdbwd): "
+                    "logits, dW and dH on our 2-SM tcgen05 GEMM, statistics epilogue, in-place dlogits; "
+                    "algorithmic 3*2NDV"}
         timeit(lambda: _ak.linear_ce_fwdbwd(H, W, lab, -100), 1, "x", max(2, steps // 4))
         ms = res.pop("x")["ms"]
         tf = flops / (ms / 1e3) / 1e12
         res[f"linear_ce_all_tcgen05_{tag}"] = {
             "ms": ms, "TFLOP/s": round(tf, 1), "frac_bf16": round(tf / bf16_peak, 3),
-            "note": "ak_linear_ce_fwdbwd: all four GEMMs on our tcgen05 kernel (logits recomputed for G)"}
+            "note": "ak_linear_ce_fwdbwd through the C-ABI wrapper directly (no autograd), same kernels"}
         timeit(lambda: _ChunkedLinearCrossEntropy.apply(H.requires_grad_(True), W.requires_grad_(True), lab, 4096,
                                                         0.0, -100, 0.0, 0.0), 1, "x", 2)
         ms2 = res.pop("x")["ms"]
         res[f"linear_ce_chunked_cublas_{tag}"] = {
             "ms": ms2, "TFLOP/s": round(flops / (ms2 / 1e3) / 1e12, 1),
             "note": "library comparator: cuBLAS GEMMs around the CE row kernel, 4096-row chunks"}
-        del H, W, lab
+        # our tcgen05 GEMM against cuBLAS on the three contractions of one 16384-row chunk
+        Nc = min(16384, Nt)
+        G = (torch.randn(Nc, Vv, device=dev) * 1e-3).to(torch.bfloat16)
+        Hc = H[:Nc]
+        cmp = {}
+        for name, ours, lib, fl in (
+                ("logits", lambda: _ak.tc_gemm(Hc, W.t()), lambda: torch.mm(Hc, W.t()), 2 * Nc * Vv * Dh),
+                ("dW", lambda: _ak.tc_gemm(G.t(), Hc, out_dtype=torch.float32),
+                 lambda: torch.mm(G.t(), Hc, out_dtype=torch.float32), 2 * Vv * Dh * Nc),
+                ("dH", lambda: _ak.tc_gemm(G, W), lambda: torch.mm(G, W), 2 * Nc * Dh * Vv)):
+            timeit(ours, 1, "x", max(3, steps // 4))
+            mo = res.pop("x")["ms"]
+            timeit(lib, 1, "x", max(3, steps // 4))
+            ml = res.pop("x")["ms"]
+            cmp[name] = {"ours_ms": mo, "cublas_ms": ml, "ours_TFLOP/s": round(fl / (mo / 1e3) / 1e12, 1),
+                         "ratio_vs_cublas": round(ml / mo, 3)}
+        res[f"linear_ce_gemms_vs_cublas_{Nc}x{Dh}x{Vv}"] = cmp
+        del H, W, lab, G, Hc
         torch.cuda.empty_cache()
 
     if want("scan1"):
@@ -926,6 +944,9 @@ def run_ours(args, world, rank, local):
                 f = v.get("frac", v.get("frac_bf16"))
                 if f is not None:
                     summary[k] = f
+                elif k.startswith("linear_ce_gemms_vs_cublas"):
+                    for name, c in v.items():
+                        summary[f"tc_gemm_{name}_vs_cublas"] = c["ratio_vs_cublas"]
     if train is not None:
         summary["train_tok_s"] = train["tok_s"]
     if comparator is not None and "speedup_total" in comparator:
