@@ -6,7 +6,8 @@ It is the GPU comparator for the headline selective scan: the vendored mamba_ssm
 CUDA GPU, compiled from their sources where they lie in the reference checkout with the compile
 flags of external/mamba/setup.py:228-244 and the architecture set to sm_100a.  Nothing here is
 part of the product path; tests/test_gpu_mamba_comparator.py checks parity with it and asserts that
-our scan is faster than it at the headline configuration.
+our scan is faster than it at the headline configuration, and bench.py times it beside our scan on the
+same inputs (its `comparator` entry) when the module has been built.
 
     python oracle/build_mamba_ref.py [--reference PATH] [--jobs N]
 
