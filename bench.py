@@ -512,6 +512,28 @@ def time_other_ops(dev, steps, warmup, hbm_peak, bf16_peak, which=None, ce_rows=
                       "note": "L2 flushed (256 MB write) before each rep; flush time subtracted; "
                               "copy_ceiling_frac = a plain 25 MB -> 25 MB copy under the same protocol"}
         del xb, dyb, flush
+        # Second protocol, no flush: one CUDA graph of 16 calls, each on its own buffers (16 sets
+        # of 50-75 MB rotate through > 1 GB, so every call reads from HBM); time = replay / 16.
+        torch.cuda.empty_cache()
+        for dt, rows in ((torch.float32, 8192), (torch.bfloat16, 16384)):
+            sets = [(torch.randn(rows, 768, device=dev).to(dt), torch.randn(rows, 768, device=dev).to(dt))
+                    for _ in range(16)]
+            wr = (1 + 0.02 * torch.randn(768, device=dev)).to(dt)
+            es = 2 if dt == torch.bfloat16 else 4
+            E = rows * 768
+            tag = f"{'bf16' if es == 2 else 'fp32'}_{rows}x768"
+            for name, nb, fn in (("fwd", 2 * E * es + 768 * es, lambda x, d: _ak.rmsnorm_fwd(x, wr, 1e-6)),
+                                 ("bwd", 3 * E * es + 2 * 768 * es, lambda x, d: _ak.rmsnorm_bwd(x, wr, d, 1e-6))):
+                def calls(fn=fn):
+                    for x, d in sets:
+                        fn(x, d)
+                timeit(calls, 16 * nb, "x", max(3, steps // 2), graph=True)
+                r = res.pop("x")
+                key = f"rmsnorm_{name}_{tag}"
+                res[key]["rotating_buffers"] = {"ms": round(r["ms"] / 16, 4), "GB/s": r["GB/s"], "frac": r["frac"],
+                                                "note": "16 calls on 16 buffer sets in one CUDA graph, no flush"}
+            del sets
+            torch.cuda.empty_cache()
 
     if want("softmax"):
         # Softmax causal scores bf16 [96*2048, 2048] (config 3): 805 MB per tensor > L2.
@@ -944,7 +966,9 @@ def run_ours(args, world, rank, local):
                 f = v.get("frac", v.get("frac_bf16"))
                 if f is not None:
                     summary[k] = f
-                elif k.startswith("linear_ce_gemms_vs_cublas"):
+                if isinstance(v.get("rotating_buffers"), dict):
+                    summary[k + "_rotating"] = v["rotating_buffers"]["frac"]
+                if k.startswith("linear_ce_gemms_vs_cublas"):
                     for name, c in v.items():
                         summary[f"tc_gemm_{name}_vs_cublas"] = c["ratio_vs_cublas"]
     if train is not None:
