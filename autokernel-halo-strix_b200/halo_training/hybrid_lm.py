@@ -103,6 +103,32 @@ class GQAAttention(nn.Module):
         return self.wo(o.transpose(1, 2).reshape(B, T, H * hd))
 
 
+class _ChannelMajorLinear(torch.autograd.Function):
+    """y[b] = W x[b] for channel-major activations x (B, in, T) -> y (B, out, T).
+
+    The Mamba block's x_proj and dt_proj read and produce the (B, D, T) layout of the conv and
+    the scan directly, so neither side needs a transpose copy.  The GEMMs run in the activation
+    dtype; the weight gradient sums the batch's per-row products in fp32 (bmm with fp32 output)
+    and is returned in the weight's own dtype."""
+
+    @staticmethod
+    def forward(ctx, x, weight):
+        wc = weight.to(x.dtype)
+        ctx.save_for_backward(x, wc)
+        ctx.w_dtype = weight.dtype
+        return torch.matmul(wc, x)
+
+    @staticmethod
+    def backward(ctx, g):
+        x, wc = ctx.saved_tensors
+        g = g.to(x.dtype)
+        dx = torch.matmul(wc.t(), g) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            dw = torch.bmm(g, x.mT, out_dtype=torch.float32).sum(0).to(ctx.w_dtype)
+        return dx, dw
+
+
 def _default_scan():
     from kernels.mamba_scan import selective_scan_fn
     return selective_scan_fn
@@ -159,19 +185,21 @@ class MambaBlock(nn.Module):
         return self.out_proj(y.transpose(1, 2))
 
     def _forward_kernels(self, h):
-        """Same computation with the layout changes done by the tiled transpose kernel
-        (torch.ops.autokernel.split_transpose / transpose_bt) and the fused conv + SiLU."""
+        """Same computation on the kernel path: in_proj's output split and transposed by one
+        kernel (torch.ops.autokernel.split_transpose), the fused conv + SiLU, x_proj and dt_proj
+        computed channel-major (no transposes), and one transpose of the scan output for
+        out_proj."""
         ops = torch.ops.autokernel
         di = self.d_inner
         xz = self.in_proj(h)                                      # (B, T, 2*d_inner)
         x, z = ops.split_transpose(xz, di)                        # (B, d_inner, T) each
         x = ops.causal_conv1d_silu(x, self.conv1d.weight.squeeze(1), self.conv1d.bias)
-        x_dbl = self.x_proj(ops.transpose_bt(x))                  # (B, T, dt_rank + 2N)
-        dt, Bm, Cm = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
-        dt = ops.transpose_bt(dt @ self.dt_proj.weight.t().to(dt.dtype))   # (B, d_inner, T)
+        x_dbl = _ChannelMajorLinear.apply(x, self.x_proj.weight)  # (B, dt_rank + 2N, T)
+        dt, Bm, Cm = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=1)
+        dt = _ChannelMajorLinear.apply(dt, self.dt_proj.weight)   # (B, d_inner, T)
         A = -torch.exp(self.A_log.float())
         scan = self._scan or _default_scan()
-        y = scan(x, dt, A, ops.transpose_bt(Bm), ops.transpose_bt(Cm), self.D.float(), z=z,
+        y = scan(x, dt, A, Bm, Cm, self.D.float(), z=z,
                  delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
         return self.out_proj(ops.transpose_bt(y))
 

@@ -340,8 +340,23 @@ def time_sscan_e2e(cfg, dev, steps, warmup, host, slices=4):
         step(s)
     e.record(st)
     torch.cuda.synchronize(dev)
+    step_ms = s.elapsed_time(e) / steps
+    # the step's copy bound: the same H2D copies alone, back to back on the copy stream
+    cs_s, cs_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(cs):
+        for rep in range(warmup + steps):
+            if rep == warmup:
+                cs_s.record(cs)
+            for k in shared:
+                dev_sh[k].copy_(pinned[k], non_blocking=True)
+            for i in range(slices):
+                for k in per_row:
+                    dev_sl[i][k].copy_(pinned[k][i * rows:(i + 1) * rows], non_blocking=True)
+        cs_e.record(cs)
+    torch.cuda.synchronize(dev)
+    copy_ms = cs_s.elapsed_time(cs_e) / steps
     d2h = res_host.numel() * res_host.element_size()
-    return s.elapsed_time(e) / steps, h2d, d2h
+    return step_ms, h2d, d2h, copy_ms
 
 
 def cpu_sscan_sample(dim_sample=48, L=2048, N=16, repeats=1):
@@ -892,10 +907,11 @@ def run_ours(args, world, rank, local):
     issue_peak = sms * 4 * sm_mhz * 1e6 / 1e9  # G warp-instructions / s
     issue_achieved = inst / (bwd_avg / 1e3) / 1e9
     if args.no_e2e:
-        e2e_ms, h2d, d2h, e2e_value = float("nan"), 0, 0, None
+        e2e_ms, h2d, d2h, e2e_value, copy_ms = float("nan"), 0, 0, None, float("nan")
     else:
-        e2e_ms, h2d, d2h = time_sscan_e2e(cfg, dev, max(2, args.steps // 2), 2, host)
+        e2e_ms, h2d, d2h, copy_ms = time_sscan_e2e(cfg, dev, max(2, args.steps // 2), 2, host)
         e2e_ms = max_over_ranks(e2e_ms, world, dev)
+        copy_ms = max_over_ranks(copy_ms, world, dev)
         e2e_value = round(world * (fwd_b + bwd_b) / (e2e_ms / 1e3) / 1e9, 2)
     comparator = None
     if rank == 0 and world == 1 and not args.no_comparator:
@@ -940,6 +956,11 @@ def run_ours(args, world, rank, local):
                      "traffic": traffic, "algorithmic_bytes_per_launch": bwd_b},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+                "copy_bound": {"h2d_only_ms": round(copy_ms, 3),
+                               "h2d_GBps": round(h2d / (copy_ms / 1e3) / 1e9, 1) if copy_ms == copy_ms else None,
+                               "frac": round(copy_ms / e2e_ms, 3) if e2e_ms == e2e_ms else None,
+                               "def": "the step's H2D copies alone (pinned, same slicing, copy stream, "
+                                      "CUDA events); frac = h2d_only_ms / ms_per_step"},
                 "api": "kernels.mamba_scan.selective_scan_fn + autograd backward, pinned host inputs, "
                        "H2D of batch slice i+1 overlapped with fwd+bwd of slice i (4 slices)"},
         # per timed step: sscan_fwd_kernel; sscan_bwd_kernel, sscan_bwd_reduce, f32_to2 (dB and dC)
@@ -971,6 +992,8 @@ def run_ours(args, world, rank, local):
                 if k.startswith("linear_ce_gemms_vs_cublas"):
                     for name, c in v.items():
                         summary[f"tc_gemm_{name}_vs_cublas"] = c["ratio_vs_cublas"]
+    if copy_ms == copy_ms and e2e_ms == e2e_ms:
+        summary["e2e_frac_of_h2d_copy_bound"] = round(copy_ms / e2e_ms, 3)
     if train is not None:
         summary["train_tok_s"] = train["tok_s"]
     if comparator is not None and "speedup_total" in comparator:
