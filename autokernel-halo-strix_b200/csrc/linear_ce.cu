@@ -213,6 +213,25 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const W
   return false;
 }
 
+// Abort-path drains.  drain_bar: a bounded wait on one phase that ignores the
+// abort flag (the MMA issuer's last commit, so TMEM is never freed under a
+// running MMA).  drain_grace: the producer's loads still in flight land on the
+// leader CTA's barrier, which a peer CTA cannot poll, so it waits a fixed 1 ms
+// (a tile load takes microseconds) before leaving the loop.
+__device__ __forceinline__ bool drain_bar(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    __nanosleep(256);
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void drain_grace() {
+  const uint64_t t0 = global_ns();
+  while (global_ns() - t0 < 1000000ull) __nanosleep(1000);
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane, as an asynchronous
 // load (tmem_ld_issue) completed by tmem_ld_wait.  The wait names the
 // destination registers as in-out operands, so no use of them can be moved
@@ -517,7 +536,8 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
     if (lane == 0) {
       const uint32_t full0 = peer_addr(smem_u32(&full[0]), 0);  // the leader's barriers
       int it = 0;
-      for (int t = pair; t < g.total; t += npairs) {
+      bool live = true;
+      for (int t = pair; live && t < g.total; t += npairs) {
         int pi, mt, nt;
         decode_tile(g, t, pi, mt, nt);
         const Prob& P = pi ? g.p[1] : g.p[0];
@@ -529,7 +549,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
         for (int kb = 0; kb < ktiles; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-          wait_bar<false>(&empty[s], ph ^ 1u, wt);
+          if (!wait_bar<false>(&empty[s], ph ^ 1u, wt)) { live = false; break; }  // issue no more loads
           if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
           const uint32_t bar = full0 + (uint32_t)(s * 8);
           const uint32_t st = smem_u32(tiles + s * STAGE_BYTES);
@@ -548,6 +568,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
           }
         }
       }
+      if (!live || *wt.abort) drain_grace();
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA only)
@@ -556,7 +577,9 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
       const uint32_t peer_empty0 = peer_addr(smem_u32(&empty[0]), 1);
       const uint32_t peer_tfull0 = peer_addr(smem_u32(&tfull[0]), 1);
       int it = 0, local = 0;
-      for (int t = pair; t < g.total; t += npairs, ++local) {
+      int last_it = -1;  // the last stage consumption whose commit was issued
+      bool live = true;
+      for (int t = pair; live && t < g.total; t += npairs, ++local) {
         int pi, mt, nt;
         decode_tile(g, t, pi, mt, nt);
         const Prob& P = pi ? g.p[1] : g.p[0];
@@ -565,13 +588,13 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
         // 8-row atoms (2048 B) of an MN-major tile
         const uint32_t astep = P.a_mn ? (2048u >> 4) : 2u, bstep = P.b_mn ? (2048u >> 4) : 2u;
         const int acc = local & 1;
-        wait_bar<true>(&tempty[acc], ((uint32_t)(local >> 1) & 1u) ^ 1u, wt);
+        if (!wait_bar<true>(&tempty[acc], ((uint32_t)(local >> 1) & 1u) ^ 1u, wt)) { live = false; break; }
         tc_fence_after();
         const uint32_t dcol = tmem_base + (uint32_t)(acc * BN);
         const int ktiles = (P.K + BK - 1) / BK;
         for (int kb = 0; kb < ktiles; ++kb, ++it) {
           const int s = it % STAGES;
-          wait_bar<false>(&full[s], (uint32_t)(it / STAGES) & 1u, wt);
+          if (!wait_bar<false>(&full[s], (uint32_t)(it / STAGES) & 1u, wt)) { live = false; break; }
           tc_fence_after();
           const uint32_t st = smem_u32(tiles + s * STAGE_BYTES);
           const uint64_t ad = smem_desc_sw128(st, P.a_mn, A_BYTES / 2);
@@ -581,10 +604,16 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
             mma2(dcol, ad + (uint64_t)(astep * k), bd + (uint64_t)(bstep * k), idesc, (kb | k) ? 1u : 0u);
           commit2(smem_u32(&empty[s]));
           commit2(peer_empty0 + (uint32_t)(s * 8));
+          last_it = it;
         }
+        if (!live) break;
         commit2(smem_u32(&tfull[acc]));
         commit2(peer_tfull0 + (uint32_t)(acc * 8));
       }
+      // after an abort: commits arrive in order, so the last one completing means every MMA
+      // issued so far has finished with TMEM and shared memory
+      if ((!live || *wt.abort) && last_it >= 0)
+        drain_bar(&empty[last_it % STAGES], (uint32_t)(last_it / STAGES) & 1u);
     }
   } else {
     // ---------------- epilogue (both CTAs): warps 2..9 own TMEM lanes 32*(warp%4) ...
@@ -601,7 +630,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
       const int row0 = mt * (2 * BM) + (int)rank * BM + quad * 32;  // this warp's 32 rows
       // the row's label is loaded before the wait, so its latency hides behind the MMAs
       const int64_t lab = (P.epi == EPI_STATS && row0 + lane < P.M) ? P.labels[row0 + lane] : -1;
-      wait_bar<false>(&tfull[acc], (uint32_t)(local >> 1) & 1u, wt);
+      if (!wait_bar<false>(&tfull[acc], (uint32_t)(local >> 1) & 1u, wt)) break;  // no accumulator to read
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
       if (P.epi == EPI_STATS) epi_stats<T>(P, tbase, row0, lane, lab, nt * BN, eg, stg);

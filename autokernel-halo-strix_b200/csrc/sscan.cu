@@ -205,12 +205,21 @@ __device__ __forceinline__ void convert_bc(int N, const T* src, float* tile, int
 
 // Wait for the chunk's tiles, convert them, and (bulk path) refill the staging
 // buffer with chunk `next_t0` (< 0: none).  `phase` counts completed copies.
+// Returns false, the same for every thread of the CTA, when the wait ran out
+// (AK_ERR_TIMEOUT is in the status word): the caller then returns at once.  The
+// one copy in flight is given one more bounded wait first, so no bulk copy
+// still targets this CTA's shared memory after it exits.
 template <typename T, int ITEMS>
-__device__ __forceinline__ void fetch_chunk(const SsParams& p, T* stage, float* tile, uint64_t* bar, int phase,
+__device__ __forceinline__ bool fetch_chunk(const SsParams& p, T* stage, float* tile, uint64_t* bar, int phase,
                                             int t0, int next_t0, const T* Bg, const T* Cg) {
   constexpr int CH = 32 * ITEMS;
   if (p.bulk) {
-    mbar_wait_bounded(bar, (uint32_t)(phase & 1), p.status);
+    const bool ok = mbar_wait_bounded(bar, (uint32_t)(phase & 1), p.status);
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0) mbar_wait_bounded(bar, (uint32_t)(phase & 1), nullptr);
+      __syncthreads();
+      return false;
+    }
   } else {
     stage_bc<T, CH>(p, stage, bar, t0, Bg, Cg, false);
     __syncthreads();
@@ -218,6 +227,7 @@ __device__ __forceinline__ void fetch_chunk(const SsParams& p, T* stage, float* 
   convert_bc<T, ITEMS>(p.N, stage, tile, min(CH, p.L - t0));
   __syncthreads();  // tile ready; staging buffer free again
   if (p.bulk && threadIdx.x == 0 && next_t0 >= 0) stage_bc<T, CH>(p, stage, bar, next_t0, Bg, Cg, true);
+  return true;
 }
 
 // Inclusive scan over lanes of g -> Q g + G (right to left).
@@ -350,7 +360,7 @@ sscan_fwd_kernel(SsParams p) {
 
   for (int k = 0; k < nch; ++k) {
     const int t0 = k * CH;
-    fetch_chunk<T, ITEMS>(p, stage, tile, bar, k, t0, k + 1 < nch ? t0 + CH : -1, Bg, Cg);
+    if (!fetch_chunk<T, ITEMS>(p, stage, tile, bar, k, t0, k + 1 < nch ? t0 + CH : -1, Bg, Cg)) return;
     const int tl = t0 + lane * ITEMS;
 
     for (int j = 0; j < p.cpw; ++j) {
@@ -469,7 +479,7 @@ sscan_bwd_kernel(SsParams p) {
     const int k = nch - 1 - it;
     const int t0 = k * CH;
     const int len = min(CH, L - t0);
-    fetch_chunk<T, ITEMS>(p, stage, tile, bar, it, t0, k > 0 ? t0 - CH : -1, Bg, Cg);
+    if (!fetch_chunk<T, ITEMS>(p, stage, tile, bar, it, t0, k > 0 ? t0 - CH : -1, Bg, Cg)) return;
     const int tl = t0 + lane * ITEMS;
 
     for (int j = 0; j < p.cpw; ++j) {
