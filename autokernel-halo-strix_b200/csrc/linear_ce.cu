@@ -58,6 +58,7 @@ constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = (BN / 2) * BK * 2;
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA
 constexpr int TMEM_COLS = 2 * BN;  // two accumulators
 constexpr int64_t kChunkRows = 16384;
+constexpr int kTileOverheadK = 4;  // per-tile cost beyond its K blocks, in K blocks (list schedule)
 
 enum Epi : int { EPI_STATS = 0, EPI_STORE = 1, EPI_NONE = 2 };  // EPI_NONE: accumulate only (timing)
 
@@ -80,10 +81,16 @@ struct Prob {
   int c_f32, accumulate;
 };
 
+// Two problems whose tiles differ in K (dW's short-K tiles and dH's long-K ones)
+// are list-scheduled: the long tiles first, round robin, then every pair takes
+// the next short tile whenever it becomes free.  lp = the long problem (-1: one
+// class, plain round robin); cL / cS = tile costs in K blocks (+ a per-tile
+// overhead), which fix the order in which pairs become free.
 struct Group {
   Prob p[2];
   int nprob, total;
   int* status;
+  int lp, nL, nS, cL, cS;
 };
 
 // ---------------------------------------------------------------------------
@@ -323,6 +330,46 @@ __device__ __forceinline__ void decode_tile(const Group& g, int t, int& pi, int&
   nt = r / gm;
 }
 
+// The tile of this pair's k-th turn (decode_tile's numbering), or -1 when it has no more.
+// Long tiles: pair + k * npairs.  Short tiles: pair p makes its j-th grab at time
+// tau = nl(p) * cL + j * cS, and grabs are served in (time, pair) order, so the
+// grab's short index is the number of grabs of all pairs that come before it: the
+// first r pairs (q + 1 long tiles) start at (q + 1) * cL, the others at q * cL.
+// Every role of both CTAs computes the same sequence, so nothing is exchanged.
+__device__ __forceinline__ int sched_tile(const Group& g, int pair, int npairs, int k) {
+  if (g.lp < 0) {
+    const int t = pair + k * npairs;
+    return t < g.total ? t : -1;
+  }
+  const int q = g.nL / npairs, r = g.nL - q * npairs;
+  const int nl = q + (pair < r ? 1 : 0);
+  if (k < nl) {
+    const int l = pair + k * npairs;
+    return g.lp == 0 ? l : g.p[0].tiles + l;
+  }
+  const int64_t cL = g.cL, cS = g.cS;
+  const int64_t tau = (int64_t)nl * cL + (int64_t)(k - nl) * cS;
+  const int64_t xa = tau - (int64_t)(q + 1) * cL, xb = tau - (int64_t)q * cL;
+  const int64_t na = xa <= 0 ? 0 : (xa + cS - 1) / cS, nb = xb <= 0 ? 0 : (xb + cS - 1) / cS;
+  int64_t sidx = (int64_t)r * na + (int64_t)(npairs - r) * nb;
+  if (xa >= 0 && xa % cS == 0) sidx += min(pair, r);
+  if (xb >= 0 && xb % cS == 0) sidx += max(0, pair - r);
+  if (sidx >= g.nS) return -1;
+  return g.lp == 0 ? g.p[0].tiles + (int)sidx : (int)sidx;
+}
+
+// This pair's tile after `prev` (its k-th turn).  kList = false: plain round robin,
+// the loop the single-class launches compile to; true: sched_tile.
+template <bool kList>
+__device__ __forceinline__ int next_tile(const Group& g, int pair, int npairs, int k, int prev) {
+  if constexpr (kList) {
+    return sched_tile(g, pair, npairs, k);
+  } else {
+    const int t = k == 0 ? pair : prev + npairs;
+    return t < g.total ? t : -1;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Epilogues (one lane = one row of the warp's 32; a warpgroup = 128 rows x its columns)
 // ---------------------------------------------------------------------------
@@ -493,7 +540,7 @@ __device__ __forceinline__ void epi_store(const Prob& P, uint32_t tbase, int row
 // ---------------------------------------------------------------------------
 // The GEMM kernel (clusters of 2 CTAs)
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, bool kList>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__ CUtensorMap tB0,
                 const __grid_constant__ CUtensorMap tA1, const __grid_constant__ CUtensorMap tB1,
@@ -537,7 +584,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
       const uint32_t full0 = peer_addr(smem_u32(&full[0]), 0);  // the leader's barriers
       int it = 0;
       bool live = true;
-      for (int t = pair; live && t < g.total; t += npairs) {
+      for (int k = 0, t = -1; live && (t = next_tile<kList>(g, pair, npairs, k, t)) >= 0; ++k) {
         int pi, mt, nt;
         decode_tile(g, t, pi, mt, nt);
         const Prob& P = pi ? g.p[1] : g.p[0];
@@ -579,7 +626,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
       int it = 0, local = 0;
       int last_it = -1;  // the last stage consumption whose commit was issued
       bool live = true;
-      for (int t = pair; live && t < g.total; t += npairs, ++local) {
+      for (int t = -1; live && (t = next_tile<kList>(g, pair, npairs, local, t)) >= 0; ++local) {
         int pi, mt, nt;
         decode_tile(g, t, pi, mt, nt);
         const Prob& P = pi ? g.p[1] : g.p[0];
@@ -622,7 +669,7 @@ tc_gemm2_kernel(const __grid_constant__ CUtensorMap tA0, const __grid_constant__
     const uint32_t stg = smem_u32(smem + STAGES * STAGE_BYTES + 256) + (uint32_t)((warp - 2) * kStageWarpBytes);
     const uint32_t tempty0 = peer_addr(smem_u32(&tempty[0]), 0);
     int local = 0;
-    for (int t = pair; t < g.total; t += npairs, ++local) {
+    for (int t = -1; (t = next_tile<kList>(g, pair, npairs, local, t)) >= 0; ++local) {
       int pi, mt, nt;
       decode_tile(g, t, pi, mt, nt);
       const Prob& P = pi ? g.p[1] : g.p[0];
@@ -811,7 +858,7 @@ int resident_pairs() {
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmem;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, tc_gemm2_kernel<T>, &cfg) != cudaSuccess || n <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&n, tc_gemm2_kernel<T, false>, &cfg) != cudaSuccess || n <= 0) {
       cudaGetLastError();
       n = sm_count() / 2;
     }
@@ -834,8 +881,19 @@ int launch_group(const Operand* A, const Operand* B, Group& g, cudaStream_t st) 
   }
   if (g.nprob == 1) { maps[2] = maps[0]; maps[3] = maps[1]; }
   g.total = g.p[0].tiles + (g.nprob > 1 ? g.p[1].tiles : 0);
+  g.lp = -1;
+  if (g.nprob == 2 && g.p[0].tiles > 0 && g.p[1].tiles > 0) {
+    const int k0 = (g.p[0].K + BK - 1) / BK, k1 = (g.p[1].K + BK - 1) / BK;
+    if (k0 != k1) {
+      g.lp = k0 > k1 ? 0 : 1;
+      g.nL = g.p[g.lp].tiles;
+      g.nS = g.p[1 - g.lp].tiles;
+      g.cL = std::max(k0, k1) + kTileOverheadK;
+      g.cS = std::min(k0, k1) + kTileOverheadK;
+    }
+  }
   if (g.total == 0) return AK_OK;
-  auto kern = tc_gemm2_kernel<T>;
+  auto kern = g.lp >= 0 ? tc_gemm2_kernel<T, true> : tc_gemm2_kernel<T, false>;
   AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem),
               "linear_ce: smem attribute");
   const int pairs = std::max(1, std::min(g.total, resident_pairs<T>()));
