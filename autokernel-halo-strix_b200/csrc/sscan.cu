@@ -73,9 +73,13 @@ struct SsParams {
   float* dC_acc;
   float* part;  // [batch][dim][N+2]
   int batch, dim, L, N, groups, dpg, nw, cpw, nsaved;
+  int nsg;  // state groups per channel: warp w works on channel slot w / nsg, states of group w % nsg
   int softplus, bulk, vec_io;
   int* status;  // caller's status word: AK_ERR_TIMEOUT when a bounded wait gave up (nullable)
 };
+
+// Channels one CTA covers: nw warps = (channel slots) x (state groups), cpw channels per slot.
+__host__ __device__ inline int channels_per_cta(const SsParams& p) { return p.nw / p.nsg * p.cpw; }
 
 __device__ __forceinline__ float softplus_f(float x) { return x <= 20.f ? log1pf(__expf(x)) : x; }
 
@@ -328,7 +332,7 @@ __device__ __forceinline__ void fwd_states(int n0, int N, const float (&dlt)[ITE
 // ITEMS steps per lane: 8 (chunk = one state stride) or 16 (chunk = two state
 // strides; lanes 15 and 31 save the states, the shuffle scan is amortised over
 // twice the steps).  KI states are interleaved per pass.
-template <typename T, int ITEMS, int KI>
+template <typename T, int ITEMS, int KI, int NSG>
 __global__ void __launch_bounds__(256, ITEMS == 8 ? 3 : 2)
 sscan_fwd_kernel(SsParams p) {
   static_assert(ITEMS * 32 % kStateStride == 0, "chunk must be a whole number of state strides");
@@ -343,7 +347,14 @@ sscan_fwd_kernel(SsParams p) {
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int b = blockIdx.y;
-  const int cpc = p.nw * p.cpw;
+  const int cpc = (p.nw / NSG) * p.cpw;
+  // state split: this warp walks states [nbeg, nend) of its channel; group 0 adds the other
+  // groups' partial y (through ybuf) and writes the output
+  const int sgi = warp % NSG, wch = warp / NSG;
+  const int nper = (N + NSG - 1) / NSG;
+  const int nbeg = min(N, sgi * nper), nend = min(N, nbeg + nper);
+  float* ybuf = scarry + cpc * N;  // [nw / nsg][nsg - 1][ITEMS][32]
+  float* ymine = sgi > 0 ? ybuf + ((wch * (NSG - 1) + sgi - 1) * ITEMS) * 32 + lane : nullptr;
   const int d0 = blockIdx.x * cpc;
   const int g = d0 / p.dpg;
   const T* Bg = reinterpret_cast<const T*>(p.Bm) + ((int64_t)b * p.groups + g) * N * L;
@@ -364,7 +375,7 @@ sscan_fwd_kernel(SsParams p) {
     const int tl = t0 + lane * ITEMS;
 
     for (int j = 0; j < p.cpw; ++j) {
-      const int cl = warp * p.cpw + j;
+      const int cl = wch * p.cpw + j;
       const int d = d0 + cl;
       const int64_t chan = (int64_t)b * p.dim + d;
       float dlt[ITEMS], du[ITEMS], y[ITEMS];
@@ -380,7 +391,7 @@ sscan_fwd_kernel(SsParams p) {
         v = (tl + i < L) ? v : 0.f;  // padded steps are the identity
         dlt[i] = v;
         S += v;
-        y[i] = Dd * du[i];
+        y[i] = sgi == 0 ? Dd * du[i] : 0.f;
         du[i] *= v;
       }
       const float A_l = lane < N ? p.A[(int64_t)d * N + lane] : 0.f;  // lane n holds A[d, n]
@@ -391,9 +402,25 @@ sscan_fwd_kernel(SsParams p) {
       const int si = k * kSavesPerChunk + (lane + 1) / kLanesPerStride - 1;
       float* save = (p.chunk_states != nullptr && (lane + 1) % kLanesPerStride == 0 && si < p.nsaved)
                         ? p.chunk_states + (chan * p.nsaved + si) * N : nullptr;
-      int n = 0;
-      for (; n + KI <= N; n += KI) fwd_states<ITEMS, KI>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
-      for (; n < N; ++n) fwd_states<ITEMS, 1>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
+      int n = nbeg;
+      for (; n + KI <= nend; n += KI) fwd_states<ITEMS, KI>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
+      for (; n < nend; ++n) fwd_states<ITEMS, 1>(n, N, dlt, du, y, S, A_l, tile, lane, carry_row, save);
+      if (NSG > 1) {  // uniform over the CTA: every warp runs the same cpw iterations
+        if (sgi > 0) {
+#pragma unroll
+          for (int i = 0; i < ITEMS; ++i) ymine[i * 32] = y[i];
+        }
+        __syncthreads();
+        if (sgi == 0) {
+          for (int g2 = 0; g2 < NSG - 1; ++g2) {
+            const float* yo = ybuf + ((wch * (NSG - 1) + g2) * ITEMS) * 32 + lane;
+#pragma unroll
+            for (int i = 0; i < ITEMS; ++i) y[i] += yo[i * 32];
+          }
+        }
+        __syncthreads();  // ybuf free for the next channel
+        if (sgi > 0) continue;
+      }
       if (p.z != nullptr) {
         float zz[ITEMS];
         load_items<T, ITEMS>(zz, reinterpret_cast<const T*>(p.z) + chan * L, tl, L, p.vec_io);
@@ -436,7 +463,7 @@ __device__ __forceinline__ void red_add_v4(float* addr, float4 v) {
                : "memory");
 }
 
-template <typename T>
+template <typename T, int NSG>
 __global__ void __launch_bounds__(256, 2)
 sscan_bwd_kernel(SsParams p) {
   constexpr int ITEMS = kItems;
@@ -448,14 +475,21 @@ sscan_bwd_kernel(SsParams p) {
   float* tile = reinterpret_cast<float*>(smem + 128 + stage_bytes<T, CH>(N));
   float* sdB = tile + 2 * N * CH;  // [N][ITEMS/2][32] float2 (step pairs)
   float* sdC = sdB + N * CH;       // [N][ITEMS/2][32] float2
-  const int cpc = p.nw * p.cpw;
+  const int cpc = (p.nw / NSG) * p.cpw;
   float* sg = sdC + N * CH;        // adjoint carries [cpc][N] (pre-multiplied by a)
   float* sdA = sg + cpc * N;       // dA partials [cpc][N]
   float* sdD = sdA + cpc * N;      // dD partials [cpc]
   float* sdb = sdD + cpc;          // dbias partials [cpc]
   int* slock = reinterpret_cast<int*>(sdb + cpc);  // one lock word per state row of sdB / sdC
+  float* xbuf = reinterpret_cast<float*>(slock + N);  // state split: [nw / nsg][nsg - 1][3][ITEMS][32]
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // state split: this warp walks states [nbeg, nend) of its channel; group 0 adds the other
+  // groups' partial y, d(delta') and du (through xbuf) and writes the per-step outputs
+  const int sgi = warp % NSG, wch = warp / NSG;
+  const int nper = (N + NSG - 1) / NSG;
+  const int nbeg = min(N, sgi * nper), nend = min(N, nbeg + nper), ncnt = nend - nbeg;
+  float* xmine = sgi > 0 ? xbuf + ((wch * (NSG - 1) + sgi - 1) * 3 * ITEMS) * 32 + lane : nullptr;
   const int b = blockIdx.y;
   const int d0 = blockIdx.x * cpc;
   const int g = d0 / p.dpg;
@@ -483,7 +517,7 @@ sscan_bwd_kernel(SsParams p) {
     const int tl = t0 + lane * ITEMS;
 
     for (int j = 0; j < p.cpw; ++j) {
-      const int cl = warp * p.cpw + j;
+      const int cl = wch * p.cpw + j;
       const int d = d0 + cl;
       const int64_t chan = (int64_t)b * p.dim + d;
       float uu[ITEMS], dlt[ITEMS], dlr[ITEMS], dy[ITEMS];
@@ -491,7 +525,7 @@ sscan_bwd_kernel(SsParams p) {
       load_items<T, ITEMS>(dlr, reinterpret_cast<const T*>(p.delta) + chan * L, tl, L, p.vec_io);
       load_items<T, ITEMS>(dy, reinterpret_cast<const T*>(p.dout) + chan * L, tl, L, p.vec_io);  // dout for now
       const float bias = p.bias ? p.bias[d] : 0.f;
-      const float Dd = p.D ? p.D[d] : 0.f;
+      const float Dd = (p.D && sgi == 0) ? p.D[d] : 0.f;  // the D u term belongs to group 0
       float S = 0.f;
 #pragma unroll
       for (int i = 0; i < ITEMS; ++i) {
@@ -528,11 +562,12 @@ sscan_bwd_kernel(SsParams p) {
       const float hc_l = (k > 0 && lane < N) ? p.chunk_states_in[(chan * p.nsaved + (k - 1)) * N + lane] : 0.f;
       float dAl_keep = 0.f;  // lane n < N keeps state n's dA partial
 
-      // warps visit the states in staggered order (warp w starts at w*N/nw), so two warps are
-      // rarely on the same state row of sdB / sdC at once; the row lock below makes it exclusive
-      const int nstart = (warp * N) / p.nw;
-      for (int nn = 0; nn < N; ++nn) {
-        const int n = nn + nstart < N ? nn + nstart : nn + nstart - N;
+      // warps visit their states in staggered order (the channel slot w of nw / nsg starts at
+      // w * ncnt / (nw / nsg)), so two warps are rarely on the same state row of sdB / sdC at
+      // once; the row lock below makes it exclusive
+      const int nstart = (wch * ncnt) / (p.nw / NSG);
+      for (int nn = 0; nn < ncnt; ++nn) {
+        const int n = nbeg + (nn + nstart < ncnt ? nn + nstart : nn + nstart - ncnt);
         const float An = __shfl_sync(0xffffffffu, A_l, n);
         const float A2 = An * kLog2e;
         float2 a2[P], h2[P], Bv2[P], Cv2[P];
@@ -663,6 +698,31 @@ sscan_bwd_kernel(SsParams p) {
         ddl[2 * j] = ddl2[j].x; ddl[2 * j + 1] = ddl2[j].y;
         duacc[2 * j] = duacc2[j].x; duacc[2 * j + 1] = duacc2[j].y;
       }
+      if (lane >= nbeg && lane < nend) sdA[cl * N + lane] += dAl_keep;  // this group's states
+      if (NSG > 1) {  // uniform over the CTA: every warp runs the same cpw iterations
+        if (sgi > 0) {
+#pragma unroll
+          for (int i = 0; i < ITEMS; ++i) {
+            xmine[i * 32] = yacc[i];
+            xmine[(ITEMS + i) * 32] = ddl[i];
+            xmine[(2 * ITEMS + i) * 32] = duacc[i];
+          }
+        }
+        __syncthreads();
+        if (sgi == 0) {
+          for (int g2 = 0; g2 < NSG - 1; ++g2) {
+            const float* xo = xbuf + ((wch * (NSG - 1) + g2) * 3 * ITEMS) * 32 + lane;
+#pragma unroll
+            for (int i = 0; i < ITEMS; ++i) {
+              yacc[i] += xo[i * 32];
+              ddl[i] += xo[(ITEMS + i) * 32];
+              duacc[i] += xo[(2 * ITEMS + i) * 32];
+            }
+          }
+        }
+        __syncthreads();  // xbuf free for the next channel
+        if (sgi > 0) continue;
+      }
       // ---- per-step outputs
       float dDl = 0.f, dbl = 0.f;
 #pragma unroll
@@ -689,7 +749,6 @@ sscan_bwd_kernel(SsParams p) {
       dDl = warp_sum(dDl);
       dbl = warp_sum(dbl);
       if (lane == 0) { sdD[cl] += dDl; sdb[cl] += dbl; }
-      if (lane < N) sdA[cl * N + lane] += dAl_keep;
     }
     __syncthreads();  // chunk consumed; sdB/sdC complete
     // flush the [n][pair][lane] float2 accumulators: 4 consecutive steps per thread, v4 reductions
@@ -765,14 +824,27 @@ int max_channels_per_cta(int64_t batch, int64_t dim) {
   return c;
 }
 
-// Channels per CTA: the largest candidate dividing dim/groups.
-void pick_layout(int dpg, int max_cpc, int* nw, int* cpw) {
+// State groups per channel: 1, or 2 / 4 when one warp per channel cannot fill the GPU
+// (batch * dim warps against 16 resident warps per SM).  Each group walks N / nsg states,
+// so a small batch gets more warps without repeating any exp.
+int state_groups(int64_t batch, int64_t dim, int N) {
+  const int64_t fill = (int64_t)sm_count() * 16;
+  int g = 1;
+  while (g < 4 && 2 * g <= N && batch * dim * g < fill) g *= 2;
+  return g;
+}
+
+// Channels per CTA: the largest candidate dividing dim/groups; at most 8 warps per CTA,
+// each (channel slot, state group) pair one warp.
+void pick_layout(int dpg, int max_cpc, int nsg, int* nw, int* cpw) {
   const int cands[] = {32, 16, 8, 4, 2, 1};
   int cpc = 1;
   for (int c : cands)
     if (c <= max_cpc && dpg % c == 0) { cpc = c; break; }
-  *nw = cpc < 8 ? cpc : 8;
-  *cpw = cpc / *nw;
+  const int slots = std::max(1, 8 / nsg);
+  const int sl = cpc < slots ? cpc : slots;
+  *nw = sl * nsg;
+  *cpw = cpc / sl;
 }
 
 int validate(int64_t batch, int64_t dim, int64_t L, int64_t N, int64_t groups, int dt) {
@@ -786,15 +858,19 @@ int validate(int64_t batch, int64_t dim, int64_t L, int64_t N, int64_t groups, i
 
 int nsaved_of(int64_t L) { return (int)((L + kStateStride - 1) / kStateStride); }
 
+// + the state-split exchange buffers: ITEMS floats per lane per non-leading group (forward),
+// three such rows (y, d(delta'), du) in the backward
 template <typename T, int CH>
-size_t fwd_smem(int N, int cpc) {
-  return 128 + stage_bytes<T, CH>(N) + (size_t)2 * N * CH * 4 + (size_t)cpc * N * 4;
+size_t fwd_smem(int N, int cpc, int nw, int nsg) {
+  return 128 + stage_bytes<T, CH>(N) + (size_t)2 * N * CH * 4 + (size_t)cpc * N * 4 +
+         (size_t)(nw / nsg) * (nsg - 1) * CH * 4;
 }
 
 template <typename T, int CH>
-size_t bwd_smem(int N, int cpc) {
+size_t bwd_smem(int N, int cpc, int nw, int nsg) {
   return 128 + stage_bytes<T, CH>(N) + (size_t)4 * N * CH * 4 + (size_t)(2 * cpc * N + 2 * cpc) * 4 +
-         (size_t)N * 4;  // + row locks
+         (size_t)N * 4 +  // row locks
+         (size_t)(nw / nsg) * (nsg - 1) * 3 * CH * 4;
 }
 
 }  // namespace
@@ -828,20 +904,26 @@ extern "C" int ak_selective_scan_fwd(void* out, float* last_state, float* chunk_
   p.dpg = (int)(dim / groups);
   p.softplus = delta_softplus ? 1 : 0;
   p.nsaved = nsaved_of(seqlen);
-  pick_layout(p.dpg, max_channels_per_cta(batch, dim), &p.nw, &p.cpw);
+  p.nsg = state_groups(batch, dim, p.N);
+  pick_layout(p.dpg, max_channels_per_cta(batch, dim), p.nsg, &p.nw, &p.cpw);
   const int es = elem_size(dt);
   p.bulk = (((seqlen * es) % 16) == 0 && aligned16(Bm) && aligned16(Cm)) ? 1 : 0;
   p.vec_io = (((seqlen * es) % 16) == 0 && aligned16(u) && aligned16(delta) && aligned16(out) &&
               (z == nullptr || aligned16(z))) ? 1 : 0;
-  const int cpc = p.nw * p.cpw;
+  const int cpc = channels_per_cta(p);
   dim3 grid((unsigned)(dim / cpc), (unsigned)batch);
   AK_DISPATCH_DTYPE(dt, T, {
     // 16 steps per lane when the 512-step tiles fit in shared memory, else 8
-    const size_t smem16 = fwd_smem<T, 32 * kFwdItems>(p.N, cpc);
+    const size_t smem16 = fwd_smem<T, 32 * kFwdItems>(p.N, cpc, p.nw, p.nsg);
     const bool wide = smem16 <= 227 * 1024;
-    const size_t smem = wide ? smem16 : fwd_smem<T, 32 * kItems>(p.N, cpc);
+    const size_t smem = wide ? smem16 : fwd_smem<T, 32 * kItems>(p.N, cpc, p.nw, p.nsg);
     AK_REQUIRE(smem <= 227 * 1024, AK_ERR_SHAPE, "selective_scan_fwd: dstate too large for shared memory");
-    auto kern = wide ? sscan_fwd_kernel<T, kFwdItems, kFwdInterleave> : sscan_fwd_kernel<T, kItems, 2>;
+    auto kern = wide ? (p.nsg == 4   ? sscan_fwd_kernel<T, kFwdItems, kFwdInterleave, 4>
+                        : p.nsg == 2 ? sscan_fwd_kernel<T, kFwdItems, kFwdInterleave, 2>
+                                     : sscan_fwd_kernel<T, kFwdItems, kFwdInterleave, 1>)
+                     : (p.nsg == 4   ? sscan_fwd_kernel<T, kItems, 2, 4>
+                        : p.nsg == 2 ? sscan_fwd_kernel<T, kItems, 2, 2>
+                                     : sscan_fwd_kernel<T, kItems, 2, 1>);
     AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "selective_scan_fwd: smem attribute");
     kern<<<grid, p.nw * 32, smem, st>>>(p);
@@ -905,19 +987,20 @@ extern "C" int ak_selective_scan_bwd(void* du, void* ddelta, float* dA, void* dB
   p.dpg = (int)(dim / groups);
   p.softplus = delta_softplus ? 1 : 0;
   p.nsaved = nsaved_of(seqlen);
-  pick_layout(p.dpg, max_channels_per_cta(batch, dim), &p.nw, &p.cpw);
+  p.nsg = state_groups(batch, dim, p.N);
+  pick_layout(p.dpg, max_channels_per_cta(batch, dim), p.nsg, &p.nw, &p.cpw);
   const int es = elem_size(dt);
   p.bulk = (((seqlen * es) % 16) == 0 && aligned16(Bm) && aligned16(Cm)) ? 1 : 0;
   p.vec_io = (((seqlen * es) % 16) == 0 && aligned16(u) && aligned16(delta) && aligned16(dout) && aligned16(du) &&
               aligned16(ddelta) && (z == nullptr || (aligned16(z) && aligned16(dz)))) ? 1 : 0;
   constexpr int CH = 32 * kItems;
-  const int cpc = p.nw * p.cpw;
+  const int cpc = channels_per_cta(p);
   AK_CUDA_TRY(cudaMemsetAsync(ws, 0, 2 * nbc * sizeof(float), st), "selective_scan_bwd: workspace clear");
   dim3 grid((unsigned)(dim / cpc), (unsigned)batch);
   AK_DISPATCH_DTYPE(dt, T, {
-    const size_t smem = bwd_smem<T, CH>(p.N, cpc);
+    const size_t smem = bwd_smem<T, CH>(p.N, cpc, p.nw, p.nsg);
     AK_REQUIRE(smem <= 227 * 1024, AK_ERR_SHAPE, "selective_scan_bwd: dstate too large for shared memory");
-    auto kern = sscan_bwd_kernel<T>;
+    auto kern = p.nsg == 4 ? sscan_bwd_kernel<T, 4> : p.nsg == 2 ? sscan_bwd_kernel<T, 2> : sscan_bwd_kernel<T, 1>;
     AK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                 "selective_scan_bwd: smem attribute");
     kern<<<grid, p.nw * 32, smem, st>>>(p);
