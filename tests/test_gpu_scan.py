@@ -129,6 +129,14 @@ def test_sscan_lowp(dtype, b, dim, L, N, groups):
     _check_sscan(_sscan_inputs(b, dim, L, N, groups, dtype, seed=L + N), dtype=dtype)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("b,dim,L,N,groups", [(2, 1536, 300, 16, 1), (1, 1536, 300, 16, 1), (2, 1536, 300, 16, 2)])
+def test_sscan_state_group_layouts(dtype, b, dim, L, N, groups):
+    """On a 148-SM B200 these shapes select one state group per channel (b = 2: 3072 warps fill
+    the GPU) and two (b = 1), the two layouts the small test shapes above do not reach."""
+    _check_sscan(_sscan_inputs(b, dim, L, N, groups, dtype, seed=b + L), dtype=dtype)
+
+
 def test_sscan_optional_inputs_absent():
     ins = list(_sscan_inputs(2, 8, 200, 16, 1, torch.float32, seed=5, with_z=False, with_D=False, with_bias=False))
     ins[1] = torch.nn.functional.softplus(ins[1])  # without softplus the caller passes a positive delta
