@@ -273,7 +273,7 @@ def time_comparator(dev, host, steps, warmup, our_fwd_ms, our_bwd_ms):
             "speedup_total": round((rf + rb) / (our_fwd_ms + our_bwd_ms), 3)}
 
 
-def time_sscan_e2e(cfg, dev, steps, warmup, host, slices=4):
+def time_sscan_e2e(cfg, dev, steps, warmup, host, slices=8):
     """Same step through the public API (selective_scan_fn + autograd) with inputs in pinned
     host memory: every step copies all its inputs H2D and reads a result (last_state) back D2H.
 
@@ -962,7 +962,7 @@ def run_ours(args, world, rank, local):
                                "def": "the step's H2D copies alone (pinned, same slicing, copy stream, "
                                       "CUDA events); frac = h2d_only_ms / ms_per_step"},
                 "api": "kernels.mamba_scan.selective_scan_fn + autograd backward, pinned host inputs, "
-                       "H2D of batch slice i+1 overlapped with fwd+bwd of slice i (4 slices)"},
+                       "H2D of batch slice i+1 overlapped with fwd+bwd of slice i (8 slices of one batch row)"},
         # per timed step: sscan_fwd_kernel; sscan_bwd_kernel, sscan_bwd_reduce, f32_to2 (dB and dC)
         "gpu_launches": 4 * args.steps,
         "clocks": clocks,
