@@ -46,11 +46,13 @@ NCU_TRAFFIC_BYTES = {
     "sscan_bwd": 2 * (106_179_072 + 42_633_984),
 }
 # smsp__inst_executed.sum (warp-instructions) per launch of the scan backward at the headline
-# shape, from the same kind of capture (B=4, doubled: the instruction count is linear in B).
+# shape, from the same kind of capture (B=4, doubled: the instruction count is linear in B) of
+# the current kernel (paired fp32 step pairs; profiles/selective_scan_kernels_B4_*, instruction
+# mix by opcode: 303.9 M at B=4, 48.3 per (step, state) lane-unit).
 # The backward is issue-bound, so its roofline is the SM's issue rate: 148 SMs x 4 schedulers x
 # one warp-instruction per clock at the clock sampled during the timed region.
 NCU_WARP_INST = {
-    "sscan_bwd": 2 * 343_400_000,
+    "sscan_bwd": 2 * 303_900_000,
 }
 
 
