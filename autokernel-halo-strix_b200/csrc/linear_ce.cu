@@ -455,11 +455,14 @@ __device__ __forceinline__ void epi_stats(const Prob& P, uint32_t tbase, int row
         put_row16<T>(C + (int64_t)row * P.ldc, cbase, P.N, v);
       }
     }
-    // the target logit (a predicated store per column keeps v in registers)
+    // the target logit: one range check per chunk (a row's target lies in one chunk of its
+    // V / 32), then a predicated store per column, which keeps v in registers
     const int rel = (int)(lab - cbase);
+    if ((unsigned)rel < 32u) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j == rel) P.tlogit[row] = v[j];
+      for (int j = 0; j < 32; ++j)
+        if (j == rel) P.tlogit[row] = v[j];
+    }
     stats_chunk(v, cbase, P.N, m, s);
     if (k + 1 < kGroupCols / 32) tmem_ld_wait(buf[(k + 1) & 1]);
   }
