@@ -375,10 +375,12 @@ __device__ __forceinline__ int next_tile(const Group& g, int pair, int npairs, i
 // ---------------------------------------------------------------------------
 // Softmax statistics of 32 logits of this lane's row (natural units in v).
 __device__ __forceinline__ void stats_chunk(const float (&v)[32], int cbase, int N, float& m, float& s) {
+  // the maximum is taken on the raw logits (log2 e > 0 and rounding are monotone, so it equals
+  // the maximum of the scaled ones); each exponent argument is then one paired FMA x log2e - m
   float2 v2[16];
   const float2 l2e = make_float2(kLog2e, kLog2e);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) v2[j] = __fmul2_rn(make_float2(v[2 * j], v[2 * j + 1]), l2e);
+  for (int j = 0; j < 16; ++j) v2[j] = make_float2(v[2 * j], v[2 * j + 1]);
   if (cbase + 32 > N) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -389,13 +391,13 @@ __device__ __forceinline__ void stats_chunk(const float (&v)[32], int cbase, int
   float lm = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 16; ++j) lm = fmaxf(lm, fmaxf(v2[j].x, v2[j].y));
-  const float mn = fmaxf(m, lm);
+  const float mn = fmaxf(m, lm * kLog2e);
   if (mn != -INFINITY) {
     const float2 neg = make_float2(-mn, -mn);
     float2 a2 = make_float2(s * ex2(m - mn), 0.f);
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const float2 d = __fadd2_rn(v2[j], neg);
+      const float2 d = __ffma2_rn(v2[j], l2e, neg);
       a2 = __fadd2_rn(a2, make_float2(ex2(d.x), ex2(d.y)));
     }
     s = a2.x + a2.y;
