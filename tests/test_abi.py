@@ -62,10 +62,53 @@ def test_workspace_queries():
     assert n.value == (2 * 2 * 2 * 16 * 300 + 2 * 8 * 18) * 4
 
 
-def test_wrappers_refuse_cpu_tensors():
+def _cpu_calls():
+    """One call of every wrapper family and of the public entry points, on CPU tensors."""
     import torch
-    with pytest.raises(RuntimeError, match="CUDA"):
-        _ak.rmsnorm_fwd(torch.zeros(2, 8), torch.ones(8))
+    bf = torch.bfloat16
+    x, w = torch.zeros(4, 64), torch.ones(64)
+    u = torch.zeros(1, 8, 32, dtype=bf)
+    A = -torch.ones(8, 4)
+    Bm = torch.zeros(1, 4, 32, dtype=bf)
+    H, W = torch.zeros(16, 64, dtype=bf), torch.zeros(64, 64, dtype=bf)
+    lab = torch.zeros(16, dtype=torch.long)
+    cs = torch.ones(32, 4)
+    q = torch.zeros(1, 2, 32, 8)
+
+    def scan_fn():
+        from kernels.mamba_scan import selective_scan_fn
+        return selective_scan_fn(u, u, A, Bm, Bm, delta_softplus=True)
+
+    def linear_ce_loss():
+        from kernels.hip.chunked_linear_cross_entropy import ChunkedLinearCrossEntropyLoss
+        return ChunkedLinearCrossEntropyLoss()(H, W, lab)
+
+    return {
+        "rmsnorm_fwd": lambda: _ak.rmsnorm_fwd(x, w),
+        "rmsnorm_bwd": lambda: _ak.rmsnorm_bwd(x, w, x),
+        "fused_res_rmsnorm_fwd": lambda: _ak.fused_res_rmsnorm_fwd(x, x, w),
+        "softmax_fwd": lambda: _ak.softmax_fwd(x),
+        "silu_gate_mul_fwd": lambda: _ak.silu_gate_mul_fwd(x, x),
+        "rope_fwd": lambda: _ak.rope_fwd(q, cs, cs),
+        "transpose_bt": lambda: _ak.transpose_bt(x.view(1, 4, 64)),
+        "ce_rows_fwd": lambda: _ak.ce_rows_fwd(x, lab[:4]),
+        "linear_ce_fwdbwd": lambda: _ak.linear_ce_fwdbwd(H, W, lab),
+        "tc_gemm": lambda: _ak.tc_gemm(H, W.t()),
+        "scan1_fwd": lambda: _ak.scan1_fwd(x.view(1, 4, 64), x.view(1, 4, 64), x.view(1, 4, 64), w, x.view(1, 4, 64)),
+        "selective_scan_fwd": lambda: _ak.selective_scan_fwd(u, u, A, Bm, Bm),
+        "causal_conv1d_fwd": lambda: _ak.causal_conv1d_fwd(u, torch.ones(8, 4)),
+        "selective_scan_fn": scan_fn,
+        "ChunkedLinearCrossEntropyLoss": linear_ce_loss,
+    }
+
+
+@pytest.mark.parametrize("name", sorted(_cpu_calls()))
+def test_wrappers_refuse_cpu_tensors(name):
+    """No CPU or PyTorch fallback anywhere on the product path: every wrapper family and the
+    public entry points raise on CPU tensors instead of computing."""
+    with pytest.raises((RuntimeError, NotImplementedError)) as e:
+        _cpu_calls()[name]()
+    assert "CUDA" in str(e.value) or "cuda" in str(e.value), str(e.value)
 
 
 def test_new_entry_points_validate_before_any_cuda_call():
