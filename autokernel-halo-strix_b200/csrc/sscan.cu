@@ -23,9 +23,17 @@
 // sequentially in registers (one SFU exp2 per step; the lane's decay product
 // is one exp2 of the summed delta), the 32 lane aggregates are combined by a
 // 5-round shuffle scan, and the chunk carry (one fp32 per channel and state)
-// lives in shared memory.  Two states are processed together so their
-// independent dependency chains interleave.  The state after every
-// kStateStride steps is saved for the backward.
+// lives in shared memory.  With 8 steps per lane the forward processes two
+// states together so their independent dependency chains interleave (16 steps
+// per lane leave no registers for it).  The state after every kStateStride
+// steps is saved for the backward.
+//
+// Small batches.  When batch * dim warps cannot fill the GPU, each channel's
+// states are split over NSG warps (state_groups: 2 or 4); a warp walks N / NSG
+// states, the other groups hand their partial per-step sums (y; in the
+// backward also d(delta') and du) to group 0 through shared memory, and group 0
+// writes the per-step outputs.  NSG is a template parameter, so the one-group
+// kernels the large batches use are unaffected.
 //
 // Backward.  Same decomposition, chunks visited in reverse.  Per chunk and
 // state the forward states are recomputed from the saved chunk-start state
