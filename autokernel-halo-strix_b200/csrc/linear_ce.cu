@@ -9,7 +9,8 @@
 //      per-row (max, sum exp) partials, picks the target logit and stores the
 //      16-bit logits into the chunk buffer G_c;
 //   2. a row kernel merges the partials into lse and the per-row loss;
-//   3. a streaming kernel turns G_c in place into (softmax - onehot) / n_valid;
+//   3. a streaming kernel turns G_c in place into softmax - onehot (unscaled: the
+//      dW / dH epilogues apply 1 / n_valid to the fp32 accumulators);
 //   4. one grouped launch of the same GEMM kernel computes dW (+)= G_c^T H_c and
 //      dH_c = G_c W, reading G_c, H and W in their row-major layouts (the
 //      operands whose contiguous dimension is M or N use MN-major shared-memory
@@ -31,9 +32,10 @@
 // warps 2-9 (two warpgroups, one per 128-column half) run the epilogue on the
 // other accumulator, so a tile's epilogue overlaps the next tile's MMAs.
 // Persistent: each CTA pair walks the tiles of up to two problems (the dW and
-// dH contractions share one launch).  Every mbarrier wait is bounded: on a
-// timeout AK_ERR_TIMEOUT goes to the caller's status word and the kernel still
-// finishes.
+// dH contractions share one launch; their short- and long-K tiles are
+// list-scheduled, see sched_tile).  Every mbarrier wait is bounded: on a
+// timeout AK_ERR_TIMEOUT goes to the caller's status word, the CTA stops
+// issuing loads and MMAs, drains what it issued, frees TMEM and finishes.
 #include "ak_common.cuh"
 
 #include <cuda.h>
