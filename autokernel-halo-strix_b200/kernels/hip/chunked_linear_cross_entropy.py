@@ -11,8 +11,9 @@ For bf16/fp16 inputs without softcap, label smoothing or z-loss the whole
 computation is one call into the library (`ak_linear_ce_fwdbwd`), and all three
 contractions run on its tcgen05 GEMM: per chunk of at most 16384 rows the logits
 GEMM reduces its tiles to softmax statistics and keeps that chunk's 16-bit
-logits, which become G = (softmax - onehot) / n_valid in place and feed
-dW += G^T h and dH = G W in one grouped GEMM launch.  Full [N, V] logits are
+logits, which become G = softmax - onehot in place and feed dW += G^T h and
+dH = G W in one grouped GEMM launch (1 / n_valid is applied to the fp32
+accumulators in the GEMM epilogue).  Full [N, V] logits are
 never stored and no cuBLAS GEMM runs.  Other feature combinations use the
 row-chunked path below (cuBLAS GEMMs around the fused CE row kernel).
 
