@@ -18,8 +18,9 @@
  *     scan and the tensor-core linear + CE) bound every wait.  When a wait runs
  *     out they write AK_ERR_TIMEOUT to the caller's `status` word (nullable; a
  *     device int, or a pinned host int whose device address comes from
- *     ak_status_device_pointer) and finish without hanging; their outputs are
- *     then invalid.  The word is only ever written on failure, so the caller
+ *     ak_status_device_pointer), stop issuing work, wait (again bounded) for
+ *     the copies and tensor-core operations they already issued, free their
+ *     tensor memory and finish without hanging; their outputs are then invalid.  The word is only ever written on failure, so the caller
  *     zeroes it once and reads it after the stream has passed the call.
  *
  * Each declaration names the reference interface it replaces, as a path inside
